@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""Benchmark: chain_from_tokens tokens/s on B200 (BASELINE.json `metric`).
+
+Workload (N=1): BASELINE config C5 -- chain_from_tokens, FP32, T=65536
+tokens per GPU, K=4096, E=128 experts, top-2, N=1408, router logits biased by
+a log-Zipf(1.0) per-expert term; seeded synthetic inputs (no dataset exists
+for this path). Every input is larger than the 126 MB L2 (X is 1 GiB, the
+expert weights 2.95 GB), so no L2 flush is needed between steps.
+
+One step = the seven-stage chain over one batch: dense_gemm -> topk_gate ->
+histogram_exclusive_scan -> token_permute -> grouped_gemm -> unpermute, all
+through libraggedroute_b200's C ABI on one stream. `value` is device-timed
+(CUDA events, inputs resident in HBM, max over ranks); `e2e` is the same chain
+through rr_chain_from_tokens with the step's X copied in from pinned host
+memory and Y copied back inside the timed region.
+
+Multi-GPU (torchrun): every rank runs its own T=65536 tokens (weak scaling).
+--impl reference: times the reference's own CPU implementation of the path
+(oracle/_ref, compiled from the reference sources) on bounded token samples of
+the same workload, with every host thread; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "chain_from_tokens tokens/s"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=None, help="override T per GPU (testing)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--stages", action="store_true", help="print the per-stage table to stderr")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def load_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        p["source"] = "measured"
+        return p
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def measure_tf32_peak(torch, device) -> float:
+    """cuBLAS TF32 GEMM throughput (TFLOP/s) on this GPU, 8192^3, best of 10.
+    The 3xTF32 roofline is this figure / 3."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=device)
+        b = torch.randn(n, n, device=device)
+        for _ in range(3):
+            torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(a, b)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        del a, b
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def load_traffic(name: str):
+    """Per-launch DRAM traffic from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(name)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    import raggedroute_b200 as rr
+    from raggedroute_b200.workloads import C5, c5_inputs
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    tokens = args.tokens or C5["tokens"]
+    k, e, n = C5["hidden"], C5["experts"], C5["output"]
+    routes = 2 * tokens
+    inp = c5_inputs(device, tokens)
+    buf = rr.ChainBuffers.allocate(tokens, k, e, n, device)
+    stream = torch.cuda.Stream(device)
+    ctx = rr.Context(stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+
+    stage_names = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
+                   "grouped_gemm", "unpermute"]
+
+    def step(events=None):
+        def mark(i):
+            if events is not None:
+                events[i].record(stream)
+        mark(0)
+        rr.dense_gemm(inp.x, inp.router_w, buf.logits, tokens, e, k, ctx=ctx)
+        mark(1)
+        rr.topk_gate_biased(buf.logits, inp.logit_bias, buf.expert_ids, buf.route_weights,
+                            tokens, e, ctx=ctx)
+        mark(2)
+        rr.histogram_exclusive_scan(buf.expert_ids, buf.counts, buf.offsets, routes, e, ctx=ctx)
+        mark(3)
+        rr.token_permute(inp.x, buf.expert_ids, buf.offsets, buf.x_permuted, buf.route_pos, None,
+                         tokens, e, 2, k, buf.workspace, ctx=ctx)
+        mark(4)
+        rr.grouped_gemm(buf.x_permuted, inp.expert_w, buf.offsets, buf.y_permuted, e, k, n,
+                        routes, ctx=ctx)
+        mark(5)
+        rr.unpermute(buf.y_permuted, buf.route_pos, buf.route_weights, buf.y, tokens, 2, n,
+                     ctx=ctx)
+        mark(6)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+
+    launches0 = rr.kernel_launch_count()
+    clocks = ClockSampler(local_rank)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for i in range(args.steps):
+            step(ev[i])
+        stop.record(stream)
+    stop.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clock_info = clocks.stop()
+    launches = rr.kernel_launch_count() - launches0
+    total_ms = start.elapsed_time(stop)
+    stage_ms = {nm: statistics.mean(ev[i][j].elapsed_time(ev[i][j + 1])
+                                    for i in range(args.steps))
+                for j, nm in enumerate(stage_names)}
+
+    # Max over ranks.
+    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = tokens * world * args.steps / (max_ms * 1e-3)
+
+    # Correctness of the timed configuration (cheap exact checks).
+    counts = buf.counts.cpu()
+    assert int(counts.sum()) == routes
+
+    # End-to-end through the public chain API with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        x_host = inp.x.cpu().pin_memory()
+        y_host = torch.empty(tokens, n, dtype=torch.float32).pin_memory()
+        x_dev = torch.empty_like(inp.x)
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                x_dev.copy_(x_host, non_blocking=True)
+                rr.chain_from_tokens(x_dev, inp.router_w, inp.expert_w, buf,
+                                     logit_bias=inp.logit_bias, ctx=ctx)
+                y_host.copy_(buf.y, non_blocking=True)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        s2 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s2.record(stream)
+            for _ in range(args.steps):
+                x_dev.copy_(x_host, non_blocking=True)
+                rr.chain_from_tokens(x_dev, inp.router_w, inp.expert_w, buf,
+                                     logit_bias=inp.logit_bias, ctx=ctx)
+                y_host.copy_(buf.y, non_blocking=True)
+            e2.record(stream)
+        e2.synchronize()
+        te = torch.tensor([s2.elapsed_time(e2)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens * world * args.steps / (float(te.item()) * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": x_host.numel() * 4,
+               "d2h_bytes_per_step": y_host.numel() * 4}
+
+    if rank != 0:
+        return None
+
+    peaks = load_peaks()
+    tf32 = measure_tf32_peak(torch, device)
+    peak_3x = tf32 / 3.0
+    gemm_flops = 2.0 * routes * k * n
+    gemm_ms = stage_ms["grouped_gemm"]
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    hbm = float(peaks["hbm_gbs"])
+    stage_bytes = {
+        "dense_gemm": 4.0 * (tokens * k + k * e + tokens * e),
+        "topk_gate": 4.0 * tokens * e + 16.0 * tokens,
+        "histogram_exclusive_scan": 4.0 * routes + 8.0 * e + 4,
+        "token_permute": 4.0 * tokens * k + 4.0 * routes * k + 8.0 * routes + 4.0 * (e + 1),
+        "grouped_gemm": 4.0 * (routes * k + e * k * n + routes * n),
+        "unpermute": 4.0 * routes * n + 8.0 * routes + 4.0 * tokens * n,
+    }
+    stages = {}
+    for nm in stage_names:
+        ms = stage_ms[nm]
+        gbs = stage_bytes[nm] / (ms * 1e-3) / 1e9
+        entry = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3)}
+        if nm == "grouped_gemm":
+            entry["TFLOP/s"] = round(achieved, 2)
+            entry["tensor_frac_3xtf32"] = round(achieved / peak_3x, 3)
+        if nm == "dense_gemm":
+            df = 2.0 * tokens * k * e / (ms * 1e-3) / 1e12
+            entry["TFLOP/s"] = round(df, 2)
+        stages[nm] = entry
+    if args.stages:
+        print(json.dumps(stages, indent=1), file=sys.stderr)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 GEMMs)",
+        "data": "synthetic (seeded; BASELINE C5 shapes and distributions)",
+        "config": {"workload": f"C5 chain_from_tokens T={tokens}/GPU K={k} E={e} top2 N={n}",
+                   "tokens_per_gpu": tokens, "hidden": k, "experts": e, "output": n,
+                   "top_k": 2, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (X 1 GiB, W 2.95 GB); no flush"},
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm", "achieved": round(achieved, 2),
+                     "peak": round(peak_3x, 2), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak_3x, 4),
+                     "peak_source": f"cuBLAS TF32 {tf32:.0f} TFLOP/s measured live / 3",
+                     "traffic": load_traffic("grouped_gemm")},
+        "stages": stages,
+        "clocks": clock_info,
+        "gpu_launches": int(launches),
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(inp, steps=1)
+    return line
+
+
+# ---------------------------------------------------------------------------
+# reference CPU arm
+# ---------------------------------------------------------------------------
+
+def _ref_lib():
+    import oracle
+    if oracle.ref is None:
+        raise RuntimeError("oracle/_ref/librr_ref.so is missing (build it with "
+                           "python oracle/build_oracle.py where the reference checkout exists)")
+    return oracle.ref
+
+
+def _sample_inputs(sample_tokens: int, device="cpu"):
+    """Host copies of a C5 token sample plus the full router/expert weights."""
+    import torch
+    from raggedroute_b200.workloads import C5, c5_inputs
+    gen_dev = "cuda" if torch.cuda.is_available() else "cpu"
+    inp = c5_inputs(gen_dev, C5["tokens"])
+    return (inp.x[:sample_tokens].contiguous().cpu(), inp.router_w.cpu(), inp.logit_bias.cpu(),
+            inp.expert_w.cpu())
+
+
+def _run_ref_chain(ref, x, wr, bias, we, threads):
+    import ctypes
+    import torch
+    t, k = x.shape
+    e = wr.shape[1]
+    n = we.shape[2]
+    y = torch.empty(t, n, dtype=torch.float32)
+    f = ctypes.POINTER(ctypes.c_float)
+    p = lambda a: ctypes.cast(a.data_ptr(), f)  # noqa: E731
+    rc = ref.rr_ref_chain_from_tokens(p(x), p(wr), p(bias), p(we), t, k, e, n, threads, p(y))
+    if rc != 0:
+        raise RuntimeError("reference CPU chain failed")
+    return y
+
+
+def cpu_baseline(inp, steps: int = 1, sample_tokens: int = 32) -> dict:
+    """The reference CPU chain on a bounded token sample (rank 0, N=1)."""
+    ref = _ref_lib()
+    threads = os.cpu_count() or 1
+    x = inp.x[:sample_tokens].contiguous().cpu()
+    wr, bias, we = inp.router_w.cpu(), inp.logit_bias.cpu(), inp.expert_w.cpu()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _run_ref_chain(ref, x, wr, bias, we, threads)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": sample_tokens / dt, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{sample_tokens} tokens of C5 per step through the reference's CPU "
+                      f"functions (oracle/_ref), {threads} host threads"}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    ref = _ref_lib()
+    threads = os.cpu_count() or 1
+    sample = int(os.environ.get("RR_REF_SAMPLE_TOKENS", "32"))
+    x, wr, bias, we = _sample_inputs(sample)
+    for _ in range(args.warmup):
+        _run_ref_chain(ref, x, wr, bias, we, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _run_ref_chain(ref, x, wr, bias, we, threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sample / dt
+    cpu = {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+           "sample": f"{sample} tokens of C5 per step through the reference's CPU functions "
+                     f"(oracle/_ref), {threads} host threads"}
+    return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f64 (reference CPU oracle)", "data": "synthetic (seeded; C5 sample)",
+            "config": {"workload": f"C5 chain_from_tokens sample T={sample} K=4096 E=128 top2 "
+                                   "N=1408", "parallelism": "host threads"},
+            "impl": "reference", "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,56 @@
+// L3 chain entry points of libraggedroute_b200 (C++ side). The reference
+// composes these in its benchmark adapter (benchmarks/adapters/
+// chain_adapter.cpp:263-467: dense_gemm -> topk_gate -> histogram(+scan) ->
+// token_permute -> grouped_gemm -> unpermute on one stream); here they are
+// library calls with the same stage order and caller-owned buffers.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "raggedroute/operators.h"
+
+namespace raggedroute {
+
+struct ChainBuffers {
+  float* logits = nullptr;          // [T, E]  (chain_from_tokens writes it)
+  std::int32_t* expert_ids = nullptr;  // [T, 2]
+  float* route_weights = nullptr;   // [T, 2]
+  std::int32_t* counts = nullptr;   // [E]
+  std::int32_t* offsets = nullptr;  // [E + 1]
+  float* x_permuted = nullptr;      // [2T, K]
+  std::int32_t* route_pos = nullptr;  // [2T]
+  float* y_permuted = nullptr;      // [2T, N]
+  float* y = nullptr;               // [T, N]  (the output)
+};
+
+struct ChainFromTokensArgs {
+  const float* x = nullptr;               // [T, K]
+  const float* router_weights = nullptr;  // [K, E]
+  const float* logit_bias = nullptr;      // optional [E], added before the gate
+  const float* expert_weights = nullptr;  // [E, K, N]
+  ChainBuffers buffers;
+  int tokens = 0;
+  int hidden = 0;
+  int experts = 0;
+  int output = 0;
+};
+
+struct ChainFromLogitsArgs {
+  const float* logits = nullptr;          // [T, E]
+  const float* x = nullptr;               // [T, K]
+  const float* expert_weights = nullptr;  // [E, K, N]
+  ChainBuffers buffers;                   // buffers.logits unused
+  int tokens = 0;
+  int hidden = 0;
+  int experts = 0;
+  int output = 0;
+};
+
+// Workspace (bytes) for either chain: the token_permute workspace at 2T routes.
+std::size_t get_chain_workspace_size(int tokens, int hidden, int experts, int output) noexcept;
+
+Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& context) noexcept;
+Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& context) noexcept;
+
+}  // namespace raggedroute

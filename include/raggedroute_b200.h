@@ -1,0 +1,215 @@
+/*
+ * raggedroute_b200.h -- C ABI of the B200-native RaggedRoute routing path.
+ *
+ * libraggedroute_b200.so exports these entry points for any FFI (ctypes, cgo,
+ * JNI, N-API). Every buffer is a CUDA device pointer unless a comment says
+ * otherwise; every call enqueues on ctx->stream and never synchronizes, never
+ * allocates on the hot path and validates all arguments before any launch.
+ * Storage is FP32 (int32 for ids/counts/offsets/positions), contiguous,
+ * row-major. Each entry point cites the RaggedRoute interface it replaces
+ * (path:line relative to the RaggedRoute project root).
+ *
+ * Library-wide limits: 1 <= experts <= RR_MAX_EXPERTS (the reference caps
+ * at 64), route counts and element offsets fit int32 indexing as in the
+ * reference.
+ */
+#ifndef RAGGEDROUTE_B200_H_
+#define RAGGEDROUTE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RR_MAX_EXPERTS 1024
+
+/* Status codes; values 0..7 equal raggedroute::StatusCode
+ * (include/raggedroute/status.h:7-16). RR_COMM_ERROR is new (expert
+ * parallelism only). */
+enum {
+  RR_SUCCESS = 0,
+  RR_INVALID_ARGUMENT = 1,
+  RR_UNSUPPORTED_ARCHITECTURE = 2,
+  RR_UNSUPPORTED_DATA_TYPE = 3,
+  RR_UNSUPPORTED_LAYOUT = 4,
+  RR_UNSUPPORTED_KERNEL_VARIANT = 5,
+  RR_INSUFFICIENT_WORKSPACE = 6,
+  RR_CUDA_ERROR = 7,
+  RR_COMM_ERROR = 8
+};
+
+/* Architecture values equal raggedroute::DeviceArchitecture
+ * (include/raggedroute/types.h:20-25) plus RR_ARCH_SM100. */
+enum { RR_ARCH_AUTO = 0, RR_ARCH_SM86 = 1, RR_ARCH_SM90 = 2, RR_ARCH_OTHER = 3, RR_ARCH_SM100 = 4 };
+
+/* Kernel families equal raggedroute::KernelFamily (types.h:29-33). */
+enum { RR_FAMILY_AUTO = 0, RR_FAMILY_CUDA_NAIVE = 1, RR_FAMILY_CUDA_OPTIMIZED = 2 };
+
+/* Replaces raggedroute::Status (include/raggedroute/status.h:18-27). message
+ * points to static storage and is never freed. */
+typedef struct rr_status {
+  int32_t code;
+  int32_t cuda_error; /* cudaError_t value */
+  const char* message;
+} rr_status;
+
+/* Replaces raggedroute::RuntimeContext (include/raggedroute/runtime.h:13-18)
+ * plus the KernelSelection carried by every reference argument struct
+ * (include/raggedroute/types.h:35-40). */
+typedef struct rr_context {
+  void* stream; /* cudaStream_t; NULL = legacy default stream */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t architecture;       /* RR_ARCH_* */
+  int32_t kernel_family;      /* RR_FAMILY_* */
+  uint32_t implementation_id; /* operator-local research id, 0 = default */
+} rr_context;
+
+/* ---- operators (include/raggedroute/operators.h:114-135) ---------------- */
+
+/* raggedroute::dense_gemm, src/dense_gemm/operator.cpp:18-58.
+ * C[m,n] = A[m,k] . B[k,n]; alpha = 1, beta = 0 only. */
+rr_status rr_dense_gemm(const float* a, const float* b, float* c, int m, int n, int k,
+                        const rr_context* ctx);
+size_t rr_dense_gemm_workspace_size(int m, int n, int k);
+
+/* raggedroute::topk_gate, src/topk_gate/operator.cpp:18-60. Deterministic top-2
+ * selected softmax; ties go to the lower expert id, NaN reads as -inf, an
+ * all-NaN row yields ids {0,1} and weights {0.5,0.5}. top_k must be 2. */
+rr_status rr_topk_gate(const float* logits, int32_t* expert_ids, float* weights, int tokens,
+                       int experts, int top_k, const rr_context* ctx);
+size_t rr_topk_gate_workspace_size(int tokens, int experts);
+
+/* rr_topk_gate with an optional per-expert bias[experts] added to every logit
+ * row before selection (NULL = rr_topk_gate). No reference counterpart: the
+ * expert-parallel configuration skews expert load through this bias, and
+ * the chain entry points use it as their gate stage. */
+rr_status rr_topk_gate_biased(const float* logits, const float* logit_bias, int32_t* expert_ids,
+                              float* weights, int tokens, int experts, int top_k,
+                              const rr_context* ctx);
+
+/* raggedroute::histogram, src/histogram/operator.cpp:20-57. counts is reset
+ * inside the call; ids outside [0, experts) are skipped. */
+rr_status rr_histogram(const int32_t* expert_ids, int32_t* counts, int route_pairs, int experts,
+                       const rr_context* ctx);
+size_t rr_histogram_workspace_size(int route_pairs, int experts);
+
+/* raggedroute::exclusive_scan, src/scan/operator.cpp:51-74. offsets[E+1];
+ * counts and offsets may alias (in-place scan). */
+rr_status rr_exclusive_scan(const int32_t* counts, int32_t* offsets, int experts,
+                            const rr_context* ctx);
+size_t rr_exclusive_scan_workspace_size(int experts);
+
+/* raggedroute::histogram_exclusive_scan, src/scan/operator.cpp:84-134.
+ * The input and both outputs must be pairwise non-overlapping. */
+rr_status rr_histogram_exclusive_scan(const int32_t* expert_ids, int32_t* counts,
+                                      int32_t* offsets, int route_pairs, int experts,
+                                      const rr_context* ctx);
+size_t rr_histogram_exclusive_scan_workspace_size(int route_pairs, int experts);
+
+/* raggedroute::token_permute, src/permute/operator.cpp:22-83.
+ * route_pos[r] = offsets[ids[r]] + #{r' < r : ids[r'] == ids[r]} (stable,
+ * route-ascending within each expert segment); x_permuted[route_pos[r], :] =
+ * x[r / top_k, :]; sorted_route (optional, may be NULL) is the inverse map.
+ * ctx->workspace must hold rr_token_permute_workspace_size(...) bytes; its
+ * first experts int32 entries end equal to the per-expert route counts (the
+ * reference's cursor post-state). */
+rr_status rr_token_permute(const float* x, const int32_t* expert_ids, const int32_t* offsets,
+                           float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
+                           int tokens, int experts, int top_k, int hidden,
+                           const rr_context* ctx);
+size_t rr_token_permute_workspace_size(int tokens, int experts, int top_k, int hidden);
+
+/* raggedroute::grouped_gemm, src/grouped_gemm/operator.cpp:17-49.
+ * y_permuted[r, :] = x_permuted[r, :] . W[e] for r in [offsets[e],
+ * offsets[e+1]); W is [experts, hidden, output]. max_expert_tokens is the
+ * caller's launch bound (0 = no-op); the tile schedule itself is read from
+ * offsets on the device, so it may be any positive value. */
+rr_status rr_grouped_gemm(const float* x_permuted, const float* expert_weights,
+                          const int32_t* offsets, float* y_permuted, int experts, int hidden,
+                          int output, int max_expert_tokens, const rr_context* ctx);
+size_t rr_grouped_gemm_workspace_size(int experts, int hidden, int output);
+
+/* raggedroute::unpermute, src/unpermute/operator.cpp:19-57.
+ * y[t, c] = sum_k w[t*top_k+k] * y_permuted[route_pos[t*top_k+k], c], summed
+ * in rank order. */
+rr_status rr_unpermute(const float* y_permuted, const int32_t* route_pos,
+                       const float* route_weights, float* y, int tokens, int top_k, int output,
+                       const rr_context* ctx);
+size_t rr_unpermute_workspace_size(int tokens, int top_k, int output);
+
+/* ---- L3 chains (benchmarks/adapters/chain_adapter.cpp:263-467) ----------- */
+
+/* chain_from_tokens: dense_gemm -> topk_gate -> histogram_exclusive_scan ->
+ * token_permute -> grouped_gemm -> unpermute on ctx->stream, no host sync.
+ * Intermediate buffers are caller-owned and are left holding each stage's
+ * result: logits[T,E], expert_ids[T,2], route_weights[T,2], counts[E],
+ * offsets[E+1], x_permuted[2T,K], route_pos[2T], y_permuted[2T,N]; y[T,N] is
+ * the output. logit_bias (optional, [E]) is added to every logit row before
+ * the gate (NULL in the reference chain). ctx->workspace must hold
+ * rr_chain_workspace_size(...) bytes. */
+rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
+                               const float* logit_bias, const float* expert_weights,
+                               float* logits, int32_t* expert_ids, float* route_weights,
+                               int32_t* counts, int32_t* offsets, float* x_permuted,
+                               int32_t* route_pos, float* y_permuted, float* y, int tokens,
+                               int hidden, int experts, int output, const rr_context* ctx);
+
+/* chain_from_logits: the same chain starting from caller-provided logits. */
+rr_status rr_chain_from_logits(const float* logits, const float* x, const float* expert_weights,
+                               int32_t* expert_ids, float* route_weights, int32_t* counts,
+                               int32_t* offsets, float* x_permuted, int32_t* route_pos,
+                               float* y_permuted, float* y, int tokens, int hidden, int experts,
+                               int output, const rr_context* ctx);
+size_t rr_chain_workspace_size(int tokens, int hidden, int experts, int output);
+
+/* ---- low-level launchers (include/raggedroute/baseline_ops.h:14-42) ------
+ * Return a cudaError_t value: cudaErrorInvalidValue (1) on bad arguments,
+ * cudaSuccess for empty work. Preconditions as in the reference: histogram
+ * counts and permute cursors are zeroed by the caller (the launchers
+ * accumulate into them). */
+int rr_launch_dense_gemm_naive(const float* a, const float* b, float* c, int m, int n, int k,
+                               void* stream);
+int rr_launch_topk_gate_naive(const float* logits, int32_t* expert_ids, float* weights,
+                              int tokens, int experts, void* stream);
+int rr_launch_histogram_naive(const int32_t* expert_ids, int32_t* counts, int route_pairs,
+                              int experts, void* stream);
+int rr_launch_exclusive_scan_naive(const int32_t* counts, int32_t* offsets, int experts,
+                                   void* stream);
+int rr_launch_token_permute_naive(const float* x, const int32_t* expert_ids,
+                                  const int32_t* offsets, int32_t* cursors, float* x_permuted,
+                                  int32_t* route_pos, int32_t* sorted_route, int tokens,
+                                  int top_k, int hidden, void* stream);
+int rr_launch_grouped_gemm_naive(const float* x_permuted, const float* expert_weights,
+                                 const int32_t* offsets, float* y_permuted, int experts,
+                                 int hidden, int output, int max_expert_tokens, void* stream);
+int rr_launch_unpermute_naive(const float* y_permuted, const int32_t* route_pos,
+                              const float* route_weights, float* y, int tokens, int top_k,
+                              int output, void* stream);
+/* src/benchmark/cache_scrub.cu:17-50: rewrites a scrub buffer to evict L2. */
+int rr_launch_cache_scrub(uint32_t* buffer, size_t elements, void* stream);
+
+/* ---- dispatch (include/raggedroute/dispatch.h:32-46) --------------------- */
+/* Maps a compute capability to RR_ARCH_*; only 10.0 is RR_ARCH_SM100. */
+int32_t rr_classify_compute_capability(int major, int minor);
+/* Resolves the current CUDA device's architecture. */
+rr_status rr_query_current_device_architecture(int32_t* architecture);
+
+/* ---- library introspection (new) ---------------------------------------- */
+/* Number of CUDA kernels this library has launched in this process. */
+uint64_t rr_kernel_launch_count(void);
+/* Reads and clears the device-side error word set by bounded waits in the
+ * library's kernels (0 = no error). Synchronizes the given stream. */
+rr_status rr_consume_device_error(void* stream, uint32_t* error_word);
+/* Which grouped-GEMM engine a shape takes: 1 = tcgen05 3xTF32, 2 = FP32 SIMT. */
+int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
+                           float* y_permuted, int hidden, int output);
+const char* rr_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* RAGGEDROUTE_B200_H_ */

@@ -1,0 +1,411 @@
+// Stable token permute for B200.
+//
+// Contract (src/permute/operator.cpp:22-83 and src/permute/cpu_reference/
+// reference.cpp:22-81 of the reference, with the slot order made
+// deterministic): for route r = t*top_k + k with expert e = ids[r],
+//   route_pos[r] = offsets[e] + #{r' < r : ids[r'] == e}
+//   x_permuted[route_pos[r], :] = x[t, :]        (bit-exact copy)
+//   sorted_route[route_pos[r]] = r               (optional)
+//   cursors[e] == #{r : ids[r] == e} afterwards  (the reference's post-state)
+// The reference assigns slots with an atomic cursor, so its order varies run
+// to run; the route-ascending order used here is the unique order that a
+// sequential counting sort produces and passes every reference set check.
+//
+// Design (no atomics on positions, so the result never depends on
+// scheduling): routes are cut into token-aligned chunks, one CTA each.
+//   1. count:  per-chunk expert histogram -> workspace [chunks][E].
+//   2. scan:   column-wise exclusive scan over chunks, seeded with offsets,
+//              giving each chunk its first slot per expert; also writes the
+//              cursor post-state.
+//   3. place:  inside a chunk each warp owns a contiguous run of routes; the
+//              per-(warp, expert) counts are scanned in shared memory and the
+//              rank inside a warp step comes from __match_any_sync plus a
+//              popcount of the lower lanes. The CTA then copies each token row
+//              once from x (128-bit loads) to its top_k destinations.
+// A single chunk needs neither step 1 nor 2 nor any workspace beyond the
+// cursors. HBM traffic is the algorithmic minimum: x read once, x_permuted
+// written once, ids read three times (4 bytes per route each).
+#include "common.cuh"
+
+namespace rrb {
+namespace {
+
+constexpr int kPlaceThreads = 256;
+constexpr int kPlaceWarps = kPlaceThreads / 32;
+constexpr int kMaxChunkRoutes = 4096;
+constexpr int kMaxPerLane = kMaxChunkRoutes / kPlaceThreads;  // 16
+constexpr int kTargetChunks = 4 * kNumSms;
+
+struct ChunkPlan {
+  int tokens_per_chunk;
+  int chunks;
+};
+
+ChunkPlan plan_chunks(int tokens, int top_k) {
+  const long long routes = static_cast<long long>(tokens) * top_k;
+  long long want = (routes + kTargetChunks - 1) / kTargetChunks;
+  long long rc = 256;
+  while (rc < want && rc < kMaxChunkRoutes) rc <<= 1;
+  int tc = static_cast<int>(rc / top_k);
+  if (tc < 1) tc = 1;
+  ChunkPlan p;
+  p.tokens_per_chunk = tc;
+  p.chunks = tokens <= 0 ? 0 : ceil_div(tokens, tc);
+  return p;
+}
+
+std::size_t align256(std::size_t v) { return (v + 255) & ~static_cast<std::size_t>(255); }
+
+__device__ __forceinline__ int warp_leader(unsigned peers) { return __ffs(peers) - 1; }
+
+// Per-chunk histogram: chunk_hist[c][e].
+__global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
+    const int32_t* __restrict__ ids, int routes, int experts, int routes_per_chunk,
+    int32_t* __restrict__ chunk_hist) {
+  extern __shared__ int hist[];
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const long long r0 = static_cast<long long>(blockIdx.x) * routes_per_chunk;
+  long long r1 = r0 + routes_per_chunk;
+  if (r1 > routes) r1 = routes;
+  const int lane = threadIdx.x & 31;
+  for (long long base = r0 + (threadIdx.x & ~31); base < r1; base += blockDim.x) {
+    const long long r = base + lane;
+    const int e = r < r1 ? __ldg(ids + r) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (lane == warp_leader(peers) && e >= 0 && e < experts) atomicAdd(hist + e, __popc(peers));
+  }
+  __syncthreads();
+  int32_t* row = chunk_hist + static_cast<long long>(blockIdx.x) * experts;
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) row[i] = hist[i];
+}
+
+// Column-wise exclusive scan over chunks, seeded with offsets. Each CTA owns
+// 32 experts (one per lane); its 32 warps split the chunk range.
+__global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict__ chunk_hist,
+                                                            const int32_t* __restrict__ offsets,
+                                                            int32_t* __restrict__ cursors,
+                                                            int chunks, int experts) {
+  __shared__ int part[32][33];
+  const int lane = threadIdx.x & 31;
+  const int grp = threadIdx.x >> 5;
+  const int e = blockIdx.x * 32 + lane;
+  const int per = (chunks + 31) / 32;
+  const int c0 = grp * per;
+  const int c1 = min(chunks, c0 + per);
+  int sum = 0;
+  if (e < experts) {
+    for (int c = c0; c < c1; ++c) sum += chunk_hist[static_cast<long long>(c) * experts + e];
+  }
+  part[grp][lane] = sum;
+  __syncthreads();
+  if (grp == 0) {
+    int run = 0;
+    for (int g = 0; g < 32; ++g) {
+      const int v = part[g][lane];
+      part[g][lane] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  if (e < experts) {
+    int run = offsets[e] + part[grp][lane];
+    for (int c = c0; c < c1; ++c) {
+      int32_t* cell = chunk_hist + static_cast<long long>(c) * experts + e;
+      const int v = *cell;
+      *cell = run;
+      run += v;
+    }
+    // The group that owns the last chunk holds the grand total.
+    if (c1 == chunks && c0 < c1) cursors[e] = run - offsets[e];
+  }
+}
+
+// Copy a row of `hidden` floats from src to top_k destinations; one warp.
+template <bool kVec>
+__device__ __forceinline__ void copy_row_warp(const float* __restrict__ src, float* __restrict__ xp,
+                                              const int* dest, int top_k, int hidden) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (kVec) {
+    const int n4 = hidden >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    int i = lane;
+    for (; i + 96 < n4; i += 128) {
+      const float4 a = __ldg(s4 + i);
+      const float4 b = __ldg(s4 + i + 32);
+      const float4 c = __ldg(s4 + i + 64);
+      const float4 d = __ldg(s4 + i + 96);
+      for (int k = 0; k < top_k; ++k) {
+        if (dest[k] < 0) continue;
+        float4* d4 = reinterpret_cast<float4*>(xp + static_cast<long long>(dest[k]) * hidden);
+        __stcs(d4 + i, a);
+        __stcs(d4 + i + 32, b);
+        __stcs(d4 + i + 64, c);
+        __stcs(d4 + i + 96, d);
+      }
+    }
+    for (; i < n4; i += 32) {
+      const float4 a = __ldg(s4 + i);
+      for (int k = 0; k < top_k; ++k) {
+        if (dest[k] < 0) continue;
+        float4* d4 = reinterpret_cast<float4*>(xp + static_cast<long long>(dest[k]) * hidden);
+        __stcs(d4 + i, a);
+      }
+    }
+  } else {
+    for (int i = lane; i < hidden; i += 32) {
+      const float a = __ldg(src + i);
+      for (int k = 0; k < top_k; ++k) {
+        if (dest[k] < 0) continue;
+        xp[static_cast<long long>(dest[k]) * hidden + i] = a;
+      }
+    }
+  }
+}
+
+// Place + copy. chunk_base == nullptr means a single chunk seeded by offsets
+// (and this kernel then also writes the cursor post-state).
+template <bool kVec>
+__global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
+    const float* __restrict__ x, const int32_t* __restrict__ ids,
+    const int32_t* __restrict__ offsets, const int32_t* __restrict__ chunk_base,
+    float* __restrict__ xp, int32_t* __restrict__ route_pos, int32_t* __restrict__ sorted_route,
+    int32_t* __restrict__ cursors, int tokens, int experts, int top_k, int hidden,
+    int tokens_per_chunk) {
+  extern __shared__ int smem[];
+  int* warp_base = smem;                            // [kPlaceWarps][experts]
+  int* pos = smem + kPlaceWarps * experts;          // [routes in chunk]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * tokens_per_chunk;
+  const int t1 = min(tokens, t0 + tokens_per_chunk);
+  const long long r0 = static_cast<long long>(t0) * top_k;
+  const int nr = (t1 - t0) * top_k;
+  // Each warp owns a contiguous run of `per_warp` routes (a multiple of 32).
+  const int per_warp = ((nr + kPlaceWarps - 1) / kPlaceWarps + 31) & ~31;
+  const int w0 = warp * per_warp;
+  const int steps = per_warp >> 5;  // <= kMaxPerLane
+
+  for (int i = threadIdx.x; i < kPlaceWarps * experts; i += blockDim.x) warp_base[i] = 0;
+  __syncthreads();
+
+  // Pass 1: per-warp expert counts; ids stay in registers.
+  int my_ids[kMaxPerLane];
+  int* my_count = warp_base + warp * experts;
+#pragma unroll
+  for (int s = 0; s < kMaxPerLane; ++s) {
+    my_ids[s] = -1;
+    if (s < steps) {
+      const int local = w0 + s * 32 + lane;
+      int e = -1;
+      if (local < nr) {
+        e = __ldg(ids + r0 + local);
+        if (e < 0 || e >= experts) e = -2;  // out of contract: skipped
+      }
+      my_ids[s] = e;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (lane == warp_leader(peers) && e >= 0) my_count[e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+
+  // Per-(warp, expert) starting slots.
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) {
+    int run = chunk_base != nullptr ? chunk_base[static_cast<long long>(blockIdx.x) * experts + e]
+                                    : offsets[e];
+    const int first = run;
+#pragma unroll
+    for (int w = 0; w < kPlaceWarps; ++w) {
+      const int v = warp_base[w * experts + e];
+      warp_base[w * experts + e] = run;
+      run += v;
+    }
+    if (chunk_base == nullptr) cursors[e] = run - first;
+  }
+  __syncthreads();
+
+  // Pass 2: stable ranks.
+  const unsigned lt = lanemask_lt();
+#pragma unroll
+  for (int s = 0; s < kMaxPerLane; ++s) {
+    if (s < steps) {
+      const int e = my_ids[s];
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      int p = -1;
+      if (e >= 0) p = my_count[e] + __popc(peers & lt);
+      __syncwarp();
+      if (e >= 0 && lane == warp_leader(peers)) my_count[e] += __popc(peers);
+      __syncwarp();
+      const int local = w0 + s * 32 + lane;
+      if (local < nr && e != -1) {
+        pos[local] = p;
+        route_pos[r0 + local] = p;
+        if (sorted_route != nullptr && p >= 0) sorted_route[p] = static_cast<int32_t>(r0 + local);
+      }
+    }
+  }
+  __syncthreads();
+
+  if (hidden <= 0) return;
+  // Copy: one warp per token row, read once, written top_k times.
+  for (int t = t0 + warp; t < t1; t += kPlaceWarps) {
+    int dest[8];
+    const int* d = pos + (t - t0) * top_k;
+    if (top_k <= 8) {
+      for (int k = 0; k < top_k; ++k) dest[k] = d[k];
+      copy_row_warp<kVec>(x + static_cast<long long>(t) * hidden, xp, dest, top_k, hidden);
+    } else {
+      for (int k0 = 0; k0 < top_k; k0 += 8) {
+        const int kn = min(8, top_k - k0);
+        for (int k = 0; k < kn; ++k) dest[k] = d[k0 + k];
+        copy_row_warp<kVec>(x + static_cast<long long>(t) * hidden, xp, dest, kn, hidden);
+      }
+    }
+  }
+}
+
+// ---- workspace-free path for the low-level launcher -----------------------
+
+// One CTA: finds the largest expert id, mirrors the caller's cursors into
+// shared memory, and ranks every route in order with a single warp. Slot =
+// offsets[e] + cursors[e] (running). Cursors are written back at the end.
+__global__ void __launch_bounds__(1024) permute_cursor_rank_kernel(
+    const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets, int32_t* cursors,
+    int32_t* __restrict__ route_pos, int32_t* __restrict__ sorted_route, int routes) {
+  __shared__ int cur[kMaxExperts];
+  __shared__ int max_id;
+  if (threadIdx.x == 0) max_id = -1;
+  __syncthreads();
+  int local_max = -1;
+  for (int r = threadIdx.x; r < routes; r += blockDim.x) {
+    const int e = __ldg(ids + r);
+    if (e >= 0 && e < kMaxExperts && e > local_max) local_max = e;
+  }
+  atomicMax(&max_id, local_max);
+  __syncthreads();
+  const int ne = max_id + 1;
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) cur[e] = cursors[e];
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const unsigned lt = lanemask_lt();
+    for (int base = 0; base < routes; base += 32) {
+      const int r = base + lane;
+      int e = r < routes ? __ldg(ids + r) : -1;
+      if (e >= kMaxExperts) e = -2;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      int p = -1;
+      if (e >= 0) p = offsets[e] + cur[e] + __popc(peers & lt);
+      __syncwarp();
+      if (e >= 0 && lane == warp_leader(peers)) cur[e] += __popc(peers);
+      __syncwarp();
+      if (r < routes) {
+        route_pos[r] = p;
+        if (sorted_route != nullptr && p >= 0) sorted_route[p] = r;
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) cursors[e] = cur[e];
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(256) permute_copy_kernel(const float* __restrict__ x,
+                                                           const int32_t* __restrict__ route_pos,
+                                                           float* __restrict__ xp, int tokens,
+                                                           int top_k, int hidden) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int t = warp; t < tokens; t += nwarps) {
+    for (int k0 = 0; k0 < top_k; k0 += 8) {
+      int dest[8];
+      const int kn = min(8, top_k - k0);
+      for (int k = 0; k < kn; ++k) dest[k] = route_pos[static_cast<long long>(t) * top_k + k0 + k];
+      copy_row_warp<kVec>(x + static_cast<long long>(t) * hidden, xp, dest, kn, hidden);
+    }
+  }
+}
+
+}  // namespace
+
+std::size_t permute_workspace_bytes(int tokens, int experts, int top_k) {
+  if (experts <= 0) return 0;
+  const std::size_t cursors = static_cast<std::size_t>(experts) * sizeof(int32_t);
+  if (tokens <= 0 || top_k <= 0) return cursors;
+  const ChunkPlan p = plan_chunks(tokens, top_k);
+  if (p.chunks <= 1) return cursors;
+  return align256(cursors) + static_cast<std::size_t>(p.chunks) * experts * sizeof(int32_t);
+}
+
+cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32_t* offsets,
+                                 float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
+                                 int tokens, int experts, int top_k, int hidden, void* workspace,
+                                 cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  const ChunkPlan p = plan_chunks(tokens, top_k);
+  int32_t* cursors = static_cast<int32_t*>(workspace);
+  int32_t* chunk_base = nullptr;
+  const int routes_per_chunk = p.tokens_per_chunk * top_k;
+  const int routes = tokens * top_k;
+  if (p.chunks > 1) {
+    chunk_base = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) +
+                                            align256(static_cast<std::size_t>(experts) * 4));
+    permute_count_kernel<<<p.chunks, kPlaceThreads, experts * sizeof(int), stream>>>(
+        ids, routes, experts, routes_per_chunk, chunk_base);
+    permute_scan_kernel<<<ceil_div(experts, 32), 1024, 0, stream>>>(chunk_base, offsets, cursors,
+                                                                      p.chunks, experts);
+    note_launch(2);
+  }
+  const bool vec = hidden % 4 == 0 && aligned_to(x, 16) && aligned_to(x_permuted, 16);
+  const std::size_t smem = (static_cast<std::size_t>(kPlaceWarps) * experts + routes_per_chunk) *
+                           sizeof(int);
+  if (smem > 48 * 1024) {
+    cudaError_t e1 = cudaFuncSetAttribute(permute_place_kernel<true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+    cudaError_t e2 = cudaFuncSetAttribute(permute_place_kernel<false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+    if (e1 != cudaSuccess) return e1;
+    if (e2 != cudaSuccess) return e2;
+  }
+  if (vec) {
+    permute_place_kernel<true><<<p.chunks, kPlaceThreads, smem, stream>>>(
+        x, ids, offsets, chunk_base, x_permuted, route_pos, sorted_route, cursors, tokens,
+        experts, top_k, hidden, p.tokens_per_chunk);
+  } else {
+    permute_place_kernel<false><<<p.chunks, kPlaceThreads, smem, stream>>>(
+        x, ids, offsets, chunk_base, x_permuted, route_pos, sorted_route, cursors, tokens,
+        experts, top_k, hidden, p.tokens_per_chunk);
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,
+                                        const int32_t* offsets, int32_t* cursors,
+                                        float* x_permuted, int32_t* route_pos,
+                                        int32_t* sorted_route, int tokens, int top_k, int hidden,
+                                        cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  const int routes = tokens * top_k;
+  permute_cursor_rank_kernel<<<1, 1024, 0, stream>>>(ids, offsets, cursors, route_pos,
+                                                     sorted_route, routes);
+  note_launch();
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess || hidden <= 0) return err;
+  const bool vec = hidden % 4 == 0 && aligned_to(x, 16) && aligned_to(x_permuted, 16);
+  const int blocks = min(ceil_div(tokens, 8), 8 * sm_count());
+  if (vec) {
+    permute_copy_kernel<true><<<blocks, 256, 0, stream>>>(x, route_pos, x_permuted, tokens, top_k,
+                                                          hidden);
+  } else {
+    permute_copy_kernel<false><<<blocks, 256, 0, stream>>>(x, route_pos, x_permuted, tokens,
+                                                           top_k, hidden);
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace rrb

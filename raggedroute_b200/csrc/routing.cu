@@ -1,0 +1,260 @@
+// Routing metadata for B200: histogram, exclusive scan and the fused
+// histogram + exclusive scan.
+//
+// Semantics follow the reference: counts[e] = #{r : ids[r] == e} with ids
+// outside [0, E) skipped (src/histogram/cuda_naive/baseline.cu:17-27);
+// offsets[0] = 0, offsets[e+1] = offsets[e] + counts[e], alias-safe
+// (src/scan/cuda_naive/baseline.cu:12-26). Integer results are exact and
+// independent of scheduling.
+//
+// Design: ids stream through 128-bit loads; each CTA keeps a shared-memory
+// histogram and adds one warp-aggregated update per distinct expert per 32
+// ids (__match_any_sync), so an all-to-one-expert input does not serialise on
+// one shared-memory address. CTA histograms merge into counts with one global
+// atomic per non-empty bin. The fused operator runs in one CTA when the input
+// is small enough to be latency-bound (no reset launch needed), otherwise the
+// CTAs merge into zeroed counts and the last CTA to finish (ticket taken on
+// offsets[E], which the scan then overwrites with the total) performs the
+// scan, so no scratch memory is needed.
+#include "common.cuh"
+
+namespace rrb {
+namespace {
+
+constexpr int kHistThreads = 512;
+// Up to this many routes the fused operator runs in a single CTA.
+constexpr int kFusedSingleCtaMaxRoutes = 1 << 15;
+
+__device__ __forceinline__ void warp_add(int* hist, int e, int experts) {
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int leader = __ffs(peers) - 1;
+  if ((threadIdx.x & 31) == leader && e >= 0 && e < experts) {
+    atomicAdd(hist + e, __popc(peers));
+  }
+}
+
+// Adds the histogram of ids[begin, end) (a contiguous slice per CTA) to the
+// shared histogram. All threads of the CTA must call it.
+__device__ void accumulate_slice(const int32_t* __restrict__ ids, long long begin, long long end,
+                                 int* hist, int experts, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  if (vec) {
+    // begin is a multiple of 4 and ids is 16-byte aligned.
+    const long long n4 = (end - begin) >> 2;
+    const int4* src = reinterpret_cast<const int4*>(ids + begin);
+    constexpr int kUnroll = 4;  // 4 x 128-bit loads in flight per lane
+    for (long long base = static_cast<long long>(warp) * 32 * kUnroll; base < n4;
+         base += static_cast<long long>(warps) * 32 * kUnroll) {
+      int4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const long long i = base + u * 32 + lane;
+        v[u] = i < n4 ? __ldg(src + i) : make_int4(-1, -1, -1, -1);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        warp_add(hist, v[u].x, experts);
+        warp_add(hist, v[u].y, experts);
+        warp_add(hist, v[u].z, experts);
+        warp_add(hist, v[u].w, experts);
+      }
+    }
+    for (long long base = begin + (n4 << 2) + static_cast<long long>(warp) * 32; base < end;
+         base += static_cast<long long>(warps) * 32) {
+      const int e = (base + lane < end) ? __ldg(ids + base + lane) : -1;
+      warp_add(hist, e, experts);
+    }
+  } else {
+    for (long long base = begin + static_cast<long long>(warp) * 32; base < end;
+         base += static_cast<long long>(warps) * 32) {
+      const int e = (base + lane < end) ? __ldg(ids + base + lane) : -1;
+      warp_add(hist, e, experts);
+    }
+  }
+}
+
+__device__ __forceinline__ void slice_of(long long routes, long long& begin, long long& end) {
+  // Slices are multiples of 4 routes so vector loads stay aligned.
+  const long long per = ((routes + gridDim.x - 1) / gridDim.x + 3) & ~3LL;
+  begin = per * blockIdx.x;
+  end = begin + per;
+  if (begin > routes) begin = routes;
+  if (end > routes) end = routes;
+}
+
+__global__ void __launch_bounds__(kHistThreads) histogram_accumulate_kernel(
+    const int32_t* __restrict__ ids, int32_t* __restrict__ counts, int routes, int experts,
+    bool vec) {
+  extern __shared__ int hist[];
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  long long begin, end;
+  slice_of(routes, begin, end);
+  accumulate_slice(ids, begin, end, hist, experts, vec);
+  __syncthreads();
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) {
+    const int c = hist[i];
+    if (c != 0) atomicAdd(counts + i, c);
+  }
+}
+
+// Block-wide exclusive scan of up to blockDim.x (<= 1024) values, one per
+// thread. Returns the exclusive prefix; *total receives the sum.
+__device__ int block_exclusive_scan(int value, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int inclusive = value;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inclusive, off);
+    if (lane >= off) inclusive += n;
+  }
+  if (lane == 31) warp_sums[warp] = inclusive;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int s = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, s, off);
+      if (lane >= off) s += n;
+    }
+    if (lane < nw) warp_sums[lane] = s;  // inclusive over warps
+  }
+  __syncthreads();
+  const int warp_prefix = warp == 0 ? 0 : warp_sums[warp - 1];
+  *total = warp_sums[(blockDim.x >> 5) - 1];
+  return warp_prefix + inclusive - value;
+}
+
+// Scans counts[0..experts) (experts <= 1024) into offsets[0..experts]. Reads
+// everything before writing anything, so counts may alias offsets.
+__device__ void scan_counts_to_offsets(const int32_t* counts, int32_t* offsets, int experts,
+                                       int* warp_sums, bool bypass_l1) {
+  const int t = threadIdx.x;
+  int v = 0;
+  if (t < experts) v = bypass_l1 ? __ldcg(counts + t) : counts[t];
+  int total = 0;
+  const int excl = block_exclusive_scan(v, warp_sums, &total);
+  __syncthreads();
+  if (t < experts) offsets[t] = excl;
+  if (t == 0) offsets[experts] = total;
+}
+
+__global__ void __launch_bounds__(1024) exclusive_scan_kernel(const int32_t* counts,
+                                                              int32_t* offsets, int experts) {
+  __shared__ int warp_sums[32];
+  scan_counts_to_offsets(counts, offsets, experts, warp_sums, false);
+}
+
+__global__ void __launch_bounds__(1024) hist_scan_single_kernel(const int32_t* __restrict__ ids,
+                                                                int32_t* __restrict__ counts,
+                                                                int32_t* __restrict__ offsets,
+                                                                int routes, int experts,
+                                                                bool vec) {
+  __shared__ int hist[kMaxExperts];
+  __shared__ int warp_sums[32];
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  accumulate_slice(ids, 0, routes, hist, experts, vec);
+  __syncthreads();
+  const int t = threadIdx.x;
+  const int v = t < experts ? hist[t] : 0;
+  int total = 0;
+  const int excl = block_exclusive_scan(v, warp_sums, &total);
+  if (t < experts) {
+    counts[t] = v;
+    offsets[t] = excl;
+  }
+  if (t == 0) offsets[experts] = total;
+}
+
+// counts and offsets[experts] are zero on entry.
+__global__ void __launch_bounds__(kHistThreads) hist_scan_multi_kernel(
+    const int32_t* __restrict__ ids, int32_t* counts, int32_t* offsets, int routes, int experts,
+    bool vec) {
+  extern __shared__ int hist[];
+  __shared__ int warp_sums[32];
+  __shared__ bool last;
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  long long begin, end;
+  slice_of(routes, begin, end);
+  accumulate_slice(ids, begin, end, hist, experts, vec);
+  __syncthreads();
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) {
+    const int c = hist[i];
+    if (c != 0) atomicAdd(counts + i, c);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(offsets + experts, 1);
+    last = ticket == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // Last CTA: exclusive scan of the merged counts (experts <= 1024, so the
+  // scan runs in chunks of blockDim.x with a running carry).
+  int carry = 0;
+  for (int base = 0; base < experts; base += blockDim.x) {
+    const int t = base + threadIdx.x;
+    const int v = t < experts ? __ldcg(counts + t) : 0;
+    int total = 0;
+    const int excl = block_exclusive_scan(v, warp_sums, &total);
+    if (t < experts) offsets[t] = carry + excl;
+    carry += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) offsets[experts] = carry;
+}
+
+int hist_grid(long long routes) {
+  const int want = ceil_div(routes, kHistThreads * 16LL);
+  const int cap = 2 * sm_count();
+  return want < 1 ? 1 : (want > cap ? cap : want);
+}
+
+}  // namespace
+
+cudaError_t launch_histogram_accumulate(const int32_t* ids, int32_t* counts, int routes,
+                                        int experts, cudaStream_t stream) {
+  if (routes <= 0) return cudaSuccess;
+  const bool vec = aligned_to(ids, 16);
+  histogram_accumulate_kernel<<<hist_grid(routes), kHistThreads, experts * sizeof(int),
+                                stream>>>(ids, counts, routes, experts, vec);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_exclusive_scan(const int32_t* counts, int32_t* offsets, int experts,
+                                  cudaStream_t stream) {
+  const int threads = ((experts + 31) / 32) * 32;
+  exclusive_scan_kernel<<<1, threads < 32 ? 32 : threads, 0, stream>>>(counts, offsets, experts);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
+                                            int32_t* offsets, int routes, int experts,
+                                            cudaStream_t stream) {
+  const bool vec = aligned_to(ids, 16);
+  if (routes <= kFusedSingleCtaMaxRoutes) {
+    hist_scan_single_kernel<<<1, 1024, 0, stream>>>(ids, counts, offsets, routes, experts, vec);
+    note_launch();
+    return cudaGetLastError();
+  }
+  cudaError_t err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * experts, stream);
+  if (err != cudaSuccess) return err;
+  err = cudaMemsetAsync(offsets + experts, 0, sizeof(int32_t), stream);
+  if (err != cudaSuccess) return err;
+  hist_scan_multi_kernel<<<hist_grid(routes), kHistThreads, experts * sizeof(int), stream>>>(
+      ids, counts, offsets, routes, experts, vec);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace rrb

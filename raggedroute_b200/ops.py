@@ -1,0 +1,226 @@
+"""Python mirror of RaggedRoute's operator API over the C ABI.
+
+Each function takes CUDA tensors (FP32 / int32, contiguous), checks shapes
+and dtypes on the host, and calls the matching ``rr_*`` entry point on the
+current torch stream (or ``ctx.stream``). Errors come back as
+``RaggedRouteError`` carrying the reference's status code. Names and argument
+meaning follow include/raggedroute/operators.h:19-135 of the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+
+import torch
+
+from raggedroute_b200._lib import Context, check, lib
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr() or None
+
+
+def _ctx(ctx: Context | None, workspace: torch.Tensor | None = None) -> ctypes.POINTER:
+    c = dataclasses.replace(ctx) if ctx is not None else Context()
+    if c.stream == 0 and torch.cuda.is_available():
+        c.stream = torch.cuda.current_stream().cuda_stream
+    if workspace is not None:
+        c.workspace = workspace.data_ptr()
+        c.workspace_bytes = workspace.numel() * workspace.element_size()
+    return ctypes.pointer(c.as_c())
+
+
+def _need(t: torch.Tensor | None, dtype: torch.dtype, name: str) -> None:
+    if t is None:
+        return
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def dense_gemm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, m: int, n: int, k: int,
+               ctx: Context | None = None) -> None:
+    """C[m,n] = A[m,k] . B[k,n] (src/dense_gemm/operator.cpp:18-58)."""
+    for t, nm in ((a, "a"), (b, "b"), (c, "c")):
+        _need(t, torch.float32, nm)
+    check(lib().rr_dense_gemm(_ptr(a), _ptr(b), _ptr(c), m, n, k, _ctx(ctx)), "dense_gemm")
+
+
+def topk_gate(logits: torch.Tensor, expert_ids: torch.Tensor, weights: torch.Tensor, tokens: int,
+              experts: int, top_k: int = 2, ctx: Context | None = None) -> None:
+    """Deterministic top-2 selected softmax (src/topk_gate/operator.cpp:18-60)."""
+    _need(logits, torch.float32, "logits")
+    _need(expert_ids, torch.int32, "expert_ids")
+    _need(weights, torch.float32, "weights")
+    check(lib().rr_topk_gate(_ptr(logits), _ptr(expert_ids), _ptr(weights), tokens, experts,
+                             top_k, _ctx(ctx)), "topk_gate")
+
+
+def topk_gate_biased(logits: torch.Tensor, logit_bias: torch.Tensor | None,
+                     expert_ids: torch.Tensor, weights: torch.Tensor, tokens: int, experts: int,
+                     top_k: int = 2, ctx: Context | None = None) -> None:
+    """topk_gate over logits + bias[E] (extension; no reference counterpart)."""
+    _need(logits, torch.float32, "logits")
+    _need(logit_bias, torch.float32, "logit_bias")
+    _need(expert_ids, torch.int32, "expert_ids")
+    _need(weights, torch.float32, "weights")
+    check(lib().rr_topk_gate_biased(_ptr(logits), _ptr(logit_bias), _ptr(expert_ids),
+                                    _ptr(weights), tokens, experts, top_k, _ctx(ctx)),
+          "topk_gate_biased")
+
+
+def histogram(expert_ids: torch.Tensor | None, counts: torch.Tensor, route_pairs: int,
+              experts: int, ctx: Context | None = None) -> None:
+    """counts[e] = #{r : ids[r] == e}, reset included (src/histogram/operator.cpp:20-57)."""
+    _need(expert_ids, torch.int32, "expert_ids")
+    _need(counts, torch.int32, "counts")
+    check(lib().rr_histogram(_ptr(expert_ids), _ptr(counts), route_pairs, experts, _ctx(ctx)),
+          "histogram")
+
+
+def exclusive_scan(counts: torch.Tensor, offsets: torch.Tensor, experts: int,
+                   ctx: Context | None = None) -> None:
+    """offsets[E+1] from counts[E]; may alias (src/scan/operator.cpp:51-74)."""
+    _need(counts, torch.int32, "counts")
+    _need(offsets, torch.int32, "offsets")
+    check(lib().rr_exclusive_scan(_ptr(counts), _ptr(offsets), experts, _ctx(ctx)),
+          "exclusive_scan")
+
+
+def histogram_exclusive_scan(expert_ids: torch.Tensor | None, counts: torch.Tensor,
+                             offsets: torch.Tensor, route_pairs: int, experts: int,
+                             ctx: Context | None = None) -> None:
+    """Fused histogram + scan (src/scan/operator.cpp:84-134)."""
+    _need(expert_ids, torch.int32, "expert_ids")
+    _need(counts, torch.int32, "counts")
+    _need(offsets, torch.int32, "offsets")
+    check(lib().rr_histogram_exclusive_scan(_ptr(expert_ids), _ptr(counts), _ptr(offsets),
+                                            route_pairs, experts, _ctx(ctx)),
+          "histogram_exclusive_scan")
+
+
+def token_permute_workspace_size(tokens: int, experts: int, top_k: int, hidden: int = 0) -> int:
+    return int(lib().rr_token_permute_workspace_size(tokens, experts, top_k, hidden))
+
+
+def token_permute(x: torch.Tensor | None, expert_ids: torch.Tensor, offsets: torch.Tensor,
+                  x_permuted: torch.Tensor | None, route_pos: torch.Tensor,
+                  sorted_route: torch.Tensor | None, tokens: int, experts: int, top_k: int,
+                  hidden: int, workspace: torch.Tensor | None,
+                  ctx: Context | None = None) -> None:
+    """Stable permute (src/permute/operator.cpp:22-83); workspace from
+    token_permute_workspace_size (its first E int32 end as the counts)."""
+    _need(x, torch.float32, "x")
+    _need(x_permuted, torch.float32, "x_permuted")
+    for t, nm in ((expert_ids, "expert_ids"), (offsets, "offsets"), (route_pos, "route_pos"),
+                  (sorted_route, "sorted_route")):
+        _need(t, torch.int32, nm)
+    check(lib().rr_token_permute(_ptr(x), _ptr(expert_ids), _ptr(offsets), _ptr(x_permuted),
+                                 _ptr(route_pos), _ptr(sorted_route), tokens, experts, top_k,
+                                 hidden, _ctx(ctx, workspace)), "token_permute")
+
+
+def grouped_gemm(x_permuted: torch.Tensor | None, expert_weights: torch.Tensor | None,
+                 offsets: torch.Tensor, y_permuted: torch.Tensor, experts: int, hidden: int,
+                 output: int, max_expert_tokens: int, ctx: Context | None = None) -> None:
+    """Ragged per-expert GEMM (src/grouped_gemm/operator.cpp:17-49)."""
+    _need(x_permuted, torch.float32, "x_permuted")
+    _need(expert_weights, torch.float32, "expert_weights")
+    _need(offsets, torch.int32, "offsets")
+    _need(y_permuted, torch.float32, "y_permuted")
+    check(lib().rr_grouped_gemm(_ptr(x_permuted), _ptr(expert_weights), _ptr(offsets),
+                                _ptr(y_permuted), experts, hidden, output, max_expert_tokens,
+                                _ctx(ctx)), "grouped_gemm")
+
+
+def unpermute(y_permuted: torch.Tensor, route_pos: torch.Tensor, route_weights: torch.Tensor,
+              y: torch.Tensor, tokens: int, top_k: int, output: int,
+              ctx: Context | None = None) -> None:
+    """Weighted combine (src/unpermute/operator.cpp:19-57)."""
+    _need(y_permuted, torch.float32, "y_permuted")
+    _need(route_pos, torch.int32, "route_pos")
+    _need(route_weights, torch.float32, "route_weights")
+    _need(y, torch.float32, "y")
+    check(lib().rr_unpermute(_ptr(y_permuted), _ptr(route_pos), _ptr(route_weights), _ptr(y),
+                             tokens, top_k, output, _ctx(ctx)), "unpermute")
+
+
+@dataclasses.dataclass
+class ChainBuffers:
+    """Caller-owned intermediate/output buffers of the L3 chain."""
+    logits: torch.Tensor | None
+    expert_ids: torch.Tensor
+    route_weights: torch.Tensor
+    counts: torch.Tensor
+    offsets: torch.Tensor
+    x_permuted: torch.Tensor
+    route_pos: torch.Tensor
+    y_permuted: torch.Tensor
+    y: torch.Tensor
+    workspace: torch.Tensor
+
+    @staticmethod
+    def allocate(tokens: int, hidden: int, experts: int, output: int,
+                 device: torch.device | str = "cuda", with_logits: bool = True) -> "ChainBuffers":
+        f32, i32 = torch.float32, torch.int32
+        ws = max(1, chain_workspace_size(tokens, hidden, experts, output))
+        return ChainBuffers(
+            logits=torch.empty(tokens, experts, dtype=f32, device=device) if with_logits else None,
+            expert_ids=torch.empty(tokens, 2, dtype=i32, device=device),
+            route_weights=torch.empty(tokens, 2, dtype=f32, device=device),
+            counts=torch.empty(experts, dtype=i32, device=device),
+            offsets=torch.empty(experts + 1, dtype=i32, device=device),
+            x_permuted=torch.empty(2 * tokens, hidden, dtype=f32, device=device),
+            route_pos=torch.empty(2 * tokens, dtype=i32, device=device),
+            y_permuted=torch.empty(2 * tokens, output, dtype=f32, device=device),
+            y=torch.empty(tokens, output, dtype=f32, device=device),
+            workspace=torch.empty((ws + 255) // 256 * 256, dtype=torch.uint8, device=device),
+        )
+
+
+def chain_workspace_size(tokens: int, hidden: int, experts: int, output: int) -> int:
+    return int(lib().rr_chain_workspace_size(tokens, hidden, experts, output))
+
+
+def chain_from_tokens(x: torch.Tensor, router_weights: torch.Tensor,
+                      expert_weights: torch.Tensor, buf: ChainBuffers,
+                      logit_bias: torch.Tensor | None = None,
+                      ctx: Context | None = None) -> torch.Tensor:
+    """Seven-stage chain X -> Y (benchmarks/adapters/chain_adapter.cpp:263-467)."""
+    tokens, hidden = x.shape
+    experts = router_weights.shape[1]
+    output = expert_weights.shape[2]
+    check(lib().rr_chain_from_tokens(
+        _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(expert_weights), _ptr(buf.logits),
+        _ptr(buf.expert_ids), _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets),
+        _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens,
+        hidden, experts, output, _ctx(ctx, buf.workspace)), "chain_from_tokens")
+    return buf.y
+
+
+def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights: torch.Tensor,
+                      buf: ChainBuffers, ctx: Context | None = None) -> torch.Tensor:
+    """Six-stage chain logits -> Y."""
+    tokens, hidden = x.shape
+    experts = logits.shape[1]
+    output = expert_weights.shape[2]
+    check(lib().rr_chain_from_logits(
+        _ptr(logits), _ptr(x), _ptr(expert_weights), _ptr(buf.expert_ids),
+        _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets), _ptr(buf.x_permuted),
+        _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens, hidden, experts, output,
+        _ctx(ctx, buf.workspace)), "chain_from_logits")
+    return buf.y
+
+
+def kernel_launch_count() -> int:
+    return int(lib().rr_kernel_launch_count())
+
+
+def grouped_gemm_engine(x_permuted: torch.Tensor, expert_weights: torch.Tensor,
+                        y_permuted: torch.Tensor, hidden: int, output: int) -> str:
+    e = lib().rr_grouped_gemm_engine(_ptr(x_permuted), _ptr(expert_weights), _ptr(y_permuted),
+                                     hidden, output)
+    return {1: "tcgen05_3xtf32", 2: "fp32_simt"}[e]

@@ -1,0 +1,101 @@
+"""L3 chain parity on the GPU (chain_from_tokens / chain_from_logits).
+
+Validation mirrors ChainAdapter::validate (benchmarks/adapters/
+chain_adapter.cpp:469-495): ids, counts and offsets exact, route weights
+within 1e-6, final output within (atol 1e-4, rtol 4e-5*K) of the float chain
+oracle. For chain_from_tokens the device router GEMM cannot reproduce the
+oracle's sequential non-FMA float sum bit-for-bit, so routing metadata is
+checked exactly against the oracle applied to the device logits, the device
+logits against the FP64 oracle within the GEMM bound, and the count of rows
+whose routing differs from the oracle's own logits is reported (expected 0).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def _check_post_logits(rrlib, oracle, buf, logits_np, x_np, we_np, bias=None):
+    t, e = logits_np.shape
+    k = x_np.shape[1]
+    ids_ref, w_ref = oracle.top2_f32(logits_np, bias)
+    ids = host(buf.expert_ids)
+    assert np.array_equal(ids, ids_ref)
+    assert oracle.compare_floating(host(buf.route_weights), w_ref, 1e-6, 1e-6)[0]
+    counts_ref = oracle.histogram(ids_ref, e)
+    offsets_ref = oracle.exclusive_scan(counts_ref)
+    assert np.array_equal(host(buf.counts), counts_ref)
+    assert np.array_equal(host(buf.offsets), offsets_ref)
+    pos_ref = oracle.stable_route_pos(ids_ref.reshape(-1), offsets_ref, e)
+    assert np.array_equal(host(buf.route_pos), pos_ref)
+    y_ref = oracle.chain_output_f32(x_np, we_np, ids_ref, w_ref)
+    ok, err, rel = oracle.compare_floating(host(buf.y), y_ref, 1e-4, 4e-5 * k)
+    assert ok, (err, rel)
+
+
+def test_chain_from_tokens_c1(rrlib, oracle, cuda):
+    from raggedroute_b200.workloads import C1, c1_inputs
+    inp = c1_inputs(cuda)
+    t, k, e, n = C1["tokens"], C1["hidden"], C1["experts"], C1["output"]
+    buf = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    rrlib.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf)
+    x_np, wr_np, we_np = host(inp.x), host(inp.router_w), host(inp.expert_w)
+    logits_dev = host(buf.logits)
+    # Device logits vs the FP64 oracle within the accumulation-aware bound.
+    ref64 = oracle.dense_gemm_f64(x_np, wr_np)
+    assert np.all(np.abs(logits_dev - ref64) <= oracle.gemm_error_bound(x_np, wr_np, k))
+    _check_post_logits(rrlib, oracle, buf, logits_dev, x_np, we_np)
+    # Routing against the oracle's own float logits.
+    ids_oracle, _ = oracle.top2_f32(oracle.chain_logits_f32(x_np, wr_np))
+    flipped = int(np.any(host(buf.expert_ids) != ids_oracle, axis=1).sum())
+    assert flipped == 0, f"{flipped} rows route differently from the oracle's logits"
+
+
+def test_chain_from_logits_c2(rrlib, oracle, cuda):
+    from raggedroute_b200.workloads import C2, c2_inputs
+    inp = c2_inputs(cuda)
+    t, k, e, n = C2["tokens"], C2["hidden"], C2["experts"], C2["output"]
+    buf = rrlib.ChainBuffers.allocate(t, k, e, n, cuda, with_logits=False)
+    rrlib.chain_from_logits(inp.logits, inp.x, inp.expert_w, buf)
+    _check_post_logits(rrlib, oracle, buf, host(inp.logits), host(inp.x), host(inp.expert_w))
+
+
+def test_chain_from_tokens_biased_small(rrlib, oracle, cuda):
+    """C5-style chain (log-Zipf logit bias) at a size the oracle finishes fast."""
+    from raggedroute_b200.workloads import normal, zipf_log_bias
+    t, k, e, n = 1024, 256, 128, 176
+    x = normal((t, k), 1.0, 41, cuda)
+    wr = normal((k, e), 1 / 16, 42, cuda)
+    we = normal((e, k, n), 1 / 16, 43, cuda)
+    bias = torch.from_numpy(zipf_log_bias(e, 1.0)).to(cuda)
+    buf = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    rrlib.chain_from_tokens(x, wr, we, buf, logit_bias=bias)
+    _check_post_logits(rrlib, oracle, buf, host(buf.logits), host(x), host(we), host(bias))
+
+
+def test_chain_zero_tokens_is_noop(rrlib, cuda):
+    buf = rrlib.ChainBuffers.allocate(1, 8, 4, 8, cuda)
+    x = torch.zeros(0, 8, device=cuda)
+    rrlib.chain_from_tokens(x, torch.zeros(8, 4, device=cuda), torch.zeros(4, 8, 8, device=cuda),
+                            buf)
+
+
+def test_chain_repeatable(rrlib, cuda):
+    """Two runs give bitwise-identical outputs (no atomics in any float path)."""
+    from raggedroute_b200.workloads import c1_inputs
+    inp = c1_inputs(cuda)
+    buf = rrlib.ChainBuffers.allocate(512, 256, 32, 64, cuda)
+    rrlib.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf)
+    y1 = buf.y.clone()
+    pos1 = buf.route_pos.clone()
+    rrlib.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, buf.y) and torch.equal(pos1, buf.route_pos)
