@@ -1,0 +1,138 @@
+"""tcgen05 3xTF32 GEMM engine: accuracy against the FP64 oracle.
+
+Tolerance: the reference's accumulation-aware FP32 bound
+4*gamma_K*sum|a||b| + 1e-7 (src/correctness/reference_validation.cpp:70-115)
+elementwise, AND a normwise relative error <= 1e-5.
+Shapes cover ragged and empty groups, partial m/n/k tiles, groups shorter than
+one tile at the start of the buffer, N > 256 and K up to 4096. Every case also
+asserts that the engine selected was tcgen05 and that no bounded wait timed
+out (device error word 0).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, device):
+    return torch.as_tensor(np.ascontiguousarray(a)).to(device)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def device_error_word(rrlib) -> int:
+    w = ctypes.c_uint32(0)
+    st = rrlib.lib().rr_consume_device_error(
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(w))
+    assert st.code == 0
+    return int(w.value)
+
+
+def check(oracle, got, a, b, ref, k):
+    bound = oracle.gemm_error_bound(a, b, k)
+    err = np.abs(got.astype(np.float64) - ref)
+    assert np.all(err <= bound), float((err - bound).max())
+    rel = oracle.normwise_rel_error(got, ref)
+    assert rel <= 1e-5, rel
+    return rel
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 16), (1, 4, 4), (100, 36, 20), (300, 1408, 64),
+                                   (4096, 128, 256), (512, 32, 256), (777, 260, 4096)])
+def test_dense_tc(rrlib, oracle, cuda, m, n, k):
+    rng = np.random.default_rng(m * 7 + n + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.normal(0, 1 / math.sqrt(k), (k, n)).astype(np.float32)
+    da, db = dev(a, cuda), dev(b, cuda)
+    c = torch.full((m, n), float("nan"), device=cuda)
+    assert rrlib.grouped_gemm_engine(da, db, c, k, n) == "tcgen05_3xtf32"
+    rrlib.dense_gemm(da, db, c, m, n, k)
+    check(oracle, host(c), a, b, oracle.dense_gemm_f64(a, b), k)
+    assert device_error_word(rrlib) == 0
+
+
+@pytest.mark.parametrize("sizes,k,n", [
+    ([128], 16, 256),
+    ([1, 0, 0, 5, 127, 129, 0, 300], 64, 96),
+    ([0, 0, 17], 40, 1408),
+    ([2000, 7, 0, 513], 512, 384),
+    ([64] * 16, 4096, 128),
+])
+def test_grouped_tc(rrlib, oracle, cuda, sizes, k, n):
+    rng = np.random.default_rng(len(sizes) * 31 + k + n)
+    sizes = np.asarray(sizes, np.int32)
+    e = sizes.size
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
+    r = int(offsets[-1])
+    x = rng.uniform(-1, 1, (r, k)).astype(np.float32)
+    w = rng.normal(0, 1 / math.sqrt(k), (e, k, n)).astype(np.float32)
+    dx, dw = dev(x, cuda), dev(w, cuda)
+    y = torch.full((r, n), float("nan"), device=cuda)
+    assert rrlib.grouped_gemm_engine(dx, dw, y, k, n) == "tcgen05_3xtf32"
+    rrlib.grouped_gemm(dx, dw, dev(offsets, cuda), y, e, k, n, r)
+    got = host(y)
+    ref = oracle.grouped_gemm_f64(x, w, offsets)
+    for i in range(e):
+        s = slice(offsets[i], offsets[i + 1])
+        if offsets[i + 1] > offsets[i]:
+            check(oracle, got[s], x[s], w[i], ref[s], k)
+    assert not np.isnan(got).any()
+    assert device_error_word(rrlib) == 0
+
+
+def test_grouped_tc_rows_outside_segments_untouched(rrlib, cuda):
+    """Rows past offsets[E] keep their previous contents."""
+    k, n = 32, 64
+    offsets = np.array([0, 50, 50, 90], np.int32)
+    x = torch.rand(128, k, device=cuda)
+    w = torch.rand(3, k, n, device=cuda)
+    y = torch.full((128, n), 7.0, device=cuda)
+    rrlib.grouped_gemm(x, w, dev(offsets, cuda), y, 3, k, n, 90)
+    torch.cuda.synchronize()
+    assert torch.all(y[90:] == 7.0)
+    assert device_error_word(rrlib) == 0
+
+
+def test_grouped_tc_c4_full_size_sampled(rrlib, oracle, cuda):
+    """C4 at full size (R=32768, E=64, K=N=1024, Zipf 1.1 groups with 6
+    empty experts, no size a multiple of 16): every expert's first, last and
+    a seeded sample of rows checked against the FP64 oracle."""
+    from raggedroute_b200.workloads import c4_group_sizes, offsets_from_sizes
+    sizes = c4_group_sizes()
+    offsets = offsets_from_sizes(sizes)
+    r, e, k, n = 32768, 64, 1024, 1024
+    g = torch.Generator(device=cuda)
+    g.manual_seed(3)
+    x = torch.rand(r, k, generator=g, device=cuda) * 2 - 1
+    w = torch.randn(e, k, n, generator=g, device=cuda) / math.sqrt(32.0 * 32.0)
+    y = torch.full((r, n), float("nan"), device=cuda)
+    rrlib.grouped_gemm(x, w, dev(offsets, cuda), y, e, k, n, r)
+    rng = np.random.default_rng(3)
+    rows = set()
+    for i in range(e):
+        if sizes[i] > 0:
+            rows.update({int(offsets[i]), int(offsets[i + 1] - 1)})
+    rows.update(rng.integers(0, r, 200).tolist())
+    rows = np.array(sorted(rows))
+    xs = host(x)[rows]
+    ws = host(w)
+    ys = host(y)[rows]
+    expert_of = np.searchsorted(offsets, rows, side="right") - 1
+    for j, row in enumerate(rows):
+        ei = expert_of[j]
+        ref = xs[j].astype(np.float64) @ ws[ei].astype(np.float64)
+        bound = oracle.gemm_error_bound(xs[j][None, :], ws[ei], k)[0]
+        assert np.all(np.abs(ys[j] - ref) <= bound)
+    assert oracle.normwise_rel_error(ys, np.stack([xs[j].astype(np.float64) @ ws[expert_of[j]]
+                                                   for j in range(len(rows))])) <= 1e-5
+    assert not torch.isnan(y).any()
+    assert device_error_word(rrlib) == 0
