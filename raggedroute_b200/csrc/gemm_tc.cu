@@ -10,20 +10,31 @@
 // lo = rna_tf32(v - hi) (v - hi is exact in FP32). Per k-step the tensor core
 // accumulates lo_a*hi_b + hi_a*lo_b + hi_a*hi_b into an FP32 TMEM
 // accumulator; the dropped lo_a*lo_b term and the TF32 rounding of lo are
-// below 2^-21 relative per product, far inside the reference's
-// accumulation-aware FP32 bound.
+// below 2^-21 relative per product. The tensor core's own accumulate step
+// loses precision with a consistent bias (measured: 2.9e-5 normwise at
+// K=4096), so the accumulator is promoted every kChunkK = 256 of K: each
+// chunk is accumulated from zero in TMEM and added into FP32 registers of the
+// epilogue warps with round-to-nearest adds. That keeps the error near
+// 2e-6 normwise at K=4096, inside the 1e-5 contract.
 //
 // Structure: a persistent CTA per SM walks the device-side tile schedule
 // (tile_sched.cuh, read from offsets, no host sync). Tiles are 128 rows x 256
 // columns; warps are specialised:
 //   warp 0     TMA producer: A (x rows, K-major, 64-byte swizzle) and B (the
 //              expert's [K, N] weights, N-major, 128-byte swizzle) per 16-wide
-//              k-block into a 4-stage ring; no multicast.
-//   warps 2-5  split: hi/lo of each landed stage (elementwise, layout-blind).
-//   warp 1     MMA issuer: 3 tcgen05.mma (M=128, N<=256, K=8) per k-step into
-//              one of two TMEM accumulators (2 x 256 columns), so the epilogue
-//              of tile i overlaps the main loop of tile i+1.
-//   warps 6-9  epilogue: tcgen05.ld 32 lanes x 32 columns, masked stores.
+//              k-block into a 4-slot raw ring; no multicast.
+//   warps 2-3  split: hi/lo of each landed k-block into a 2-slot operand ring.
+//              kind::tf32 MMAs take K-major operands only (an N-major B reads
+//              as zeros on sm_100a), so B is transposed to K-major here, with
+//              a bank-conflict-free lane mapping; the raw slot is released as
+//              soon as it has been read.
+//   warp 1     MMA issuer: 3 tcgen05.mma (M=128, N<=256, K=8) per k-step; each
+//              256-wide K chunk goes to one of two TMEM accumulators
+//              (2 x 256 columns), alternating, so promotion of chunk c and the
+//              store of tile i overlap the MMAs of the next chunk / tile.
+//   warps 4-19 epilogue: 16 warps = 4 TMEM lane quarters x 4 column groups of
+//              64; each thread keeps its 64 running sums in registers, adds
+//              each finished chunk (tcgen05.ld) and stores the row at the end.
 // A partial last m-tile of an expert is loaded shifted back so it ends at the
 // segment end: TMA never reads a row at or beyond offsets[E], and rows before
 // the segment come from the previous expert (computed, never stored) or are
@@ -45,30 +56,43 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 16;                               // fp32 elements per k-block
-constexpr int kStages = 4;
+constexpr int kRawStages = 4;                         // TMA ring
+constexpr int kOpStages = 2;                          // hi/lo operand ring
 constexpr int kABytes = kBM * kBK * 4;                // 8 KB (64 B rows)
 constexpr int kBChunkBytes = 32 * kBK * 4;            // 2 KB: 32 columns x 16 k rows
 constexpr int kBBytes = kBN * kBK * 4;                // 16 KB
-constexpr int kStageBytes = 2 * (kABytes + kBBytes);  // raw + lo = 48 KB
+constexpr int kRawBytes = kABytes + kBBytes;          // 24 KB: A raw | B raw (N-major)
+constexpr int kOpBytes = 2 * (kABytes + kBBytes);     // 48 KB: A hi | A lo | B hi | B lo
+constexpr int kOffBRaw = kABytes;
+constexpr int kOffAHi = 0;
 constexpr int kOffALo = kABytes;
-constexpr int kOffBRaw = 2 * kABytes;
+constexpr int kOffBHi = 2 * kABytes;
 constexpr int kOffBLo = 2 * kABytes + kBBytes;
-constexpr int kThreads = 320;
+constexpr int kChunkKb = 16;  // k-blocks per promoted chunk (K = 256)
+constexpr int kSplitWarps = 2;
+constexpr int kEpilogueWarps = 16;
+constexpr int kFirstEpilogueWarp = 2 + kSplitWarps;
+// 640 threads: the 96-register cap leaves room for 64 running sums per
+// epilogue thread without spills.
+constexpr int kThreads = (kFirstEpilogueWarp + kEpilogueWarps) * 32;
 constexpr int kTmemCols = 512;
-constexpr int kSplitThreads = 128;
-constexpr int kEpilogueThreads = 128;
+constexpr int kSplitThreads = kSplitWarps * 32;
+constexpr int kEpilogueThreads = kEpilogueWarps * 32;
+constexpr int kEpiCols = kBN / 4;  // columns per epilogue thread
 
 struct alignas(1024) Smem {
-  uint8_t stage[kStages][kStageBytes];
-  uint64_t full[kStages];
-  uint64_t split[kStages];
-  uint64_t empty[kStages];
+  uint8_t raw[kRawStages][kRawBytes];
+  uint8_t op[kOpStages][kOpBytes];
+  uint64_t raw_full[kRawStages];
+  uint64_t raw_empty[kRawStages];
+  uint64_t op_full[kOpStages];
+  uint64_t op_empty[kOpStages];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
   int failed;
-  int issued[kStages];
+  int issued[kRawStages];
   int prefix[kMaxExperts + 1];
   int scratch[33];
 };
@@ -92,9 +116,7 @@ __device__ __forceinline__ TileGeom geom(int t, const int32_t* offsets, int expe
   return g;
 }
 
-__device__ __forceinline__ void split_vec(float4* raw, float4* lo, int i) {
-  const float4 v = raw[i];
-  float4 h, l;
+__device__ __forceinline__ void split4(const float4 v, float4& h, float4& l) {
   h.x = tf32_rna(v.x);
   h.y = tf32_rna(v.y);
   h.z = tf32_rna(v.z);
@@ -103,8 +125,18 @@ __device__ __forceinline__ void split_vec(float4* raw, float4* lo, int i) {
   l.y = tf32_rna(v.y - h.y);
   l.z = tf32_rna(v.z - h.z);
   l.w = tf32_rna(v.w - h.w);
-  raw[i] = h;
-  lo[i] = l;
+}
+
+// Byte offset of 16-byte chunk kc (k = 4*kc..4*kc+3) of row r in a K-major
+// tile of 16 fp32 per row with the 64-byte swizzle (TMA and UMMA agree on it).
+__device__ __forceinline__ int kmajor64_offset(int r, int kc) {
+  return r * 64 + ((kc ^ ((r >> 1) & 3)) << 4);
+}
+
+// Element (k, n) of the N-major raw B tile: 32-column chunks of 16 rows x
+// 128 bytes with the 128-byte swizzle.
+__device__ __forceinline__ int nmajor128_offset(int k, int n) {
+  return (n >> 5) * kBChunkBytes + k * 128 + ((((n & 31) >> 2) ^ (k & 7)) << 4) + ((n & 3) << 2);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
@@ -120,11 +152,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
   const int num_kb = (hidden + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.split[i], kSplitThreads);
-      mbar_init(&s.empty[i], 1);
+    for (int i = 0; i < kRawStages; ++i) {
+      mbar_init(&s.raw_full[i], 1);
+      mbar_init(&s.raw_empty[i], kSplitThreads);
       s.issued[i] = 0;
+    }
+    for (int i = 0; i < kOpStages; ++i) {
+      mbar_init(&s.op_full[i], kSplitThreads);
+      mbar_init(&s.op_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tmem_full[i], 1);
@@ -158,16 +193,16 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         const int nchunks = (g.ncols + 31) >> 5;
         const uint32_t bytes = kABytes + nchunks * kBChunkBytes;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&s.empty[stage], phase ^ 1u, err, failed)) break;
-          uint8_t* st = s.stage[stage];
-          mbar_arrive_expect_tx(&s.full[stage], bytes);
-          tma_load_2d(st, &tma_a, &s.full[stage], kb * kBK, g.base);
+          if (!mbar_wait(&s.raw_empty[stage], phase ^ 1u, err, failed)) break;
+          uint8_t* st = s.raw[stage];
+          mbar_arrive_expect_tx(&s.raw_full[stage], bytes);
+          tma_load_2d(st, &tma_a, &s.raw_full[stage], kb * kBK, g.base);
           for (int j = 0; j < nchunks; ++j) {
-            tma_load_3d(st + kOffBRaw + j * kBChunkBytes, &tma_b, &s.full[stage],
+            tma_load_3d(st + kOffBRaw + j * kBChunkBytes, &tma_b, &s.raw_full[stage],
                         g.col0 + 32 * j, kb * kBK, g.expert);
           }
           s.issued[stage] += 1;
-          if (++stage == kStages) {
+          if (++stage == kRawStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -181,46 +216,55 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok && !*failed; t += gridDim.x) {
         const TileGeom g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
         const int n_mma = (g.ncols + 15) & ~15;
-        const uint32_t idesc = idesc_tf32(kBM, n_mma, false, true);
-        if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, err, failed)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(acc * kBN);
-        bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&s.split[stage], phase, err, failed)) {
+        const uint32_t idesc = idesc_tf32(kBM, n_mma, false, false);
+        for (int kc = 0; kc < num_kb && ok; kc += kChunkKb) {
+          if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, err, failed)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_raw = smem_u32(s.stage[stage]);
-          const uint32_t a_lo = a_raw + kOffALo;
-          const uint32_t b_raw = a_raw + kOffBRaw;
-          const uint32_t b_lo = a_raw + kOffBLo;
+          const uint32_t d = tmem + static_cast<uint32_t>(acc * kBN);
+          const int kend = min(num_kb, kc + kChunkKb);
+          for (int kb = kc; kb < kend; ++kb) {
+            if (!mbar_wait(&s.op_full[stage], phase, err, failed)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t base = smem_u32(s.op[stage]);
+            const uint32_t a_hi = base + kOffAHi;
+            const uint32_t a_lo = base + kOffALo;
+            const uint32_t b_hi = base + kOffBHi;
+            const uint32_t b_lo = base + kOffBLo;
 #pragma unroll
-          for (int ks = 0; ks < kBK / 8; ++ks) {
-            const uint64_t ah = smem_desc(a_raw + ks * 32, 16, 512, Swizzle::k64B);
-            const uint64_t al = smem_desc(a_lo + ks * 32, 16, 512, Swizzle::k64B);
-            const uint64_t bh = smem_desc(b_raw + ks * 1024, kBChunkBytes, 1024, Swizzle::k128B);
-            const uint64_t bl = smem_desc(b_lo + ks * 1024, kBChunkBytes, 1024, Swizzle::k128B);
-            const uint32_t first = (kb == 0 && ks == 0) ? 0u : 1u;
-            mma_tf32(d, al, bh, idesc, first);
-            mma_tf32(d, ah, bl, idesc, 1u);
-            mma_tf32(d, ah, bh, idesc, 1u);
+            for (int ks = 0; ks < kBK / 8; ++ks) {
+              // K-major, 64-byte swizzle: 8-row groups 512 B apart; the second
+              // k-step starts 32 B into each row.
+              const uint64_t ah = smem_desc(a_hi + ks * 32, 16, 512, Swizzle::k64B);
+              const uint64_t al = smem_desc(a_lo + ks * 32, 16, 512, Swizzle::k64B);
+              const uint64_t bh = smem_desc(b_hi + ks * 32, 16, 512, Swizzle::k64B);
+              const uint64_t bl = smem_desc(b_lo + ks * 32, 16, 512, Swizzle::k64B);
+              const uint32_t first = (kb == kc && ks == 0) ? 0u : 1u;
+              mma_tf32(d, al, bh, idesc, first);
+              mma_tf32(d, ah, bl, idesc, 1u);
+              mma_tf32(d, ah, bh, idesc, 1u);
+            }
+            mma_commit(&s.op_empty[stage]);
+            if (++stage == kOpStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          mma_commit(&s.empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+          if (!ok) break;
+          mma_commit(&s.tmem_full[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
           }
-        }
-        if (!ok) break;
-        mma_commit(&s.tmem_full[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
         }
       }
       // All MMAs this thread issued are complete once mma_done fires.
@@ -228,81 +272,126 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
       int dummy = 0;
       mbar_wait(&s.mma_done, 0, err, &dummy);
     }
-  } else if (warp < 6) {
-    // ---------------- hi/lo split ----------------
+  } else if (warp < kFirstEpilogueWarp) {
+    // ---------------- hi/lo split (+ B transpose) ----------------
     const int tid = threadIdx.x - 64;
-    int stage = 0;
-    uint32_t phase = 0;
+    int rstage = 0, ostage = 0;
+    uint32_t rphase = 0, ophase = 0;
     for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
       const TileGeom g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
-      const int nb4 = ((g.ncols + 31) >> 5) * (kBChunkBytes / 16);
+      const int nrows_b = ((g.ncols + 31) >> 5) << 5;  // B rows (columns of W) loaded
       bool ok = true;
       for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&s.full[stage], phase, err, failed)) {
+        if (!mbar_wait(&s.raw_full[rstage], rphase, err, failed) ||
+            !mbar_wait(&s.op_empty[ostage], ophase ^ 1u, err, failed)) {
           ok = false;
           break;
         }
-        uint8_t* st = s.stage[stage];
-        float4* a_raw = reinterpret_cast<float4*>(st);
-        float4* a_lo = reinterpret_cast<float4*>(st + kOffALo);
-        float4* b_raw = reinterpret_cast<float4*>(st + kOffBRaw);
-        float4* b_lo = reinterpret_cast<float4*>(st + kOffBLo);
+        const uint8_t* raw = s.raw[rstage];
+        uint8_t* op = s.op[ostage];
+        // A: same K-major layout in and out.
 #pragma unroll
-        for (int i = tid; i < kABytes / 16; i += kSplitThreads) split_vec(a_raw, a_lo, i);
-        for (int i = tid; i < nb4; i += kSplitThreads) split_vec(b_raw, b_lo, i);
+        for (int i = tid; i < kABytes / 16; i += kSplitThreads) {
+          float4 h, l;
+          split4(reinterpret_cast<const float4*>(raw)[i], h, l);
+          reinterpret_cast<float4*>(op + kOffAHi)[i] = h;
+          reinterpret_cast<float4*>(op + kOffALo)[i] = l;
+        }
+        // B: N-major raw -> K-major hi/lo. Item (n, kc): a warp covers 32
+        // consecutive n of one kc, so the 4 scalar reads per row are
+        // conflict-free and the 16-byte writes take the minimum 4 wavefronts.
+        const uint8_t* braw = raw + kOffBRaw;
+        for (int it = tid; it < nrows_b * 4; it += kSplitThreads) {
+          const int n = (it & 31) + ((it >> 7) << 5);
+          const int kc = (it >> 5) & 3;
+          float4 v;
+          v.x = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 0, n));
+          v.y = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 1, n));
+          v.z = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 2, n));
+          v.w = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 3, n));
+          float4 h, l;
+          split4(v, h, l);
+          const int o = kmajor64_offset(n, kc);
+          *reinterpret_cast<float4*>(op + kOffBHi + o) = h;
+          *reinterpret_cast<float4*>(op + kOffBLo + o) = l;
+        }
+        // Order this thread's generic reads (raw) and writes (operands)
+        // before the async proxy (next TMA into raw, MMA reads of op).
         fence_proxy_async_smem();
-        mbar_arrive(&s.split[stage]);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+        mbar_arrive(&s.raw_empty[rstage]);
+        mbar_arrive(&s.op_full[ostage]);
+        if (++rstage == kRawStages) {
+          rstage = 0;
+          rphase ^= 1u;
+        }
+        if (++ostage == kOpStages) {
+          ostage = 0;
+          ophase ^= 1u;
         }
       }
       if (!ok) break;
     }
   } else {
-    // ---------------- epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    // ---------------- epilogue: promotion + store ----------------
+    const int ew = warp - kFirstEpilogueWarp;
+    const int quarter = warp & 3;      // TMEM lanes this warp may access
+    const int cgroup = ew >> 2;        // 64-column group of the tile
     const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool vec = (output & 3) == 0;
-    for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok && !*failed; t += gridDim.x) {
       const TileGeom g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
-      if (!mbar_wait(&s.tmem_full[acc], acc_phase, err, failed)) break;
-      tc_fence_after();
-      const int row = g.base + row_in_tile;
-      const bool valid = row >= g.row0 && row < g.row_end;
-      float* out = y + static_cast<long long>(row) * output + g.col0;
-      for (int c0 = 0; c0 < g.ncols; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + static_cast<uint32_t>(acc * kBN + c0) +
-                               (static_cast<uint32_t>(quarter * 32) << 16),
-                           r);
-        tmem_ld_wait();
-        if (valid) {
-          const int w = min(32, g.ncols - c0);
-          if (vec) {
+      const int c_begin = cgroup * kEpiCols;
+      const bool active = c_begin < g.ncols;  // warp-uniform
+      float sum[kEpiCols];
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              if (j < w) {
-                *reinterpret_cast<float4*>(out + c0 + j) =
-                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-              }
-            }
-          } else {
+      for (int j = 0; j < kEpiCols; ++j) sum[j] = 0.0f;
+      for (int kc = 0; kc < num_kb; kc += kChunkKb) {
+        if (!mbar_wait(&s.tmem_full[acc], acc_phase, err, failed)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (active) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < w) out[c0 + j] = __uint_as_float(r[j]);
-            }
+          for (int c = 0; c < kEpiCols; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(tmem + static_cast<uint32_t>(acc * kBN + c_begin + c) + lane_addr,
+                               r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sum[c + j] += __uint_as_float(r[j]);
           }
         }
+        tc_fence_before();
+        mbar_arrive(&s.tmem_empty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&s.tmem_empty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
+      if (!ok) break;
+      const int row = g.base + row_in_tile;
+      if (active && row >= g.row0 && row < g.row_end) {
+        const int w = min(kEpiCols, g.ncols - c_begin);
+        float* out = y + static_cast<long long>(row) * output + g.col0 + c_begin;
+        if (vec) {
+#pragma unroll
+          for (int j = 0; j < kEpiCols; j += 4) {
+            if (j < w) {
+              *reinterpret_cast<float4*>(out + j) =
+                  make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kEpiCols; ++j) {
+            if (j < w) out[j] = sum[j];
+          }
+        }
       }
     }
   }
@@ -310,10 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
   __syncthreads();
   if (warp == 0 && lane == 0 && *failed) {
     // Drain TMA loads still in flight into this CTA's shared memory.
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kRawStages; ++i) {
       if (s.issued[i] > 0) {
         int dummy = 0;
-        mbar_wait(&s.full[i], static_cast<uint32_t>((s.issued[i] - 1) & 1), err, &dummy);
+        mbar_wait(&s.raw_full[i], static_cast<uint32_t>((s.issued[i] - 1) & 1), err, &dummy);
       }
     }
   }
