@@ -48,6 +48,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stages", action="store_true", help="print the per-stage table to stderr")
+    ap.add_argument("--only-stage", default=None,
+                    choices=["dense_gemm", "topk_gate", "histogram_exclusive_scan",
+                             "token_permute", "grouped_gemm", "unpermute"],
+                    help="profiling aid: run the chain once, then time only this stage")
     return ap.parse_args()
 
 
@@ -189,27 +193,33 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     stage_names = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
                    "grouped_gemm", "unpermute"]
 
-    def step(events=None):
-        def mark(i):
+    def step(events=None, only=None):
+        """One chain step, stage by stage; `only` runs just that stage index."""
+        calls = [
+            lambda: rr.dense_gemm(inp.x, inp.router_w, buf.logits, tokens, e, k, ctx=ctx),
+            lambda: rr.topk_gate_biased(buf.logits, inp.logit_bias, buf.expert_ids,
+                                        buf.route_weights, tokens, e, ctx=ctx),
+            lambda: rr.histogram_exclusive_scan(buf.expert_ids, buf.counts, buf.offsets, routes,
+                                                e, ctx=ctx),
+            lambda: rr.token_permute(inp.x, buf.expert_ids, buf.offsets, buf.x_permuted,
+                                     buf.route_pos, None, tokens, e, 2, k, buf.workspace,
+                                     ctx=ctx),
+            lambda: rr.grouped_gemm(buf.x_permuted, inp.expert_w, buf.offsets, buf.y_permuted,
+                                    e, k, n, routes, ctx=ctx),
+            lambda: rr.unpermute(buf.y_permuted, buf.route_pos, buf.route_weights, buf.y, tokens,
+                                 2, n, ctx=ctx),
+        ]
+        for i, call in enumerate(calls):
+            if only is not None and i != only:
+                continue
             if events is not None:
                 events[i].record(stream)
-        mark(0)
-        rr.dense_gemm(inp.x, inp.router_w, buf.logits, tokens, e, k, ctx=ctx)
-        mark(1)
-        rr.topk_gate_biased(buf.logits, inp.logit_bias, buf.expert_ids, buf.route_weights,
-                            tokens, e, ctx=ctx)
-        mark(2)
-        rr.histogram_exclusive_scan(buf.expert_ids, buf.counts, buf.offsets, routes, e, ctx=ctx)
-        mark(3)
-        rr.token_permute(inp.x, buf.expert_ids, buf.offsets, buf.x_permuted, buf.route_pos, None,
-                         tokens, e, 2, k, buf.workspace, ctx=ctx)
-        mark(4)
-        rr.grouped_gemm(buf.x_permuted, inp.expert_w, buf.offsets, buf.y_permuted, e, k, n,
-                        routes, ctx=ctx)
-        mark(5)
-        rr.unpermute(buf.y_permuted, buf.route_pos, buf.route_weights, buf.y, tokens, 2, n,
-                     ctx=ctx)
-        mark(6)
+            call()
+            if events is not None:
+                events[i + 1].record(stream)
+
+    if args.only_stage is not None:
+        return run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -340,6 +350,26 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(inp, steps=1)
     return line
+
+
+def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) -> dict:
+    """Runs the whole chain once (untimed setup), then `steps` launches of one
+    stage through the same C ABI call the chain uses; reports its mean time.
+    Meant as a small, single-kernel command for Nsight Compute."""
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    with torch.cuda.stream(stream):
+        step(ev)
+    stream.synchronize()
+    idx = stage_names.index(args.only_stage)
+    times = []
+    for _ in range(max(1, args.steps)):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        with torch.cuda.stream(stream):
+            step(evs, only=idx)
+        stream.synchronize()
+        times.append(evs[idx].elapsed_time(evs[idx + 1]))
+    return {"stage": args.only_stage, "tokens": tokens, "ms": statistics.mean(times),
+            "ms_min": min(times)}
 
 
 # ---------------------------------------------------------------------------

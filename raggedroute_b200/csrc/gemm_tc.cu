@@ -12,10 +12,10 @@
 // accumulator; the dropped lo_a*lo_b term and the TF32 rounding of lo are
 // below 2^-21 relative per product. The tensor core's own accumulate step
 // loses precision with a consistent bias (measured: 2.9e-5 normwise at
-// K=4096), so the accumulator is promoted every kChunkK = 256 of K: each
-// chunk is accumulated from zero in TMEM and added into FP32 registers of the
-// epilogue warps with round-to-nearest adds. That keeps the error near
-// 2e-6 normwise at K=4096, inside the 1e-5 contract.
+// K=4096), so the accumulator is promoted every 512 of K: each chunk is
+// accumulated from zero into the partial P (TMEM columns 0-255) and added,
+// with round-to-nearest FP32 adds on the CUDA cores, into the running sum S
+// (TMEM columns 256-511). The last chunk's S + P goes straight to global.
 //
 // Structure: a persistent CTA per SM walks the device-side tile schedule
 // (tile_sched.cuh, read from offsets, no host sync). Tiles are 128 rows x 256
@@ -23,18 +23,18 @@
 //   warp 0     TMA producer: A (x rows, K-major, 64-byte swizzle) and B (the
 //              expert's [K, N] weights, N-major, 128-byte swizzle) per 16-wide
 //              k-block into a 4-slot raw ring; no multicast.
-//   warps 2-3  split: hi/lo of each landed k-block into a 2-slot operand ring.
-//              kind::tf32 MMAs take K-major operands only (an N-major B reads
-//              as zeros on sm_100a), so B is transposed to K-major here, with
-//              a bank-conflict-free lane mapping; the raw slot is released as
-//              soon as it has been read.
-//   warp 1     MMA issuer: 3 tcgen05.mma (M=128, N<=256, K=8) per k-step; each
-//              256-wide K chunk goes to one of two TMEM accumulators
-//              (2 x 256 columns), alternating, so promotion of chunk c and the
-//              store of tile i overlap the MMAs of the next chunk / tile.
-//   warps 4-19 epilogue: 16 warps = 4 TMEM lane quarters x 4 column groups of
-//              64; each thread keeps its 64 running sums in registers, adds
-//              each finished chunk (tcgen05.ld) and stores the row at the end.
+//   warp 1     MMA issuer: 3 tcgen05.mma (M=128, N<=256, K=8) per k-step into
+//              P; it waits for P to be promoted before the next chunk.
+//   warps 2-17 workers (16 warps = 4 TMEM lane quarters x 4 column groups):
+//              (a) split: hi/lo of each landed k-block into a 2-slot operand
+//              ring. kind::tf32 MMAs take K-major operands only (an N-major B
+//              reads as zeros on sm_100a), so B is transposed to K-major here
+//              with a bank-conflict-free lane mapping; the raw slot is released
+//              as soon as it has been read.
+//              (b) promotion: S = P, S += P, or y = S + P for the tile's last
+//              chunk, each thread covering 64 columns of one TMEM lane.
+//              Promotion of chunk c runs after the first k-block of the next
+//              chunk has been split, so the MMA resumes at once.
 // A partial last m-tile of an expert is loaded shifted back so it ends at the
 // segment end: TMA never reads a row at or beyond offsets[E], and rows before
 // the segment come from the previous expert (computed, never stored) or are
@@ -68,17 +68,15 @@ constexpr int kOffAHi = 0;
 constexpr int kOffALo = kABytes;
 constexpr int kOffBHi = 2 * kABytes;
 constexpr int kOffBLo = 2 * kABytes + kBBytes;
-constexpr int kChunkKb = 16;  // k-blocks per promoted chunk (K = 256)
-constexpr int kSplitWarps = 2;
-constexpr int kEpilogueWarps = 16;
-constexpr int kFirstEpilogueWarp = 2 + kSplitWarps;
-// 640 threads: the 96-register cap leaves room for 64 running sums per
-// epilogue thread without spills.
-constexpr int kThreads = (kFirstEpilogueWarp + kEpilogueWarps) * 32;
+constexpr int kChunkKb = 32;  // k-blocks per promoted chunk (K = 512)
+constexpr uint32_t kColP = 0;  // TMEM columns of the chunk partial
+constexpr uint32_t kColS = 256;  // TMEM columns of the running sum
+constexpr int kWorkerWarps = 16;
+constexpr int kFirstWorkerWarp = 2;
+constexpr int kThreads = (kFirstWorkerWarp + kWorkerWarps) * 32;  // 576
 constexpr int kTmemCols = 512;
-constexpr int kSplitThreads = kSplitWarps * 32;
-constexpr int kEpilogueThreads = kEpilogueWarps * 32;
-constexpr int kEpiCols = kBN / 4;  // columns per epilogue thread
+constexpr int kWorkerThreads = kWorkerWarps * 32;
+constexpr int kEpiCols = kBN / 4;  // columns per worker thread
 
 struct alignas(1024) Smem {
   uint8_t raw[kRawStages][kRawBytes];
@@ -87,8 +85,8 @@ struct alignas(1024) Smem {
   uint64_t raw_empty[kRawStages];
   uint64_t op_full[kOpStages];
   uint64_t op_empty[kOpStages];
-  uint64_t tmem_full[2];
-  uint64_t tmem_empty[2];
+  uint64_t tmem_full;   // P holds a finished chunk
+  uint64_t tmem_empty;  // P has been promoted
   uint64_t mma_done;
   uint32_t tmem_base;
   int failed;
@@ -154,17 +152,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRawStages; ++i) {
       mbar_init(&s.raw_full[i], 1);
-      mbar_init(&s.raw_empty[i], kSplitThreads);
+      mbar_init(&s.raw_empty[i], kWorkerWarps);
       s.issued[i] = 0;
     }
     for (int i = 0; i < kOpStages; ++i) {
-      mbar_init(&s.op_full[i], kSplitThreads);
+      mbar_init(&s.op_full[i], kWorkerWarps);
       mbar_init(&s.op_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s.tmem_full[i], 1);
-      mbar_init(&s.tmem_empty[i], kEpilogueThreads);
-    }
+    mbar_init(&s.tmem_full, 1);
+    mbar_init(&s.tmem_empty, kWorkerWarps);
     mbar_init(&s.mma_done, 1);
     s.failed = 0;
     fence_mbar_init();
@@ -214,7 +210,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok && !*failed; t += gridDim.x) {
@@ -222,12 +217,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         const int n_mma = (g.ncols + 15) & ~15;
         const uint32_t idesc = idesc_tf32(kBM, n_mma, false, false);
         for (int kc = 0; kc < num_kb && ok; kc += kChunkKb) {
-          if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, err, failed)) {
+          if (!mbar_wait(&s.tmem_empty, acc_phase ^ 1u, err, failed)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + static_cast<uint32_t>(acc * kBN);
+          const uint32_t d = tmem + kColP;
           const int kend = min(num_kb, kc + kChunkKb);
           for (int kb = kc; kb < kend; ++kb) {
             if (!mbar_wait(&s.op_full[stage], phase, err, failed)) {
@@ -260,11 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
             }
           }
           if (!ok) break;
-          mma_commit(&s.tmem_full[acc]);
-          if (++acc == 2) {
-            acc = 0;
-            acc_phase ^= 1u;
-          }
+          mma_commit(&s.tmem_full);
+          acc_phase ^= 1u;
         }
       }
       // All MMAs this thread issued are complete once mma_done fires.
@@ -272,54 +264,69 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
       int dummy = 0;
       mbar_wait(&s.mma_done, 0, err, &dummy);
     }
-  } else if (warp < kFirstEpilogueWarp) {
-    // ---------------- hi/lo split (+ B transpose) ----------------
-    const int tid = threadIdx.x - 64;
+  } else {
+    // ---------------- workers: split + promotion + store ----------------
+    const int tid = threadIdx.x - kFirstWorkerWarp * 32;  // 0..511
+    const int ew = warp - kFirstWorkerWarp;
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int cgroup = ew >> 2;    // 64-column group of the tile
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const bool vec = (output & 3) == 0;
     int rstage = 0, ostage = 0;
-    uint32_t rphase = 0, ophase = 0;
-    for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
-      const TileGeom g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
-      const int nrows_b = ((g.ncols + 31) >> 5) << 5;  // B rows (columns of W) loaded
-      bool ok = true;
-      for (int kb = 0; kb < num_kb; ++kb) {
+    uint32_t rphase = 0, ophase = 0, acc_phase = 0;
+    // The chunk awaiting promotion (tile geometry + whether it ends its tile).
+    bool pending = false, pending_first = false, pending_last = false;
+    TileGeom pg{};
+    int t = blockIdx.x;
+    int kb = 0;
+    TileGeom g{};
+    if (t < total) g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
+    // One iteration = split one k-block (while any remain), then promote the
+    // previously finished chunk. A final iteration without a k-block drains
+    // the last chunk.
+    while (!*failed) {
+      const bool have_block = t < total;
+      if (have_block) {
         if (!mbar_wait(&s.raw_full[rstage], rphase, err, failed) ||
             !mbar_wait(&s.op_empty[ostage], ophase ^ 1u, err, failed)) {
-          ok = false;
           break;
         }
-        const uint8_t* raw = s.raw[rstage];
-        uint8_t* op = s.op[ostage];
-        // A: same K-major layout in and out.
-#pragma unroll
-        for (int i = tid; i < kABytes / 16; i += kSplitThreads) {
+        const uint32_t raw = smem_u32(s.raw[rstage]);
+        const uint32_t op = smem_u32(s.op[ostage]);
+        // A: same K-major layout in and out (one 16-byte chunk per thread).
+        {
           float4 h, l;
-          split4(reinterpret_cast<const float4*>(raw)[i], h, l);
-          reinterpret_cast<float4*>(op + kOffAHi)[i] = h;
-          reinterpret_cast<float4*>(op + kOffALo)[i] = l;
+          split4(lds_v4(raw + tid * 16), h, l);
+          sts_v4(op + kOffAHi + tid * 16, h);
+          sts_v4(op + kOffALo + tid * 16, l);
         }
         // B: N-major raw -> K-major hi/lo. Item (n, kc): a warp covers 32
         // consecutive n of one kc, so the 4 scalar reads per row are
         // conflict-free and the 16-byte writes take the minimum 4 wavefronts.
-        const uint8_t* braw = raw + kOffBRaw;
-        for (int it = tid; it < nrows_b * 4; it += kSplitThreads) {
+        const uint32_t braw = raw + kOffBRaw;
+        const int nitems_b = (((g.ncols + 31) >> 5) << 5) * 4;
+        for (int it = tid; it < nitems_b; it += kWorkerThreads) {
           const int n = (it & 31) + ((it >> 7) << 5);
           const int kc = (it >> 5) & 3;
           float4 v;
-          v.x = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 0, n));
-          v.y = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 1, n));
-          v.z = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 2, n));
-          v.w = *reinterpret_cast<const float*>(braw + nmajor128_offset(4 * kc + 3, n));
+          v.x = lds_f32(braw + nmajor128_offset(4 * kc + 0, n));
+          v.y = lds_f32(braw + nmajor128_offset(4 * kc + 1, n));
+          v.z = lds_f32(braw + nmajor128_offset(4 * kc + 2, n));
+          v.w = lds_f32(braw + nmajor128_offset(4 * kc + 3, n));
           float4 h, l;
           split4(v, h, l);
           const int o = kmajor64_offset(n, kc);
-          *reinterpret_cast<float4*>(op + kOffBHi + o) = h;
-          *reinterpret_cast<float4*>(op + kOffBLo + o) = l;
+          sts_v4(op + kOffBHi + o, h);
+          sts_v4(op + kOffBLo + o, l);
         }
         // Order this thread's generic reads (raw) and writes (operands)
         // before the async proxy (next TMA into raw, MMA reads of op).
         fence_proxy_async_smem();
-        mbar_arrive(&s.raw_empty[rstage]);
-        mbar_arrive(&s.op_full[ostage]);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.raw_empty[rstage]);
+          mbar_arrive(&s.op_full[ostage]);
+        }
         if (++rstage == kRawStages) {
           rstage = 0;
           rphase ^= 1u;
@@ -329,69 +336,73 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
           ophase ^= 1u;
         }
       }
-      if (!ok) break;
-    }
-  } else {
-    // ---------------- epilogue: promotion + store ----------------
-    const int ew = warp - kFirstEpilogueWarp;
-    const int quarter = warp & 3;      // TMEM lanes this warp may access
-    const int cgroup = ew >> 2;        // 64-column group of the tile
-    const int row_in_tile = quarter * 32 + lane;
-    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    const bool vec = (output & 3) == 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < total && ok && !*failed; t += gridDim.x) {
-      const TileGeom g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
-      const int c_begin = cgroup * kEpiCols;
-      const bool active = c_begin < g.ncols;  // warp-uniform
-      float sum[kEpiCols];
-#pragma unroll
-      for (int j = 0; j < kEpiCols; ++j) sum[j] = 0.0f;
-      for (int kc = 0; kc < num_kb; kc += kChunkKb) {
-        if (!mbar_wait(&s.tmem_full[acc], acc_phase, err, failed)) {
-          ok = false;
-          break;
-        }
+      if (pending) {
+        // Promotion of the finished chunk in P.
+        if (!mbar_wait(&s.tmem_full, acc_phase, err, failed)) break;
         tc_fence_after();
+        const int c_begin = cgroup * kEpiCols;
+        const bool active = c_begin < pg.ncols;  // warp-uniform
+        const int row = pg.base + quarter * 32 + lane;
+        const bool store_row = pending_last && active && row >= pg.row0 && row < pg.row_end;
+        float* out = y + static_cast<long long>(row) * output + pg.col0 + c_begin;
+        const int w = min(kEpiCols, pg.ncols - c_begin);
         if (active) {
 #pragma unroll
           for (int c = 0; c < kEpiCols; c += 16) {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(tmem + static_cast<uint32_t>(acc * kBN + c_begin + c) + lane_addr,
-                               r);
-            tmem_ld_wait();
+            const uint32_t col = static_cast<uint32_t>(c_begin + c);
+            uint32_t p[16];
+            tmem_ld_32x32b_x16(tmem + kColP + col + lane_addr, p);
+            if (!pending_first) {
+              uint32_t q[16];
+              tmem_ld_32x32b_x16(tmem + kColS + col + lane_addr, q);
+              tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) sum[c + j] += __uint_as_float(r[j]);
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&s.tmem_empty[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
-        }
-      }
-      if (!ok) break;
-      const int row = g.base + row_in_tile;
-      if (active && row >= g.row0 && row < g.row_end) {
-        const int w = min(kEpiCols, g.ncols - c_begin);
-        float* out = y + static_cast<long long>(row) * output + g.col0 + c_begin;
-        if (vec) {
+              for (int j = 0; j < 16; ++j) {
+                p[j] = __float_as_uint(__uint_as_float(q[j]) + __uint_as_float(p[j]));
+              }
+            } else {
+              tmem_ld_wait();
+            }
+            if (!pending_last) {
+              tmem_st_32x32b_x16(tmem + kColS + col + lane_addr, p);
+            } else if (store_row) {
+              if (vec) {
 #pragma unroll
-          for (int j = 0; j < kEpiCols; j += 4) {
-            if (j < w) {
-              *reinterpret_cast<float4*>(out + j) =
-                  make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                for (int j = 0; j < 16; j += 4) {
+                  if (c + j < w) {
+                    *reinterpret_cast<float4*>(out + c + j) =
+                        make_float4(__uint_as_float(p[j]), __uint_as_float(p[j + 1]),
+                                    __uint_as_float(p[j + 2]), __uint_as_float(p[j + 3]));
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  if (c + j < w) out[c + j] = __uint_as_float(p[j]);
+                }
+              }
             }
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < kEpiCols; ++j) {
-            if (j < w) out[j] = sum[j];
-          }
+          if (!pending_last) tmem_st_wait();
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tmem_empty);
+        acc_phase ^= 1u;
+        pending = false;
+      }
+      if (!have_block) break;
+      // The k-block just split ends a chunk: it is promoted next iteration.
+      if ((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) {
+        pending = true;
+        pending_first = kb < kChunkKb;
+        pending_last = (kb + 1 == num_kb);
+        pg = g;
+      }
+      if (++kb == num_kb) {
+        kb = 0;
+        t += gridDim.x;
+        if (t < total) g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
       }
     }
   }
