@@ -122,6 +122,22 @@ rr_status rr_token_permute(const float* x, const int32_t* expert_ids, const int3
                            const rr_context* ctx);
 size_t rr_token_permute_workspace_size(int tokens, int experts, int top_k, int hidden);
 
+/* rr_token_permute for callers that cannot allocate device memory: same
+ * arguments, results and checks, but ctx->workspace is ignored and the
+ * scratch lives in a fixed 4 MiB array inside the library (held by every GPU
+ * that loads it until exit). It has no counterpart in the reference; it
+ * exists for callers whose device memory is owned by a planner or pool with
+ * nothing spare, or that reach this library through a binding without access
+ * to a CUDA allocator. Calls whose rr_token_permute_workspace_size exceeds
+ * 4 MiB fail with RR_INVALID_ARGUMENT. It never allocates or frees. All calls
+ * share the array, so calls that overlap on the GPU race and must be
+ * serialised by the caller; the first call on each device looks up the
+ * array's address and should precede any stream capture. */
+rr_status rr_token_permute_no_alloc(const float* x, const int32_t* expert_ids,
+                                    const int32_t* offsets, float* x_permuted, int32_t* route_pos,
+                                    int32_t* sorted_route, int tokens, int experts, int top_k,
+                                    int hidden, const rr_context* ctx);
+
 /* raggedroute::grouped_gemm, src/grouped_gemm/operator.cpp:17-49.
  * y_permuted[r, :] = x_permuted[r, :] . W[e] for r in [offsets[e],
  * offsets[e+1]); W is [experts, hidden, output]. max_expert_tokens is the

@@ -84,6 +84,7 @@ SIGNATURES = {
     "rr_histogram_exclusive_scan_workspace_size": (ctypes.c_size_t, [_I, _I]),
     "rr_token_permute": (RRStatus, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _CTX]),
     "rr_token_permute_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I]),
+    "rr_token_permute_no_alloc": (RRStatus, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _CTX]),
     "rr_grouped_gemm": (RRStatus, [_P, _P, _P, _P, _I, _I, _I, _I, _CTX]),
     "rr_grouped_gemm_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
     "rr_unpermute": (RRStatus, [_P, _P, _P, _P, _I, _I, _I, _CTX]),
