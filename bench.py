@@ -14,7 +14,10 @@ through libraggedroute_b200's C ABI on one stream. `value` is device-timed
 through rr_chain_from_tokens with the step's X copied in from pinned host
 memory and Y copied back inside the timed region.
 
-Multi-GPU (torchrun): every rank runs its own T=65536 tokens (weak scaling).
+Multi-GPU (torchrun): expert parallelism -- every rank runs its own T=65536
+tokens (weak scaling) and owns E/N experts (LPT placement on the expected
+router load, experts relabelled contiguously); dispatch and combine are NCCL
+all-to-all-v inside libraggedroute_b200 (rr_ep_chain_from_tokens).
 --impl reference: times the reference's own CPU implementation of the path
 (oracle/_ref, compiled from the reference sources) on bounded token samples of
 the same workload, with every host thread; rank 0 only.
@@ -23,6 +26,8 @@ from __future__ import annotations
 
 import argparse
 import json
+
+import numpy as np
 import math
 import os
 import statistics
@@ -184,10 +189,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     tokens = args.tokens or C5["tokens"]
     k, e, n = C5["hidden"], C5["experts"], C5["output"]
     routes = 2 * tokens
-    inp = c5_inputs(device, tokens)
+    inp = c5_inputs(device, tokens, rank=rank)
     buf = rr.ChainBuffers.allocate(tokens, k, e, n, device)
     stream = torch.cuda.Stream(device)
     ctx = rr.Context(stream=stream.cuda_stream)
+    ep = None
+    ep_info = None
+    if world > 1:
+        # Expert parallelism: LPT placement on the expected (bias-driven)
+        # load, experts relabelled so each rank's are contiguous.
+        from raggedroute_b200.ep import ExpertParallel
+        from raggedroute_b200.placement import (expected_loads_from_bias, imbalance,
+                                                lpt_placement, relabel_permutation)
+        bias_np = inp.logit_bias.cpu().numpy()
+        loads = expected_loads_from_bias(bias_np)
+        rank_of = lpt_placement(loads, world)
+        perm = torch.from_numpy(relabel_permutation(rank_of)).to(device)
+        inp.router_w = inp.router_w[:, perm].contiguous()
+        inp.logit_bias = inp.logit_bias[perm].contiguous()
+        inp.expert_w = inp.expert_w[perm].contiguous()
+        local = e // world
+        local_w = inp.expert_w[rank * local:(rank + 1) * local].contiguous()
+        ep = ExpertParallel(e, tokens, k, n, timeout_s=300.0)
+        contiguous = np.repeat(np.arange(world), local)
+        ep_info = {"placement": "lpt+relabel", "experts_per_rank": local,
+                   "expected_imbalance": round(imbalance(loads, rank_of, world), 4),
+                   "contiguous_imbalance": round(imbalance(loads, contiguous, world), 4)}
     torch.cuda.synchronize()
 
     stage_names = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
@@ -221,14 +248,27 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if args.only_stage is not None:
         return run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n)
 
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+
+    def ep_step():
+        ep.chain_from_tokens(inp.x, inp.router_w, local_w, buf, logit_bias=inp.logit_bias,
+                             ctx=ctx)
+
+    if ep is not None:
+        # Per-stage kernel times of this GPU's workload come from an untimed
+        # stage-by-stage pass of the single-GPU chain (same kernels).
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                step(ev[i])
+        stream.synchronize()
+
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step()
+            step() if ep is None else ep_step()
     stream.synchronize()
 
     launches0 = rr.kernel_launch_count()
     clocks = ClockSampler(local_rank)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -238,7 +278,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     with torch.cuda.stream(stream):
         start.record(stream)
         for i in range(args.steps):
-            step(ev[i])
+            step(ev[i]) if ep is None else ep_step()
         stop.record(stream)
     stop.synchronize()
     torch.cuda.synchronize()
@@ -250,6 +290,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     stage_ms = {nm: statistics.mean(ev[i][j].elapsed_time(ev[i][j + 1])
                                     for i in range(args.steps))
                 for j, nm in enumerate(stage_names)}
+    if ep is not None:
+        sent, received = ep.last_step_rows()
+        rows = torch.tensor([received], device=device, dtype=torch.float64)
+        gathered = [torch.zeros_like(rows) for _ in range(world)]
+        dist.all_gather(gathered, rows)
+        per_rank = [int(g.item()) for g in gathered]
+        ep_info["rows_received_per_rank"] = per_rank
+        ep_info["measured_imbalance"] = round(max(per_rank) / (sum(per_rank) / world), 4)
 
     # Max over ranks.
     t = torch.tensor([total_ms], device=device, dtype=torch.float64)
@@ -268,12 +316,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         x_host = inp.x.cpu().pin_memory()
         y_host = torch.empty(tokens, n, dtype=torch.float32).pin_memory()
         x_dev = torch.empty_like(inp.x)
-        with torch.cuda.stream(stream):
-            for _ in range(max(1, args.warmup)):
-                x_dev.copy_(x_host, non_blocking=True)
+        def e2e_step():
+            x_dev.copy_(x_host, non_blocking=True)
+            if ep is None:
                 rr.chain_from_tokens(x_dev, inp.router_w, inp.expert_w, buf,
                                      logit_bias=inp.logit_bias, ctx=ctx)
-                y_host.copy_(buf.y, non_blocking=True)
+            else:
+                ep.chain_from_tokens(x_dev, inp.router_w, local_w, buf,
+                                     logit_bias=inp.logit_bias, ctx=ctx)
+            y_host.copy_(buf.y, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                e2e_step()
         stream.synchronize()
         if world > 1:
             dist.barrier()
@@ -282,10 +337,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         with torch.cuda.stream(stream):
             s2.record(stream)
             for _ in range(args.steps):
-                x_dev.copy_(x_host, non_blocking=True)
-                rr.chain_from_tokens(x_dev, inp.router_w, inp.expert_w, buf,
-                                     logit_bias=inp.logit_bias, ctx=ctx)
-                y_host.copy_(buf.y, non_blocking=True)
+                e2e_step()
             e2.record(stream)
         e2.synchronize()
         te = torch.tensor([s2.elapsed_time(e2)], device=device, dtype=torch.float64)
@@ -295,6 +347,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                "h2d_bytes_per_step": x_host.numel() * 4,
                "d2h_bytes_per_step": y_host.numel() * 4}
 
+    if ep is not None:
+        ep.close()
     if rank != 0:
         return None
 
@@ -335,7 +389,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "data": "synthetic (seeded; BASELINE C5 shapes and distributions)",
         "config": {"workload": f"C5 chain_from_tokens T={tokens}/GPU K={k} E={e} top2 N={n}",
                    "tokens_per_gpu": tokens, "hidden": k, "experts": e, "output": n,
-                   "top_k": 2, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "top_k": 2, "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (X 1 GiB, W 2.95 GB); no flush"},
         "roofline": {"bound": "tensor", "kernel": "grouped_gemm", "achieved": round(achieved, 2),
                      "peak": round(peak_3x, 2), "unit": "TFLOP/s",
@@ -347,6 +401,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "gpu_launches": int(launches),
         "e2e": e2e,
     }
+    if ep_info is not None:
+        line["ep"] = ep_info
+        line["roofline"]["note"] = ("per-GPU stage pass of the single-GPU chain on rank 0's "
+                                    "tokens (same kernels), untimed region")
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(inp, steps=1)
     return line

@@ -181,6 +181,41 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
                                int output, const rr_context* ctx);
 size_t rr_chain_workspace_size(int tokens, int hidden, int experts, int output);
 
+/* ---- expert parallelism (new: the reference is single-GPU) ----------------
+ * One process per GPU. Rank g owns experts [g*E/G, (g+1)*E/G). A step runs
+ * the local routing stages, all-gathers the per-expert counts (one pinned
+ * host read per step sizes the exchange), dispatches x_permuted rows with
+ * NCCL send/recv, runs the grouped GEMM on received rows, combines back and
+ * unpermutes, all on ctx->stream. Every host wait has a deadline; on expiry
+ * the communicator is aborted and RR_COMM_ERROR returned. */
+#define RR_EP_UNIQUE_ID_BYTES 128
+typedef struct rr_ep rr_ep;
+
+/* Rank 0 creates the id; the caller distributes it to the other ranks. */
+rr_status rr_ep_get_unique_id(void* unique_id /* RR_EP_UNIQUE_ID_BYTES, host */);
+/* Plan-time: NCCL communicator (non-blocking) and worst-case receive buffers
+ * (nranks * 2 * max_tokens rows). experts must be a multiple of nranks. */
+rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int experts, int max_tokens,
+                       int hidden, int output, double timeout_seconds, rr_ep** out);
+rr_status rr_ep_destroy(rr_ep* ep);
+/* chain_from_tokens across ranks: x [tokens, K] and the replicated router
+ * weights / bias on every rank; local_expert_weights [E/G, K, N] are this
+ * rank's experts; the other buffers are as for rr_chain_from_tokens and
+ * ctx->workspace holds rr_chain_workspace_size(tokens, K, E, N) bytes. */
+rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router_weights,
+                                  const float* logit_bias, const float* local_expert_weights,
+                                  float* logits, int32_t* expert_ids, float* route_weights,
+                                  int32_t* counts, int32_t* offsets, float* x_permuted,
+                                  int32_t* route_pos, float* y_permuted, float* y, int tokens,
+                                  const rr_context* ctx);
+/* Rows this rank sent / received in its last step (load-balance reporting). */
+rr_status rr_ep_last_step_rows(const rr_ep* ep, int64_t* rows_sent, int64_t* rows_received);
+/* The exchange plan of one rank from the [nranks][experts] counts (pure host
+ * arithmetic): rows sent to / received from each peer and block offsets. */
+rr_status rr_ep_plan(const int32_t* count_all, int nranks, int rank, int experts,
+                     int64_t* send_rows, int64_t* send_offsets, int64_t* recv_rows,
+                     int64_t* recv_offsets);
+
 /* ---- low-level launchers (include/raggedroute/baseline_ops.h:14-42) ------
  * Return a cudaError_t value: cudaErrorInvalidValue (1) on bad arguments,
  * cudaSuccess for empty work. Preconditions as in the reference: histogram

@@ -58,6 +58,10 @@ cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
                                             int32_t* offsets, int routes, int experts,
                                             cudaStream_t stream);
 
+// Expert-parallel receive offsets (nranks * local <= 1024 groups).
+cudaError_t launch_ep_recv_offsets(const int32_t* count_all, int32_t* recv_offsets, int nranks,
+                                   int experts, int rank, int local, cudaStream_t stream);
+
 // permute.cu
 std::size_t permute_workspace_bytes(int tokens, int experts, int top_k);
 // Stable permute; workspace holds >= permute_workspace_bytes(...) bytes and
@@ -80,18 +84,22 @@ cudaError_t launch_unpermute(const float* y_permuted, const int32_t* route_pos,
                              int output, cudaStream_t stream);
 
 // gemm_simt.cu / gemm_tc.cu
-// Grouped GEMM with rows split by offsets[experts+1]; offsets == nullptr means
-// one group covering `rows` rows (dense GEMM).
+// Grouped GEMM with rows split by offsets[experts+1] (`experts` row groups);
+// offsets == nullptr means one group covering `rows` rows (dense GEMM). Group
+// g multiplies by weight set (g % weight_sets) of w[weight_sets, hidden,
+// output]; weight_sets = 0 means one weight set per group. The
+// expert-parallel runtime uses weight_sets < experts for its
+// (source rank, local expert) groups.
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets,
                                 float* y, int experts, int rows, int hidden, int output,
-                                cudaStream_t stream);
+                                cudaStream_t stream, int weight_sets = 0);
 cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,
-                                     cudaStream_t stream);
+                                     cudaStream_t stream, int weight_sets = 0);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
-                                   cudaStream_t stream);
+                                   cudaStream_t stream, int weight_sets = 0);
 
 // misc.cu
 cudaError_t launch_cache_scrub(uint32_t* buffer, std::size_t elements, cudaStream_t stream);

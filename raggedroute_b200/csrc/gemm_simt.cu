@@ -20,7 +20,7 @@ constexpr int kThreads = 256;
 
 __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const int32_t* __restrict__ offsets,
-    float* __restrict__ y, int experts, int rows, int hidden, int output) {
+    float* __restrict__ y, int experts, int rows, int hidden, int output, int wsets) {
   __shared__ int prefix[kMaxExperts + 1];
   __shared__ int scratch[33];
   __shared__ float as[kBK][kBM + 4];
@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
   const int ty = threadIdx.x / 16;  // row group
   for (int t = blockIdx.x; t < total; t += gridDim.x) {
     const TileCoord tc = tile_coord(t, offsets, experts, rows, prefix, kBM, kBN, n_tiles_n);
-    const float* we = w + static_cast<long long>(tc.expert) * hidden * output;
+    const float* we = w + static_cast<long long>(tc.expert % wsets) * hidden * output;
     float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
 
 cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, int weight_sets) {
+  const int wsets = weight_sets > 0 ? weight_sets : experts;
   if (output <= 0) return cudaSuccess;
   int grid = 4 * sm_count();
   if (offsets == nullptr) {
@@ -98,7 +99,7 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
     if (tiles < grid) grid = static_cast<int>(tiles);
   }
   grouped_gemm_simt_kernel<<<grid, kThreads, 0, stream>>>(x, w, offsets, y, experts, rows, hidden,
-                                                          output);
+                                                          output, wsets);
   note_launch();
   return cudaGetLastError();
 }

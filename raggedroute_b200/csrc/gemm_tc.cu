@@ -140,7 +140,7 @@ __device__ __forceinline__ int nmajor128_offset(int k, int n) {
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
     const int32_t* __restrict__ offsets, float* __restrict__ y, int experts, int rows,
-    int hidden, int output, unsigned* err) {
+    int hidden, int output, int wsets, unsigned* err) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
           tma_load_2d(st, &tma_a, &s.raw_full[stage], kb * kBK, g.base);
           for (int j = 0; j < nchunks; ++j) {
             tma_load_3d(st + kOffBRaw + j * kBChunkBytes, &tma_b, &s.raw_full[stage],
-                        g.col0 + 32 * j, kb * kBK, g.expert);
+                        g.col0 + 32 * j, kb * kBK, g.expert % wsets);
           }
           s.issued[stage] += 1;
           if (++stage == kRawStages) {
@@ -474,7 +474,8 @@ bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidde
 
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
-                                   cudaStream_t stream) {
+                                   cudaStream_t stream, int weight_sets) {
+  const int wsets = weight_sets > 0 ? weight_sets : experts;
   EncodeTiledFn encode = encode_fn();
   if (encode == nullptr || !kernel_configured()) return cudaErrorNotSupported;
   // A: x [rows, hidden] row-major. Shifted last tiles never read at or past
@@ -496,7 +497,7 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
   {
     // B: W [experts, hidden, output] viewed as {output, hidden, experts}.
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(output), static_cast<cuuint64_t>(hidden),
-                                static_cast<cuuint64_t>(experts)};
+                                static_cast<cuuint64_t>(wsets)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(output) * 4,
                                    static_cast<cuuint64_t>(output) * hidden * 4};
     const cuuint32_t box[3] = {32, kBK, 1};
@@ -516,18 +517,20 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
     if (tiles < grid) grid = static_cast<int>(tiles);
   }
   grouped_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      ma, mb, offsets, y, experts, rows, hidden, output, device_error_word());
+      ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word());
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets, float* y,
                                 int experts, int rows, int hidden, int output,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, int weight_sets) {
   if (tc_gemm_supported(x, w, y, hidden, output)) {
-    return launch_grouped_gemm_tc(x, w, offsets, y, experts, rows, hidden, output, stream);
+    return launch_grouped_gemm_tc(x, w, offsets, y, experts, rows, hidden, output, stream,
+                                  weight_sets);
   }
-  return launch_grouped_gemm_simt(x, w, offsets, y, experts, rows, hidden, output, stream);
+  return launch_grouped_gemm_simt(x, w, offsets, y, experts, rows, hidden, output, stream,
+                                  weight_sets);
 }
 
 }  // namespace rrb

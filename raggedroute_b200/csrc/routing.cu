@@ -212,6 +212,28 @@ __global__ void __launch_bounds__(kHistThreads) hist_scan_multi_kernel(
   if (threadIdx.x == 0) offsets[experts] = carry;
 }
 
+// Expert-parallel receive offsets: group q = p * local + le holds the rows
+// that source rank p routed to this rank's local expert le, i.e.
+// count_all[p * experts + rank * local + le]; offsets are their exclusive scan.
+__global__ void __launch_bounds__(1024) ep_recv_offsets_kernel(const int32_t* __restrict__ count_all,
+                                                               int32_t* __restrict__ recv_offsets,
+                                                               int nranks, int experts, int rank,
+                                                               int local) {
+  __shared__ int warp_sums[32];
+  const int groups = nranks * local;  // <= 1024
+  const int q = threadIdx.x;
+  int v = 0;
+  if (q < groups) {
+    const int p = q / local;
+    const int le = q - p * local;
+    v = count_all[static_cast<long long>(p) * experts + rank * local + le];
+  }
+  int total = 0;
+  const int excl = block_exclusive_scan(v, warp_sums, &total);
+  if (q < groups) recv_offsets[q] = excl;
+  if (q == 0) recv_offsets[groups] = total;
+}
+
 int hist_grid(long long routes) {
   const int want = ceil_div(routes, kHistThreads * 16LL);
   const int cap = 2 * sm_count();
@@ -253,6 +275,14 @@ cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
   if (err != cudaSuccess) return err;
   hist_scan_multi_kernel<<<hist_grid(routes), kHistThreads, experts * sizeof(int), stream>>>(
       ids, counts, offsets, routes, experts, vec);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_recv_offsets(const int32_t* count_all, int32_t* recv_offsets, int nranks,
+                                   int experts, int rank, int local, cudaStream_t stream) {
+  ep_recv_offsets_kernel<<<1, 1024, 0, stream>>>(count_all, recv_offsets, nranks, experts, rank,
+                                                 local);
   note_launch();
   return cudaGetLastError();
 }

@@ -1,0 +1,83 @@
+"""Python handle for the expert-parallel runtime (rr_ep_* in the C ABI).
+
+torch.distributed is only the bootstrap here: rank 0 asks the library for an
+NCCL unique id and the process group broadcasts it; the library then owns
+its own NCCL communicator and does every exchange itself.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from raggedroute_b200._lib import Context, check, lib
+from raggedroute_b200.ops import ChainBuffers, _ctx, _ptr
+
+UNIQUE_ID_BYTES = 128
+
+
+class ExpertParallel:
+    def __init__(self, experts: int, max_tokens: int, hidden: int, output: int,
+                 rank: int | None = None, world: int | None = None, group=None,
+                 timeout_s: float = 120.0):
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        self.experts, self.hidden, self.output = experts, hidden, output
+        self.local = experts // self.world
+        uid = torch.zeros(UNIQUE_ID_BYTES, dtype=torch.uint8)
+        if self.world > 1:
+            if self.rank == 0:
+                buf = (ctypes.c_uint8 * UNIQUE_ID_BYTES)()
+                check(lib().rr_ep_get_unique_id(ctypes.cast(buf, ctypes.c_void_p)),
+                      "rr_ep_get_unique_id")
+                uid = torch.tensor(list(buf), dtype=torch.uint8)
+            dev_uid = uid.cuda() if dist.get_backend(group) == "nccl" else uid
+            dist.broadcast(dev_uid, src=0, group=group)
+            uid = dev_uid.cpu()
+        raw = (ctypes.c_uint8 * UNIQUE_ID_BYTES)(*uid.tolist())
+        handle = ctypes.c_void_p()
+        check(lib().rr_ep_create(ctypes.cast(raw, ctypes.c_void_p), self.world, self.rank,
+                                 experts, max_tokens, hidden, output, timeout_s,
+                                 ctypes.byref(handle)), "rr_ep_create")
+        self._h = handle
+
+    def chain_from_tokens(self, x: torch.Tensor, router_weights: torch.Tensor,
+                          local_expert_weights: torch.Tensor, buf: ChainBuffers,
+                          logit_bias: torch.Tensor | None = None,
+                          ctx: Context | None = None) -> torch.Tensor:
+        tokens = x.shape[0]
+        check(lib().rr_ep_chain_from_tokens(
+            self._h, _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(local_expert_weights),
+            _ptr(buf.logits), _ptr(buf.expert_ids), _ptr(buf.route_weights), _ptr(buf.counts),
+            _ptr(buf.offsets), _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.y_permuted),
+            _ptr(buf.y), tokens, _ctx(ctx, buf.workspace)), "rr_ep_chain_from_tokens")
+        return buf.y
+
+    def last_step_rows(self) -> tuple[int, int]:
+        s, r = ctypes.c_int64(), ctypes.c_int64()
+        check(lib().rr_ep_last_step_rows(self._h, ctypes.byref(s), ctypes.byref(r)),
+              "rr_ep_last_step_rows")
+        return int(s.value), int(r.value)
+
+    def close(self) -> None:
+        if self._h:
+            lib().rr_ep_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def plan(count_all, rank: int):
+    """rr_ep_plan for a [nranks, experts] int32 array (host)."""
+    import numpy as np
+    c = np.ascontiguousarray(count_all, dtype=np.int32)
+    g, e = c.shape
+    out = [np.zeros(g, np.int64) for _ in range(4)]
+    ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    check(lib().rr_ep_plan(ptr(c), g, rank, e, *[ptr(a) for a in out]), "rr_ep_plan")
+    return tuple(out)  # send_rows, send_offsets, recv_rows, recv_offsets

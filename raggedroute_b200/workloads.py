@@ -128,12 +128,14 @@ def offsets_from_sizes(sizes: np.ndarray) -> np.ndarray:
     return np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
 
 
-def c5_inputs(device="cuda", tokens: int | None = None) -> ChainInputs:
+def c5_inputs(device="cuda", tokens: int | None = None, rank: int = 0) -> ChainInputs:
     """Expert-parallel chain_from_tokens, T=65536 K=4096 E=128 N=1408, seed 4,
-    router logits biased by log-Zipf(1.0) per expert."""
+    router logits biased by log-Zipf(1.0) per expert. Each rank of a
+    multi-GPU run draws its own token batch (seed offset by rank); the
+    weights are shared."""
     t = tokens or C5["tokens"]
     k, e, n, s = C5["hidden"], C5["experts"], C5["output"], C5["seed"]
-    return ChainInputs(x=normal((t, k), 1.0, s * 10 + 1, device),
+    return ChainInputs(x=normal((t, k), 1.0, s * 10 + 1 + 1000 * rank, device),
                        router_w=normal((k, e), 1.0 / math.sqrt(k), s * 10 + 2, device),
                        logit_bias=torch.from_numpy(zipf_log_bias(e, 1.0)).to(device),
                        expert_w=normal((e, k, n), 1.0 / math.sqrt(k), s * 10 + 3, device))

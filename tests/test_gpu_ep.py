@@ -1,0 +1,51 @@
+"""Expert-parallel chain on the GPU.
+
+* One rank (no communicator): rr_ep_chain_from_tokens equals
+  rr_chain_from_tokens bit for bit.
+* Two or more GPUs: tests/ep_worker.py under torchrun; every rank's EP output
+  must equal its single-GPU chain bit for bit (LPT-relabelled experts, Zipf
+  logit bias). Skipped, with the reason, when fewer than two GPUs are visible.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_ep_single_rank_matches_chain(rrlib, cuda):
+    from raggedroute_b200.ep import ExpertParallel
+    from raggedroute_b200.workloads import normal, zipf_log_bias
+    t, k, e, n = 2000, 256, 64, 128
+    x = normal((t, k), 1.0, 11, cuda)
+    wr = normal((k, e), 1 / 16, 12, cuda)
+    we = normal((e, k, n), 1 / 16, 13, cuda)
+    bias = torch.from_numpy(zipf_log_bias(e, 1.0)).to(cuda)
+    ep = ExpertParallel(e, t, k, n, rank=0, world=1)
+    b1 = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    b2 = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    ep.chain_from_tokens(x, wr, we, b1, logit_bias=bias)
+    rrlib.chain_from_tokens(x, wr, we, b2, logit_bias=bias)
+    torch.cuda.synchronize()
+    assert torch.equal(b1.route_pos, b2.route_pos)
+    assert torch.equal(b1.y.view(torch.int32), b2.y.view(torch.int32))
+    assert ep.last_step_rows() == (2 * t, 2 * t)
+    ep.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
+def test_ep_multi_gpu_matches_single_gpu_chain(rrlib, cuda):
+    world = min(torch.cuda.device_count(), 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
+           "--master-port=29531", os.path.join(ROOT, "tests", "ep_worker.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert res.returncode == 0, res.stdout[-4000:] + res.stderr[-4000:]
