@@ -177,6 +177,16 @@ def load_traffic(name: str):
 # our arm
 # ---------------------------------------------------------------------------
 
+def workload_config(tokens: int, world: int) -> dict:
+    """The `config` object both arms report (BASELINE C5 per GPU)."""
+    from raggedroute_b200.workloads import C5
+    k, e, n = C5["hidden"], C5["experts"], C5["output"]
+    return {"workload": f"C5 chain_from_tokens T={tokens}/GPU K={k} E={e} top2 N={n}",
+            "tokens_per_gpu": tokens, "hidden": k, "experts": e, "output": n, "top_k": 2,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (X 1 GiB, W 2.95 GB); no flush"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -387,10 +397,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 GEMMs)",
         "data": "synthetic (seeded; BASELINE C5 shapes and distributions)",
-        "config": {"workload": f"C5 chain_from_tokens T={tokens}/GPU K={k} E={e} top2 N={n}",
-                   "tokens_per_gpu": tokens, "hidden": k, "experts": e, "output": n,
-                   "top_k": 2, "parallelism": f"ep{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (X 1 GiB, W 2.95 GB); no flush"},
+        "config": workload_config(tokens, world),
         "roofline": {"bound": "tensor", "kernel": "grouped_gemm", "achieved": round(achieved, 2),
                      "peak": round(peak_3x, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak_3x, 4),
@@ -482,7 +489,13 @@ def cpu_baseline(inp, steps: int = 1, sample_tokens: int = 32) -> dict:
                       f"functions (oracle/_ref), {threads} host threads"}
 
 
+C5_TOKENS = 65536
+
+
 def run_reference(args, rank: int) -> dict | None:
+    """Times the reference's CPU implementation of the path on bounded samples
+    of the C5 workload: each step runs `sample` tokens through the reference
+    CPU chain and the value is tokens per second (rank 0 only)."""
     if rank != 0:
         return None
     ref = _ref_lib()
@@ -503,23 +516,37 @@ def run_reference(args, rank: int) -> dict | None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f64 (reference CPU oracle)", "data": "synthetic (seeded; C5 sample)",
-            "config": {"workload": f"C5 chain_from_tokens sample T={sample} K=4096 E=128 top2 "
-                                   "N=1408", "parallelism": "host threads"},
+            "config": workload_config(C5_TOKENS, args.gpus),
             "impl": "reference", "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
 
 def main() -> int:
+    # Only the JSON line goes to stdout: libraries (NCCL prints its version on
+    # communicator creation) write to stdout too, so fd 1 is pointed at stderr
+    # for the run and the result is written to the saved descriptor.
+    result_fd = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    try:
+        line = _main()
+    finally:
+        sys.stdout.flush()
+        os.dup2(result_fd, 1)
+    if line is not None:
+        os.write(result_fd, (json.dumps(line) + "\n").encode())
+    os.close(result_fd)
+    return 0
+
+
+def _main() -> dict | None:
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        line = run_reference(args, rank)
-        if line is not None:
-            print(json.dumps(line), flush=True)
-        return 0
+        return run_reference(args, rank)
     if world > 1:
         import datetime
 
@@ -529,14 +556,11 @@ def main() -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
-    if line is not None:
-        print(json.dumps(line), flush=True)
-    return 0
 
 
 if __name__ == "__main__":

@@ -8,12 +8,16 @@
 //      stable permute -> rows for rank p are contiguous in x_permuted;
 //   2. ncclAllGather of the E counts; one pinned read of the G x E counts
 //      (the only host synchronisation) gives every rank its NCCL sizes;
-//   3. dispatch: grouped ncclSend/ncclRecv of x_permuted row blocks;
-//   4. grouped GEMM over the received rows, one group per (source rank,
-//      local expert), weight set = group % L;
-//   5. combine: the reverse send/recv returns each y row to the position its
-//      x row came from in x_permuted;
-//   6. local unpermute.
+//   3. the rows this rank routed to its own experts go straight into the
+//      grouped GEMM (x_permuted -> y_permuted, no copy);
+//   4. the other G-1 blocks move in G-1 pairwise rounds on a communication
+//      stream (round i: send to rank+i, receive from rank-i); the grouped GEMM
+//      of a received block (one group per local expert, weight set = local
+//      expert) starts as soon as its round lands, so transfers overlap the
+//      GEMM of earlier blocks;
+//   5. combine: after a block's GEMM its y rows go back in the matching
+//      reverse round, landing where the x rows came from in x_permuted;
+//   6. local unpermute once every combine round has landed.
 // The communicator is non-blocking; every host wait on NCCL or the stream has
 // a deadline, after which the communicator is aborted and RR_COMM_ERROR is
 // returned, so a lost peer cannot hang the caller forever. Plan-time
@@ -48,6 +52,11 @@ struct rr_ep {
   int32_t* count_all = nullptr;
   int32_t* recv_offsets = nullptr;
   int32_t* h_count_all = nullptr;  // pinned
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t local_ready = nullptr;
+  cudaEvent_t combine_done = nullptr;
+  std::vector<cudaEvent_t> dispatched;  // per round
+  std::vector<cudaEvent_t> computed;    // per round
   bool broken = false;
   long long last_sent = 0;
   long long last_received = 0;
@@ -133,6 +142,11 @@ void free_ep(rr_ep* ep) {
   cudaFree(ep->count_all);
   cudaFree(ep->recv_offsets);
   cudaFreeHost(ep->h_count_all);
+  for (cudaEvent_t ev : ep->dispatched) cudaEventDestroy(ev);
+  for (cudaEvent_t ev : ep->computed) cudaEventDestroy(ev);
+  if (ep->local_ready != nullptr) cudaEventDestroy(ep->local_ready);
+  if (ep->combine_done != nullptr) cudaEventDestroy(ep->combine_done);
+  if (ep->comm_stream != nullptr) cudaStreamDestroy(ep->comm_stream);
   if (ep->comm != nullptr) ncclCommDestroy(ep->comm);
   delete ep;
 }
@@ -214,6 +228,16 @@ rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int experts,
   if (e == cudaSuccess) e = cudaMalloc(&ep->count_all, sizeof(int32_t) * nranks * experts);
   if (e == cudaSuccess) e = cudaMalloc(&ep->recv_offsets, sizeof(int32_t) * (experts + 1));
   if (e == cudaSuccess) e = cudaMallocHost(&ep->h_count_all, sizeof(int32_t) * nranks * experts);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ep->comm_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->local_ready, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->combine_done, cudaEventDisableTiming);
+  for (int i = 0; e == cudaSuccess && i < nranks; ++i) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    e = cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
+    ep->dispatched.push_back(a);
+    ep->computed.push_back(b);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
     free_ep(ep);
@@ -304,66 +328,84 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     return e == cudaSuccess ? ok() : st(RR_CUDA_ERROR, "EP launch failed", e);
   }
 
-  // 2. Counts exchange and the step's exchange plan.
-  rr_status s = check_nccl(ep, ncclAllGather(counts, ep->count_all, E, ncclInt32, ep->comm,
-                                             stream),
+  // 2. Counts exchange and the step's exchange plan (all NCCL work runs on
+  //    the communication stream, in the same order on every rank).
+  cudaStream_t cs = ep->comm_stream;
+  e = cudaEventRecord(ep->local_ready, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ep->local_ready, 0);
+  if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP stream ordering failed", e);
+  rr_status s = check_nccl(ep, ncclAllGather(counts, ep->count_all, E, ncclInt32, ep->comm, cs),
                            "ncclAllGather of expert counts failed");
   if (s.code != RR_SUCCESS) return s;
   e = cudaMemcpyAsync(ep->h_count_all, ep->count_all, sizeof(int32_t) * G * E,
-                      cudaMemcpyDeviceToHost, stream);
+                      cudaMemcpyDeviceToHost, cs);
   if (e != cudaSuccess) return st(RR_CUDA_ERROR, "counts read-back failed", e);
-  s = wait_stream(ep, stream);
+  s = wait_stream(ep, cs);
   if (s.code != RR_SUCCESS) return s;
   std::vector<int64_t> send_rows(G), send_off(G), recv_rows(G), recv_off(G);
   s = rr_ep_plan(ep->h_count_all, G, ep->rank, E, send_rows.data(), send_off.data(),
                  recv_rows.data(), recv_off.data());
   if (s.code != RR_SUCCESS) return s;
-  const int64_t total_recv = recv_off[G - 1] + recv_rows[G - 1];
-  // Capacity is the worst case (every rank routes everything here), so every
-  // rank always takes the same collective steps.
   ep->last_sent = send_off[G - 1] + send_rows[G - 1];
-  ep->last_received = total_recv;
+  ep->last_received = recv_off[G - 1] + recv_rows[G - 1];
   e = rrb::launch_ep_recv_offsets(ep->count_all, ep->recv_offsets, G, E, ep->rank, ep->local,
                                   stream);
   if (e != cudaSuccess) return st(RR_CUDA_ERROR, "receive offsets launch failed", e);
 
-  // 3. Dispatch.
-  ncclGroupStart();
-  for (int p = 0; p < G; ++p) {
-    if (send_rows[p] > 0) {
-      ncclSend(x_permuted + send_off[p] * K, static_cast<size_t>(send_rows[p]) * K, ncclFloat, p,
-               ep->comm, stream);
-    }
-    if (recv_rows[p] > 0) {
-      ncclRecv(ep->recv_x + recv_off[p] * K, static_cast<size_t>(recv_rows[p]) * K, ncclFloat, p,
-               ep->comm, stream);
-    }
-  }
-  s = check_nccl(ep, ncclGroupEnd(), "NCCL dispatch failed");
-  if (s.code != RR_SUCCESS) return s;
-
-  // 4. Grouped GEMM over (source rank, local expert) groups.
-  if (total_recv > 0) {
-    e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets, ep->recv_y,
-                                 G * ep->local, static_cast<int>(total_recv), K, N, stream,
-                                 ep->local);
+  const int g = ep->rank;
+  const int L = ep->local;
+  // 3. This rank's own block: no transfer.
+  if (send_rows[g] > 0) {
+    e = rrb::launch_grouped_gemm(x_permuted, local_expert_weights, offsets + g * L, y_permuted, L,
+                                 routes, K, N, stream, L);
     if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP grouped GEMM launch failed", e);
   }
-
-  // 5. Combine (the reverse exchange).
-  ncclGroupStart();
-  for (int p = 0; p < G; ++p) {
-    if (recv_rows[p] > 0) {
-      ncclSend(ep->recv_y + recv_off[p] * N, static_cast<size_t>(recv_rows[p]) * N, ncclFloat, p,
-               ep->comm, stream);
+  // 4. Dispatch rounds; each received block's GEMM waits for its round.
+  for (int i = 1; i < G; ++i) {
+    const int dst = (g + i) % G;
+    const int src = (g - i + G) % G;
+    ncclGroupStart();
+    if (send_rows[dst] > 0) {
+      ncclSend(x_permuted + send_off[dst] * K, static_cast<size_t>(send_rows[dst]) * K, ncclFloat,
+               dst, ep->comm, cs);
     }
-    if (send_rows[p] > 0) {
-      ncclRecv(y_permuted + send_off[p] * N, static_cast<size_t>(send_rows[p]) * N, ncclFloat, p,
-               ep->comm, stream);
+    if (recv_rows[src] > 0) {
+      ncclRecv(ep->recv_x + recv_off[src] * K, static_cast<size_t>(recv_rows[src]) * K, ncclFloat,
+               src, ep->comm, cs);
     }
+    s = check_nccl(ep, ncclGroupEnd(), "NCCL dispatch failed");
+    if (s.code != RR_SUCCESS) return s;
+    e = cudaEventRecord(ep->dispatched[i], cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ep->dispatched[i], 0);
+    if (e == cudaSuccess && recv_rows[src] > 0) {
+      e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets + src * L,
+                                   ep->recv_y, L, static_cast<int>(ep->last_received), K, N,
+                                   stream, L);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(ep->computed[i], stream);
+    if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP dispatch/GEMM ordering failed", e);
   }
-  s = check_nccl(ep, ncclGroupEnd(), "NCCL combine failed");
-  if (s.code != RR_SUCCESS) return s;
+  // 5. Combine rounds: block i returns to its source as soon as its GEMM ends.
+  for (int i = 1; i < G; ++i) {
+    const int dst = (g + i) % G;
+    const int src = (g - i + G) % G;
+    e = cudaStreamWaitEvent(cs, ep->computed[i], 0);
+    if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP combine ordering failed", e);
+    ncclGroupStart();
+    if (recv_rows[src] > 0) {
+      ncclSend(ep->recv_y + recv_off[src] * N, static_cast<size_t>(recv_rows[src]) * N, ncclFloat,
+               src, ep->comm, cs);
+    }
+    if (send_rows[dst] > 0) {
+      ncclRecv(y_permuted + send_off[dst] * N, static_cast<size_t>(send_rows[dst]) * N, ncclFloat,
+               dst, ep->comm, cs);
+    }
+    s = check_nccl(ep, ncclGroupEnd(), "NCCL combine failed");
+    if (s.code != RR_SUCCESS) return s;
+  }
+  e = cudaEventRecord(ep->combine_done, cs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ep->combine_done, 0);
+  if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP combine ordering failed", e);
 
   // 6. Local unpermute.
   if (tokens > 0) {
