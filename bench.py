@@ -205,26 +205,31 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     ctx = rr.Context(stream=stream.cuda_stream)
     ep = None
     ep_info = None
+    ep_buf = None
     if world > 1:
-        # Expert parallelism: LPT placement on the expected (bias-driven)
-        # load, experts relabelled so each rank's are contiguous.
+        # Expert parallelism with hot-expert replication: per-expert loads are
+        # measured by routing this rank's batch (single-GPU stages), summed
+        # over ranks, and turned into virtual experts placed by LPT.
         from raggedroute_b200.ep import ExpertParallel
-        from raggedroute_b200.placement import (expected_loads_from_bias, imbalance,
-                                                lpt_placement, relabel_permutation)
-        bias_np = inp.logit_bias.cpu().numpy()
-        loads = expected_loads_from_bias(bias_np)
-        rank_of = lpt_placement(loads, world)
-        perm = torch.from_numpy(relabel_permutation(rank_of)).to(device)
-        inp.router_w = inp.router_w[:, perm].contiguous()
-        inp.logit_bias = inp.logit_bias[perm].contiguous()
-        inp.expert_w = inp.expert_w[perm].contiguous()
-        local = e // world
-        local_w = inp.expert_w[rank * local:(rank + 1) * local].contiguous()
-        ep = ExpertParallel(e, tokens, k, n, timeout_s=300.0)
-        contiguous = np.repeat(np.arange(world), local)
-        ep_info = {"placement": "lpt+relabel", "experts_per_rank": local,
-                   "expected_imbalance": round(imbalance(loads, rank_of, world), 4),
-                   "contiguous_imbalance": round(imbalance(loads, contiguous, world), 4)}
+        from raggedroute_b200.placement import ReplicatedPlacement
+        rr.dense_gemm(inp.x, inp.router_w, buf.logits, tokens, e, k)
+        rr.topk_gate_biased(buf.logits, inp.logit_bias, buf.expert_ids, buf.route_weights,
+                            tokens, e)
+        rr.histogram(buf.expert_ids, buf.counts, routes, e)
+        loads = buf.counts.to(torch.float64)
+        dist.all_reduce(loads)
+        pl = ReplicatedPlacement(loads.cpu().numpy(), world)
+        v_experts = pl.virtual_experts
+        local = v_experts // world
+        v2r = torch.from_numpy(pl.virtual_to_real[rank * local:(rank + 1) * local]).to(device)
+        local_w = inp.expert_w[v2r].contiguous()
+        remap = torch.from_numpy(pl.remap[rank]).to(device)
+        ep = ExpertParallel(v_experts, tokens, k, n, timeout_s=300.0, router_experts=e)
+        ep_buf = rr.ChainBuffers.allocate(tokens, k, v_experts, n, device, router_experts=e)
+        ep_info = {"placement": "replicated hot experts + LPT", "virtual_experts": v_experts,
+                   "virtual_experts_per_rank": local,
+                   "replicas_of_hottest": [int(r) for r in sorted(pl.replicas)[::-1][:4]],
+                   "expected_imbalance": round(pl.imbalance(), 4)}
     torch.cuda.synchronize()
 
     stage_names = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
@@ -261,8 +266,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
 
     def ep_step():
-        ep.chain_from_tokens(inp.x, inp.router_w, local_w, buf, logit_bias=inp.logit_bias,
-                             ctx=ctx)
+        ep.chain_from_tokens(inp.x, inp.router_w, local_w, ep_buf, logit_bias=inp.logit_bias,
+                             expert_remap=remap, ctx=ctx)
 
     if ep is not None:
         # Per-stage kernel times of this GPU's workload come from an untimed
@@ -332,9 +337,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 rr.chain_from_tokens(x_dev, inp.router_w, inp.expert_w, buf,
                                      logit_bias=inp.logit_bias, ctx=ctx)
             else:
-                ep.chain_from_tokens(x_dev, inp.router_w, local_w, buf,
-                                     logit_bias=inp.logit_bias, ctx=ctx)
-            y_host.copy_(buf.y, non_blocking=True)
+                ep.chain_from_tokens(x_dev, inp.router_w, local_w, ep_buf,
+                                     logit_bias=inp.logit_bias, expert_remap=remap, ctx=ctx)
+            y_host.copy_((buf if ep is None else ep_buf).y, non_blocking=True)
 
         with torch.cuda.stream(stream):
             for _ in range(max(1, args.warmup)):

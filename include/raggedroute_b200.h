@@ -182,12 +182,15 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
 size_t rr_chain_workspace_size(int tokens, int hidden, int experts, int output);
 
 /* ---- expert parallelism (new: the reference is single-GPU) ----------------
- * One process per GPU. Rank g owns experts [g*E/G, (g+1)*E/G). A step runs
- * the local routing stages, all-gathers the per-expert counts (one pinned
- * host read per step sizes the exchange), dispatches x_permuted rows with
- * NCCL send/recv, runs the grouped GEMM on received rows, combines back and
- * unpermutes, all on ctx->stream. Every host wait has a deadline; on expiry
- * the communicator is aborted and RR_COMM_ERROR returned. */
+ * One process per GPU. The router scores R real experts; the gate maps each
+ * selected id through a per-rank remap table to one of V virtual experts
+ * (a real expert's weights on one rank; hot experts get several), and rank
+ * g owns virtual experts [g*V/G, (g+1)*V/G). A step runs the local routing
+ * stages, all-gathers the per-virtual-expert counts (one pinned host read per
+ * step sizes the exchange), dispatches x_permuted rows with NCCL send/recv in
+ * pairwise rounds overlapped with the grouped GEMM of arrived blocks, combines
+ * back and unpermutes, all ordered on ctx->stream. Every host wait has a
+ * deadline; on expiry the communicator is aborted and RR_COMM_ERROR returned. */
 #define RR_EP_UNIQUE_ID_BYTES 128
 typedef struct rr_ep rr_ep;
 
@@ -195,15 +198,19 @@ typedef struct rr_ep rr_ep;
 rr_status rr_ep_get_unique_id(void* unique_id /* RR_EP_UNIQUE_ID_BYTES, host */);
 /* Plan-time: NCCL communicator (non-blocking) and worst-case receive buffers
  * (nranks * 2 * max_tokens rows). experts must be a multiple of nranks. */
-rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int experts, int max_tokens,
-                       int hidden, int output, double timeout_seconds, rr_ep** out);
+rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int router_experts,
+                       int experts, int max_tokens, int hidden, int output,
+                       double timeout_seconds, rr_ep** out);
 rr_status rr_ep_destroy(rr_ep* ep);
-/* chain_from_tokens across ranks: x [tokens, K] and the replicated router
- * weights / bias on every rank; local_expert_weights [E/G, K, N] are this
- * rank's experts; the other buffers are as for rr_chain_from_tokens and
- * ctx->workspace holds rr_chain_workspace_size(tokens, K, E, N) bytes. */
+/* chain_from_tokens across ranks: x [tokens, K]; router weights [K, R] and
+ * bias [R] (optional) replicated on every rank; expert_remap [R] (device;
+ * NULL only when R == V) maps this rank's routes to virtual experts;
+ * local_expert_weights [V/G, K, N] are this rank's virtual experts. logits is
+ * [tokens, R]; expert_ids receive virtual ids; counts/offsets are over V;
+ * ctx->workspace holds rr_chain_workspace_size(tokens, K, V, N) bytes. */
 rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router_weights,
-                                  const float* logit_bias, const float* local_expert_weights,
+                                  const float* logit_bias, const int32_t* expert_remap,
+                                  const float* local_expert_weights,
                                   float* logits, int32_t* expert_ids, float* route_weights,
                                   int32_t* counts, int32_t* offsets, float* x_permuted,
                                   int32_t* route_pos, float* y_permuted, float* y, int tokens,

@@ -43,9 +43,11 @@ inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b -
 
 // ---- launchers (implemented in the .cu files) -------------------------------
 
-// topk_gate.cu
+// topk_gate.cu. remap (optional, [experts]) replaces each selected id by
+// remap[id] on output (the expert-parallel runtime's virtual expert ids).
 cudaError_t launch_topk_gate(const float* logits, const float* bias, int32_t* ids, float* weights,
-                             int tokens, int experts, cudaStream_t stream);
+                             int tokens, int experts, cudaStream_t stream,
+                             const int32_t* remap = nullptr);
 
 // routing.cu
 cudaError_t launch_histogram_accumulate(const int32_t* ids, int32_t* counts, int routes,

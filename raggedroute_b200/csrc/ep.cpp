@@ -1,9 +1,13 @@
 // Expert-parallel chain_from_tokens over NCCL (one process per GPU).
 //
-// The reference is single-GPU. Here the chain shards by expert: rank g owns
-// the contiguous expert range [g*L, (g+1)*L), L = experts / nranks (a caller
-// balances load by relabelling experts before building the weights; see
-// raggedroute_b200/placement.py). Per step, on the caller's stream:
+// The reference is single-GPU. Here the chain shards by expert. The router
+// scores R real experts; the gate rewrites each selected real id through a
+// per-rank remap table into one of V "virtual" experts, and rank g owns the
+// contiguous virtual range [g*L, (g+1)*L), L = V / nranks. A virtual expert
+// is a real expert's weights placed on one rank; a hot expert gets several
+// virtual copies on different ranks and each source rank's remap sends its
+// tokens to one of them (raggedroute_b200/placement.py builds the tables).
+// Per step, on the caller's stream:
 //   1. local: router GEMM, biased top-2 gate, histogram+scan over all E,
 //      stable permute -> rows for rank p are contiguous in x_permuted;
 //   2. ncclAllGather of the E counts; one pinned read of the G x E counts
@@ -40,7 +44,8 @@ struct rr_ep {
   ncclComm_t comm = nullptr;
   int nranks = 1;
   int rank = 0;
-  int experts = 0;
+  int experts = 0;         // virtual experts (routing metadata, exchange)
+  int router_experts = 0;  // real experts scored by the router
   int local = 0;
   int max_tokens = 0;
   int hidden = 0;
@@ -196,15 +201,16 @@ rr_status rr_ep_plan(const int32_t* count_all, int nranks, int rank, int experts
   return ok();
 }
 
-rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int experts, int max_tokens,
-                       int hidden, int output, double timeout_seconds, rr_ep** out) {
+rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int router_experts,
+                       int experts, int max_tokens, int hidden, int output,
+                       double timeout_seconds, rr_ep** out) {
   if (out == nullptr) return st(RR_INVALID_ARGUMENT, "out must not be null");
   *out = nullptr;
   if (nranks < 1 || rank < 0 || rank >= nranks || experts < 2 || experts > RR_MAX_EXPERTS ||
-      experts % nranks != 0 || max_tokens <= 0 || hidden <= 0 || output <= 0 ||
-      max_tokens > (1 << 30) / 2) {
+      experts % nranks != 0 || router_experts < 2 || router_experts > RR_MAX_EXPERTS ||
+      max_tokens <= 0 || hidden <= 0 || output <= 0 || max_tokens > (1 << 30) / 2) {
     return st(RR_INVALID_ARGUMENT,
-              "rr_ep_create requires nranks | experts <= 1024 and positive sizes");
+              "rr_ep_create requires nranks | virtual experts <= 1024 and positive sizes");
   }
   if (nranks > 1 && unique_id == nullptr) {
     return st(RR_INVALID_ARGUMENT, "unique_id must not be null for nranks > 1");
@@ -214,6 +220,7 @@ rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int experts,
   ep->nranks = nranks;
   ep->rank = rank;
   ep->experts = experts;
+  ep->router_experts = router_experts;
   ep->local = experts / nranks;
   ep->max_tokens = max_tokens;
   ep->hidden = hidden;
@@ -276,7 +283,8 @@ rr_status rr_ep_last_step_rows(const rr_ep* ep, int64_t* rows_sent, int64_t* row
 }
 
 rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router_weights,
-                                  const float* logit_bias, const float* local_expert_weights,
+                                  const float* logit_bias, const int32_t* expert_remap,
+                                  const float* local_expert_weights,
                                   float* logits, int32_t* expert_ids, float* route_weights,
                                   int32_t* counts, int32_t* offsets, float* x_permuted,
                                   int32_t* route_pos, float* y_permuted, float* y, int tokens,
@@ -287,6 +295,10 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     return st(RR_INVALID_ARGUMENT, "tokens must be in [0, max_tokens] of the EP plan");
   }
   const int E = ep->experts, K = ep->hidden, N = ep->output, G = ep->nranks;
+  const int RE = ep->router_experts;
+  if (expert_remap == nullptr && RE != E) {
+    return st(RR_INVALID_ARGUMENT, "an expert remap is required when virtual != router experts");
+  }
   if (x == nullptr || router_weights == nullptr || local_expert_weights == nullptr ||
       logits == nullptr || expert_ids == nullptr || route_weights == nullptr ||
       counts == nullptr || offsets == nullptr || x_permuted == nullptr || route_pos == nullptr ||
@@ -302,9 +314,10 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
   // 1. Local stages (identical to the single-GPU chain).
   cudaError_t e = cudaSuccess;
   if (tokens > 0) {
-    e = rrb::launch_grouped_gemm(x, router_weights, nullptr, logits, 1, tokens, K, E, stream);
+    e = rrb::launch_grouped_gemm(x, router_weights, nullptr, logits, 1, tokens, K, RE, stream);
     if (e == cudaSuccess) {
-      e = rrb::launch_topk_gate(logits, logit_bias, expert_ids, route_weights, tokens, E, stream);
+      e = rrb::launch_topk_gate(logits, logit_bias, expert_ids, route_weights, tokens, RE, stream,
+                                expert_remap);
     }
   }
   if (e == cudaSuccess) {

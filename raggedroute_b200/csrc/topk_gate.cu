@@ -15,7 +15,8 @@
 // first (they compare equal in float), NaN becomes -inf, and the id half
 // breaks ties toward the lower id. Each lane keeps its local top-2 keys; the
 // group merges them with xor shuffles. The kernel is HBM-bound: 4*E bytes in
-// and 16 bytes out per row.
+// and 16 bytes out per row. An optional remap table rewrites each selected id
+// on output (the expert-parallel runtime's replicated "virtual" experts).
 #include "common.cuh"
 
 namespace rrb {
@@ -55,7 +56,8 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
                                                         const float* __restrict__ bias,
                                                         int32_t* __restrict__ ids,
                                                         float* __restrict__ weights, int tokens,
-                                                        int experts, bool pair_stores) {
+                                                        int experts, bool pair_stores,
+                                                        const int32_t* __restrict__ remap) {
   constexpr int kRowsPerWarp = 32 / L;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -133,6 +135,10 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
       w1 = rel * w0;
     }
   }
+  if (remap != nullptr) {
+    id0 = __ldg(remap + id0);
+    id1 = __ldg(remap + id1);
+  }
   if (pair_stores) {
     reinterpret_cast<int2*>(ids)[row] = make_int2(id0, id1);
     reinterpret_cast<float2*>(weights)[row] = make_float2(w0, w1);
@@ -146,44 +152,46 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
 
 template <int L, bool kVec>
 cudaError_t launch_l(const float* logits, const float* bias, int32_t* ids, float* weights,
-                     int tokens, int experts, bool pair, cudaStream_t stream) {
+                     int tokens, int experts, bool pair, const int32_t* remap,
+                     cudaStream_t stream) {
   constexpr int kThreads = 256;
   constexpr int kRowsPerBlock = (kThreads / 32) * (32 / L);
   const int blocks = ceil_div(tokens, kRowsPerBlock);
   topk_gate_kernel<L, kVec><<<blocks, kThreads, 0, stream>>>(logits, bias, ids, weights, tokens,
-                                                             experts, pair);
+                                                             experts, pair, remap);
   note_launch();
   return cudaGetLastError();
 }
 
 template <bool kVec>
 cudaError_t launch_vec(const float* logits, const float* bias, int32_t* ids, float* weights,
-                       int tokens, int experts, bool pair, cudaStream_t stream) {
+                       int tokens, int experts, bool pair, const int32_t* remap,
+                       cudaStream_t stream) {
   // About two loads (8 candidates with 128-bit loads) per lane.
   const int items = kVec ? (experts >> 2) : experts;
   int want = (items + (kVec ? 1 : 3)) / (kVec ? 2 : 4);
   int l = 1;
   while (l < want && l < 32) l <<= 1;
   switch (l) {
-    case 1: return launch_l<1, kVec>(logits, bias, ids, weights, tokens, experts, pair, stream);
-    case 2: return launch_l<2, kVec>(logits, bias, ids, weights, tokens, experts, pair, stream);
-    case 4: return launch_l<4, kVec>(logits, bias, ids, weights, tokens, experts, pair, stream);
-    case 8: return launch_l<8, kVec>(logits, bias, ids, weights, tokens, experts, pair, stream);
-    case 16: return launch_l<16, kVec>(logits, bias, ids, weights, tokens, experts, pair, stream);
-    default: return launch_l<32, kVec>(logits, bias, ids, weights, tokens, experts, pair, stream);
+    case 1: return launch_l<1, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 2: return launch_l<2, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 4: return launch_l<4, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 8: return launch_l<8, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 16: return launch_l<16, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    default: return launch_l<32, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_topk_gate(const float* logits, const float* bias, int32_t* ids, float* weights,
-                             int tokens, int experts, cudaStream_t stream) {
+                             int tokens, int experts, cudaStream_t stream, const int32_t* remap) {
   if (tokens <= 0) return cudaSuccess;
   const bool vec = (experts % 4 == 0) && aligned_to(logits, 16) &&
                    (bias == nullptr || aligned_to(bias, 16));
   const bool pair = aligned_to(ids, 8) && aligned_to(weights, 8);
-  return vec ? launch_vec<true>(logits, bias, ids, weights, tokens, experts, pair, stream)
-             : launch_vec<false>(logits, bias, ids, weights, tokens, experts, pair, stream);
+  return vec ? launch_vec<true>(logits, bias, ids, weights, tokens, experts, pair, remap, stream)
+             : launch_vec<false>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
 }
 
 }  // namespace rrb

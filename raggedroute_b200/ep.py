@@ -18,12 +18,17 @@ UNIQUE_ID_BYTES = 128
 
 
 class ExpertParallel:
+    """`experts` virtual experts (V) are split evenly over the ranks; the
+    router scores `router_experts` real experts (R, default V) and
+    chain_from_tokens takes this rank's remap table R -> V when they differ."""
+
     def __init__(self, experts: int, max_tokens: int, hidden: int, output: int,
                  rank: int | None = None, world: int | None = None, group=None,
-                 timeout_s: float = 120.0):
+                 timeout_s: float = 120.0, router_experts: int | None = None):
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
         self.experts, self.hidden, self.output = experts, hidden, output
+        self.router_experts = experts if router_experts is None else router_experts
         self.local = experts // self.world
         uid = torch.zeros(UNIQUE_ID_BYTES, dtype=torch.uint8)
         if self.world > 1:
@@ -38,17 +43,20 @@ class ExpertParallel:
         raw = (ctypes.c_uint8 * UNIQUE_ID_BYTES)(*uid.tolist())
         handle = ctypes.c_void_p()
         check(lib().rr_ep_create(ctypes.cast(raw, ctypes.c_void_p), self.world, self.rank,
-                                 experts, max_tokens, hidden, output, timeout_s,
-                                 ctypes.byref(handle)), "rr_ep_create")
+                                 self.router_experts, experts, max_tokens, hidden, output,
+                                 timeout_s, ctypes.byref(handle)), "rr_ep_create")
         self._h = handle
 
     def chain_from_tokens(self, x: torch.Tensor, router_weights: torch.Tensor,
                           local_expert_weights: torch.Tensor, buf: ChainBuffers,
                           logit_bias: torch.Tensor | None = None,
+                          expert_remap: torch.Tensor | None = None,
                           ctx: Context | None = None) -> torch.Tensor:
+        """buf must be allocated for V virtual experts with logits [T, R]."""
         tokens = x.shape[0]
         check(lib().rr_ep_chain_from_tokens(
-            self._h, _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(local_expert_weights),
+            self._h, _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(expert_remap),
+            _ptr(local_expert_weights),
             _ptr(buf.logits), _ptr(buf.expert_ids), _ptr(buf.route_weights), _ptr(buf.counts),
             _ptr(buf.offsets), _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.y_permuted),
             _ptr(buf.y), tokens, _ctx(ctx, buf.workspace)), "rr_ep_chain_from_tokens")

@@ -164,11 +164,15 @@ class ChainBuffers:
 
     @staticmethod
     def allocate(tokens: int, hidden: int, experts: int, output: int,
-                 device: torch.device | str = "cuda", with_logits: bool = True) -> "ChainBuffers":
+                 device: torch.device | str = "cuda", with_logits: bool = True,
+                 router_experts: int | None = None) -> "ChainBuffers":
+        """`experts` sizes the routing metadata; logits are [tokens,
+        router_experts] (default: experts; differs for replicated EP)."""
         f32, i32 = torch.float32, torch.int32
         ws = max(1, chain_workspace_size(tokens, hidden, experts, output))
+        re = experts if router_experts is None else router_experts
         return ChainBuffers(
-            logits=torch.empty(tokens, experts, dtype=f32, device=device) if with_logits else None,
+            logits=torch.empty(tokens, re, dtype=f32, device=device) if with_logits else None,
             expert_ids=torch.empty(tokens, 2, dtype=i32, device=device),
             route_weights=torch.empty(tokens, 2, dtype=f32, device=device),
             counts=torch.empty(experts, dtype=i32, device=device),

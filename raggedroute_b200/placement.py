@@ -54,3 +54,75 @@ def imbalance(loads, rank_of, nranks: int) -> float:
     loads = np.asarray(loads, dtype=np.float64)
     per_rank = np.bincount(np.asarray(rank_of), weights=loads, minlength=nranks)
     return float(per_rank.max() / per_rank.mean())
+
+
+class ReplicatedPlacement:
+    """Virtual-expert placement for the EP runtime.
+
+    Every real expert e gets r_e = clamp(ceil(load_e / fair_share), 1, G)
+    replicas ("virtual experts"); replica j serves the source ranks s with
+    (s * r_e) // G == j, so a hot expert's tokens are split by source rank.
+    Virtual experts are placed by LPT under the runtime's constraint that every
+    rank owns the same number of them (zero-load padding entries fill up), with
+    replicas of one expert kept on distinct ranks when possible, and then
+    numbered rank by rank so each rank's virtual ids are contiguous.
+
+    Attributes: virtual_experts (V, a multiple of nranks), virtual_to_real [V]
+    (padding entries point at real expert 0 and are never routed to),
+    remap [nranks, R] (real id -> virtual id for routes from source rank s),
+    rank_load [nranks] (expected load per rank).
+    """
+
+    def __init__(self, loads, nranks: int, max_virtual: int = 1024):
+        loads = np.asarray(loads, dtype=np.float64)
+        r_experts = loads.size
+        total = float(loads.sum())
+        fair = total / nranks if total > 0 else 1.0
+        reps = np.clip(np.ceil(loads / fair - 1e-9), 1, nranks).astype(np.int64)
+        items = []  # (load, real expert, replica index)
+        for e in range(r_experts):
+            r = int(reps[e])
+            for j in range(r):
+                n_src = sum(1 for s in range(nranks) if (s * r) // nranks == j)
+                items.append((loads[e] * n_src / nranks, e, j))
+        pad = (-len(items)) % nranks
+        items += [(0.0, -1, 0)] * pad
+        v_count = len(items)
+        if v_count > max_virtual:
+            raise ValueError("too many virtual experts")
+        per = v_count // nranks
+        rank_load = np.zeros(nranks)
+        slots = np.full(nranks, per)
+        hosts: dict[int, set] = {}
+        rank_of_item = np.empty(v_count, dtype=np.int64)
+        for i in sorted(range(v_count), key=lambda i: -items[i][0]):
+            load, e, _ = items[i]
+            free = [r for r in range(nranks) if slots[r] > 0]
+            avoid = hosts.get(e, set()) if e >= 0 else set()
+            pool = [r for r in free if r not in avoid] or free
+            r = min(pool, key=lambda q: rank_load[q])
+            rank_of_item[i] = r
+            rank_load[r] += load
+            slots[r] -= 1
+            if e >= 0:
+                hosts.setdefault(e, set()).add(r)
+        order = sorted(range(v_count), key=lambda i: (rank_of_item[i], i))
+        self.nranks = nranks
+        self.router_experts = r_experts
+        self.virtual_experts = v_count
+        self.replicas = reps
+        self.virtual_to_real = np.zeros(v_count, dtype=np.int64)
+        replica_vid = {}
+        for v, i in enumerate(order):
+            _, e, j = items[i]
+            self.virtual_to_real[v] = max(e, 0)
+            if e >= 0:
+                replica_vid[(e, j)] = v
+        self.remap = np.zeros((nranks, r_experts), dtype=np.int32)
+        for s in range(nranks):
+            for e in range(r_experts):
+                self.remap[s, e] = replica_vid[(e, (s * int(reps[e])) // nranks)]
+        self.rank_load = rank_load
+
+    def imbalance(self) -> float:
+        return float(self.rank_load.max() / self.rank_load.mean())

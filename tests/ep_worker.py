@@ -20,8 +20,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 def main() -> int:
     import raggedroute_b200 as rr
     from raggedroute_b200.ep import ExpertParallel
-    from raggedroute_b200.placement import (expected_loads_from_bias, lpt_placement,
-                                            relabel_permutation)
+    from raggedroute_b200.placement import ReplicatedPlacement
     from raggedroute_b200.workloads import normal, zipf_log_bias
 
     rank = int(os.environ["RANK"])
@@ -30,31 +29,42 @@ def main() -> int:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    t, k, e, n = int(os.environ.get("EP_T", "3000")), 256, 32, 96
+    t, k, e, n = int(os.environ.get("EP_T", "3000")), 256, 32, 96  # E % world == 0
     x = normal((t, k), 1.0, 1000 + rank, dev)
     wr = normal((k, e), 1 / 16, 7, dev)
     we = normal((e, k, n), 1 / 16, 8, dev)
-    bias_np = zipf_log_bias(e, 1.0)
-    perm = relabel_permutation(lpt_placement(expected_loads_from_bias(bias_np), world))
-    perm_t = torch.from_numpy(perm).to(dev)
-    wr = wr[:, perm_t].contiguous()
-    we = we[perm_t].contiguous()
-    bias = torch.from_numpy(bias_np[perm]).to(dev)
-    local = e // world
-    local_w = we[rank * local:(rank + 1) * local].contiguous()
-
-    ep = ExpertParallel(e, t, k, n)
-    b_ep = rr.ChainBuffers.allocate(t, k, e, n, dev)
+    bias = torch.from_numpy(zipf_log_bias(e, 1.0)).to(dev)
     b_ref = rr.ChainBuffers.allocate(t, k, e, n, dev)
+    # Loads from this batch's routing, summed over ranks -> replicated placement.
+    rr.chain_from_tokens(x, wr, we, b_ref, logit_bias=bias)
+    loads = b_ref.counts.to(torch.float64)
+    dist.all_reduce(loads)
+    pl = ReplicatedPlacement(loads.cpu().numpy(), world)
+    v = pl.virtual_experts
+    local = v // world
+    v2r_all = torch.from_numpy(pl.virtual_to_real).to(dev)
+    local_w = we[v2r_all[rank * local:(rank + 1) * local]].contiguous()
+    remap = torch.from_numpy(pl.remap[rank]).to(dev)
+    ep = ExpertParallel(v, t, k, n, router_experts=e)
+    b_ep = rr.ChainBuffers.allocate(t, k, v, n, dev, router_experts=e)
     ok = True
     for step in range(2):
-        ep.chain_from_tokens(x, wr, local_w, b_ep, logit_bias=bias)
+        ep.chain_from_tokens(x, wr, local_w, b_ep, logit_bias=bias, expert_remap=remap)
         rr.chain_from_tokens(x, wr, we, b_ref, logit_bias=bias)
         torch.cuda.synchronize()
-        for name in ("expert_ids", "counts", "offsets", "route_pos"):
-            if not torch.equal(getattr(b_ep, name), getattr(b_ref, name)):
-                print(f"rank {rank} step {step}: {name} differs", flush=True)
-                ok = False
+        # Virtual ids map back to the single-GPU chain's real ids; virtual
+        # counts sum to the real counts.
+        if not torch.equal(v2r_all[b_ep.expert_ids.long()].to(torch.int32), b_ref.expert_ids):
+            print(f"rank {rank} step {step}: expert ids differ", flush=True)
+            ok = False
+        real_counts = torch.zeros(e, dtype=torch.int64, device=dev)
+        real_counts.index_add_(0, v2r_all, b_ep.counts.to(torch.int64))
+        if not torch.equal(real_counts.to(torch.int32), b_ref.counts):
+            print(f"rank {rank} step {step}: counts differ", flush=True)
+            ok = False
+        if not torch.equal(b_ep.route_weights, b_ref.route_weights):
+            print(f"rank {rank} step {step}: route weights differ", flush=True)
+            ok = False
         if not torch.equal(b_ep.y.view(torch.int32), b_ref.y.view(torch.int32)):
             diff = (b_ep.y - b_ref.y).abs().max().item()
             print(f"rank {rank} step {step}: y differs (max {diff})", flush=True)

@@ -132,3 +132,28 @@ def test_ep_two_rank_gloo_matches_single_process(tmp_path, rrlib, oracle):
         ref = oracle.unpermute_f64(yp, pos, w)
         got = np.load(tmp_path / f"y{rank}.npy")
         np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6)
+
+
+def test_replicated_placement_splits_hot_experts():
+    from raggedroute_b200.placement import ReplicatedPlacement
+    rng = np.random.default_rng(0)
+    e = 128
+    from raggedroute_b200.workloads import zipf_log_bias
+    logits = rng.standard_normal((20000, e)) + zipf_log_bias(e, 1.0)[None, :]
+    loads = np.bincount(np.argsort(-logits, axis=1)[:, :2].reshape(-1), minlength=e)
+    for g in (1, 2, 4, 8):
+        pl = ReplicatedPlacement(loads, g)
+        v = pl.virtual_experts
+        assert v % g == 0 and v <= 1024
+        # Every source rank maps every real expert to a virtual copy of it.
+        for s in range(g):
+            assert np.array_equal(pl.virtual_to_real[pl.remap[s]], np.arange(e))
+        # Replicas of one expert sit on distinct ranks.
+        local = v // g
+        for r_e in np.flatnonzero(pl.replicas > 1):
+            vids = {int(pl.remap[s, r_e]) for s in range(g)}
+            assert len({vid // local for vid in vids}) == len(vids)
+        assert pl.imbalance() < 1.05, (g, pl.imbalance())
+    # Without skew nothing is replicated.
+    flat = ReplicatedPlacement(np.ones(64), 8)
+    assert flat.virtual_experts == 64 and flat.imbalance() == 1.0
