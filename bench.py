@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=None, help="override T per GPU (testing)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ep-transport", choices=["auto", "peer", "nccl"], default="auto",
+                    help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--stages", action="store_true", help="print the per-stage table to stderr")
     ap.add_argument("--only-stage", default=None,
                     choices=["dense_gemm", "topk_gate", "histogram_exclusive_scan",
@@ -224,9 +226,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         v2r = torch.from_numpy(pl.virtual_to_real[rank * local:(rank + 1) * local]).to(device)
         local_w = inp.expert_w[v2r].contiguous()
         remap = torch.from_numpy(pl.remap[rank]).to(device)
-        ep = ExpertParallel(v_experts, tokens, k, n, timeout_s=300.0, router_experts=e)
+        ep = ExpertParallel(v_experts, tokens, k, n, timeout_s=300.0, router_experts=e,
+                            transport=args.ep_transport)
         ep_buf = rr.ChainBuffers.allocate(tokens, k, v_experts, n, device, router_experts=e)
-        ep_info = {"placement": "replicated hot experts + LPT", "virtual_experts": v_experts,
+        ep_info = {"transport": ep.transport,
+                   "placement": "replicated hot experts + LPT", "virtual_experts": v_experts,
                    "virtual_experts_per_rank": local,
                    "replicas_of_hottest": [int(r) for r in sorted(pl.replicas)[::-1][:4]],
                    "expected_imbalance": round(pl.imbalance(), 4)}

@@ -185,23 +185,45 @@ size_t rr_chain_workspace_size(int tokens, int hidden, int experts, int output);
  * One process per GPU. The router scores R real experts; the gate maps each
  * selected id through a per-rank remap table to one of V virtual experts
  * (a real expert's weights on one rank; hot experts get several), and rank
- * g owns virtual experts [g*V/G, (g+1)*V/G). A step runs the local routing
- * stages, all-gathers the per-virtual-expert counts (one pinned host read per
- * step sizes the exchange), dispatches x_permuted rows with NCCL send/recv in
- * pairwise rounds overlapped with the grouped GEMM of arrived blocks, combines
- * back and unpermutes, all ordered on ctx->stream. Every host wait has a
- * deadline; on expiry the communicator is aborted and RR_COMM_ERROR returned. */
+ * g owns virtual experts [g*V/G, (g+1)*V/G). Two transports move the rows:
+ *
+ * RR_EP_TRANSPORT_PEER (one node, GPUs that map each other's memory): every
+ *   rank's receive buffers are mapped into every other rank at create time.
+ *   A step runs the local routing stages, all-gathers the per-virtual-expert
+ *   counts, and then the permute kernel writes each route's row straight into
+ *   its owner's receive buffer (dispatch fused into the permute), the owner's
+ *   grouped GEMM writes each output row straight back into the source rank's
+ *   buffer (combine fused into the GEMM epilogue), and the source
+ *   unpermutes. Two one-word NCCL all-reduces order the phases across ranks.
+ *   No host synchronisation inside a step; x_permuted and y_permuted are not
+ *   used (may be NULL).
+ * RR_EP_TRANSPORT_NCCL: x_permuted rows move with NCCL send/recv in pairwise
+ *   rounds overlapped with the grouped GEMM of arrived blocks and come back
+ *   the same way into y_permuted; one pinned host read of the counts per step
+ *   sizes the rounds.
+ * RR_EP_TRANSPORT_AUTO picks PEER when every rank can map every other rank's
+ * memory, else NCCL. All work is ordered on ctx->stream. Every host wait has
+ * a deadline; on expiry the communicator is aborted and RR_COMM_ERROR
+ * returned. */
 #define RR_EP_UNIQUE_ID_BYTES 128
+#define RR_EP_TRANSPORT_AUTO 0
+#define RR_EP_TRANSPORT_NCCL 1
+#define RR_EP_TRANSPORT_PEER 2
 typedef struct rr_ep rr_ep;
 
 /* Rank 0 creates the id; the caller distributes it to the other ranks. */
 rr_status rr_ep_get_unique_id(void* unique_id /* RR_EP_UNIQUE_ID_BYTES, host */);
-/* Plan-time: NCCL communicator (non-blocking) and worst-case receive buffers
- * (nranks * 2 * max_tokens rows). experts must be a multiple of nranks. */
+/* Plan-time: NCCL communicator (non-blocking), worst-case receive buffers
+ * (nranks * 2 * max_tokens rows, below 2^31) and, for the peer transport,
+ * the cross-rank mappings. experts must be a multiple of nranks. Collective:
+ * every rank calls it with the same sizes and transport. */
 rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int router_experts,
                        int experts, int max_tokens, int hidden, int output,
-                       double timeout_seconds, rr_ep** out);
+                       double timeout_seconds, int transport, rr_ep** out);
+/* Collective when nranks > 1 (a barrier precedes the unmapping). */
 rr_status rr_ep_destroy(rr_ep* ep);
+/* The transport the plan uses (RR_EP_TRANSPORT_NCCL or _PEER). */
+rr_status rr_ep_transport(const rr_ep* ep, int* transport);
 /* chain_from_tokens across ranks: x [tokens, K]; router weights [K, R] and
  * bias [R] (optional) replicated on every rank; expert_remap [R] (device;
  * NULL only when R == V) maps this rank's routes to virtual experts;
@@ -215,7 +237,8 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
                                   int32_t* counts, int32_t* offsets, float* x_permuted,
                                   int32_t* route_pos, float* y_permuted, float* y, int tokens,
                                   const rr_context* ctx);
-/* Rows this rank sent / received in its last step (load-balance reporting). */
+/* Rows this rank sent / received in its last step (load-balance reporting);
+ * waits, with the plan's deadline, for that step to finish on the device. */
 rr_status rr_ep_last_step_rows(const rr_ep* ep, int64_t* rows_sent, int64_t* rows_received);
 /* The exchange plan of one rank from the [nranks][experts] counts (pure host
  * arithmetic): rows sent to / received from each peer and block offsets. */

@@ -107,8 +107,9 @@ SIGNATURES = {
     "rr_grouped_gemm_engine": (_I, [_P, _P, _P, _I, _I]),
     "rr_version": (ctypes.c_char_p, []),
     "rr_ep_get_unique_id": (RRStatus, [_P]),
-    "rr_ep_create": (RRStatus, [_P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_double,
-                                ctypes.POINTER(ctypes.c_void_p)]),
+    "rr_ep_create": (RRStatus, [_P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_double, _I,
+                                 ctypes.POINTER(ctypes.c_void_p)]),
+    "rr_ep_transport": (RRStatus, [_P, ctypes.POINTER(ctypes.c_int)]),
     "rr_ep_destroy": (RRStatus, [_P]),
     "rr_ep_chain_from_tokens": (RRStatus, [_P] * 15 + [_I, _CTX]),
     "rr_ep_last_step_rows": (RRStatus, [_P, ctypes.POINTER(ctypes.c_int64),

@@ -19,6 +19,49 @@ constexpr int kNumSms = 148;  // B200; the launchers query the real count once.
 constexpr unsigned kErrMbarTimeout = 1u << 0;
 constexpr unsigned kErrTmemAlloc = 1u << 1;
 constexpr unsigned kErrScheduler = 1u << 2;
+constexpr unsigned kErrEpCapacity = 1u << 3;
+
+// Expert-parallel peer transport. A packed row address names a row of a
+// buffer that one rank owns: (rank << kPeerRankShift) | row.
+constexpr int kPeerRankShift = 40;
+constexpr long long kPeerRowMask = (1LL << kPeerRankShift) - 1;
+
+// Output-row redirection for a GEMM: output row r is written to
+// base[dst[r] >> 40] + (dst[r] & kPeerRowMask) * output. base is a device
+// array of one pointer per rank (this process's mapping of every rank's
+// buffer, its own included). An address whose rank is not below nranks or
+// whose row is not below row_limit is not stored.
+struct RowScatter {
+  const int64_t* dst = nullptr;
+  float* const* base = nullptr;
+  int nranks = 0;
+  long long row_limit = 0;
+};
+
+// Resolves a packed row address, or nullptr when it is out of range.
+__device__ __forceinline__ float* scatter_row(const RowScatter& sc, long long row, int output) {
+  const long long d = __ldg(sc.dst + row);
+  const long long rank = d >> kPeerRankShift;
+  const long long r = d & kPeerRowMask;
+  if (d < 0 || rank >= sc.nranks || r >= sc.row_limit) return nullptr;
+  return sc.base[rank] + r * output;
+}
+
+// Dispatch side of the peer transport, used by the token permute: a route to
+// virtual expert e (owner rank e / local) is copied to
+// x_base[owner] + (dest_off[e] + rank of the route inside e) * hidden, and
+// its return address (me << 40 | local permuted slot) goes to
+// ret_base[owner][same row]. Rows at or beyond `capacity` are dropped and
+// flagged (kErrEpCapacity).
+struct PeerDispatch {
+  float* const* x_base = nullptr;
+  int64_t* const* ret_base = nullptr;
+  const int32_t* dest_off = nullptr;
+  int local = 1;
+  int me = 0;
+  long long capacity = 0;
+  unsigned* err = nullptr;
+};
 
 // Counts every kernel this library launches (for the bench's launch claim).
 void note_launch(int n = 1);
@@ -63,6 +106,15 @@ cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
 // Expert-parallel receive offsets (nranks * local <= 1024 groups).
 cudaError_t launch_ep_recv_offsets(const int32_t* count_all, int32_t* recv_offsets, int nranks,
                                    int experts, int rank, int local, cudaStream_t stream);
+// Peer-transport layout from count_all [nranks][experts]: every rank's
+// receive buffer is expert-major (local expert, then source rank). Writes
+// dest_off[experts] (where this rank's rows of each expert start on its
+// owner) and recv_offsets[local + 1] (this rank's grouped-GEMM offsets,
+// clipped to capacity; an overflow sets kErrEpCapacity in err).
+cudaError_t launch_ep_peer_layout(const int32_t* count_all, int32_t* dest_off,
+                                  int32_t* recv_offsets, int nranks, int experts, int rank,
+                                  int local, long long capacity, unsigned* err,
+                                  cudaStream_t stream);
 
 // permute.cu
 std::size_t permute_workspace_bytes(int tokens, int experts, int top_k);
@@ -72,6 +124,12 @@ cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32
                                  float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
                                  int tokens, int experts, int top_k, int hidden, void* workspace,
                                  cudaStream_t stream);
+// The same permute (identical route_pos) whose copy goes to other ranks'
+// receive buffers through the peer mapping instead of to x_permuted.
+cudaError_t launch_token_permute_peer(const float* x, const int32_t* ids, const int32_t* offsets,
+                                      int32_t* route_pos, int tokens, int experts, int top_k,
+                                      int hidden, void* workspace, const PeerDispatch& peer,
+                                      cudaStream_t stream);
 // Workspace-free stable permute for the low-level launcher: the expert count
 // is unknown, cursors accumulate (caller zeroes them).
 cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,
@@ -91,17 +149,22 @@ cudaError_t launch_unpermute(const float* y_permuted, const int32_t* route_pos,
 // g multiplies by weight set (g % weight_sets) of w[weight_sets, hidden,
 // output]; weight_sets = 0 means one weight set per group. The
 // expert-parallel runtime uses weight_sets < experts for its
-// (source rank, local expert) groups.
+// (source rank, local expert) groups. scatter (optional) redirects every
+// stored output row (peer transport combine); y is then only an alignment
+// witness for the engine choice.
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets,
                                 float* y, int experts, int rows, int hidden, int output,
-                                cudaStream_t stream, int weight_sets = 0);
+                                cudaStream_t stream, int weight_sets = 0,
+                                const RowScatter* scatter = nullptr);
 cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,
-                                     cudaStream_t stream, int weight_sets = 0);
+                                     cudaStream_t stream, int weight_sets = 0,
+                                     const RowScatter* scatter = nullptr);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
-                                   cudaStream_t stream, int weight_sets = 0);
+                                   cudaStream_t stream, int weight_sets = 0,
+                                   const RowScatter* scatter = nullptr);
 
 // misc.cu
 cudaError_t launch_cache_scrub(uint32_t* buffer, std::size_t elements, cudaStream_t stream);

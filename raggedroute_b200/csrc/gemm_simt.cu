@@ -20,7 +20,8 @@ constexpr int kThreads = 256;
 
 __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const int32_t* __restrict__ offsets,
-    float* __restrict__ y, int experts, int rows, int hidden, int output, int wsets) {
+    float* __restrict__ y, int experts, int rows, int hidden, int output, int wsets,
+    const RowScatter scatter) {
   __shared__ int prefix[kMaxExperts + 1];
   __shared__ int scratch[33];
   __shared__ float as[kBK][kBM + 4];
@@ -75,20 +76,27 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
     for (int i = 0; i < 4; ++i) {
       const int r = tc.row0 + ty * 4 + i;
       if (r >= tc.row_end) continue;
+      float* out = y + static_cast<long long>(r) * output;
+      if (scatter.dst != nullptr) {
+        out = scatter_row(scatter, r, output);
+        if (out == nullptr) continue;
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = tc.col0 + tx * 4 + j;
-        if (c < output) y[static_cast<long long>(r) * output + c] = acc[i][j];
+        if (c < output) out[c] = acc[i][j];
       }
     }
   }
+  if (scatter.dst != nullptr) __threadfence_system();
 }
 
 }  // namespace
 
 cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,
-                                     cudaStream_t stream, int weight_sets) {
+                                     cudaStream_t stream, int weight_sets,
+                                     const RowScatter* scatter) {
   const int wsets = weight_sets > 0 ? weight_sets : experts;
   if (output <= 0) return cudaSuccess;
   int grid = 4 * sm_count();
@@ -99,7 +107,9 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
     if (tiles < grid) grid = static_cast<int>(tiles);
   }
   grouped_gemm_simt_kernel<<<grid, kThreads, 0, stream>>>(x, w, offsets, y, experts, rows, hidden,
-                                                          output, wsets);
+                                                          output, wsets,
+                                                          scatter != nullptr ? *scatter
+                                                                             : RowScatter{});
   note_launch();
   return cudaGetLastError();
 }

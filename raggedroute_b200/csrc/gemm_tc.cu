@@ -140,7 +140,7 @@ __device__ __forceinline__ int nmajor128_offset(int k, int n) {
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
     const int32_t* __restrict__ offsets, float* __restrict__ y, int experts, int rows,
-    int hidden, int output, int wsets, unsigned* err) {
+    int hidden, int output, int wsets, unsigned* err, const RowScatter scatter) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
@@ -343,8 +343,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         const int c_begin = cgroup * kEpiCols;
         const bool active = c_begin < pg.ncols;  // warp-uniform
         const int row = pg.base + quarter * 32 + lane;
-        const bool store_row = pending_last && active && row >= pg.row0 && row < pg.row_end;
+        bool store_row = pending_last && active && row >= pg.row0 && row < pg.row_end;
         float* out = y + static_cast<long long>(row) * output + pg.col0 + c_begin;
+        if (scatter.dst != nullptr && store_row) {
+          float* dst_row = scatter_row(scatter, row, output);
+          store_row = dst_row != nullptr;
+          out = dst_row + pg.col0 + c_begin;
+        }
         const int w = min(kEpiCols, pg.ncols - c_begin);
         if (active) {
 #pragma unroll
@@ -407,6 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     }
   }
 
+  // Scattered rows may live in another rank's memory: complete those stores
+  // before the kernel ends (the barrier that follows publishes them).
+  if (scatter.dst != nullptr && warp >= kFirstWorkerWarp) __threadfence_system();
   __syncthreads();
   if (warp == 0 && lane == 0 && *failed) {
     // Drain TMA loads still in flight into this CTA's shared memory.
@@ -474,7 +482,8 @@ bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidde
 
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
-                                   cudaStream_t stream, int weight_sets) {
+                                   cudaStream_t stream, int weight_sets,
+                                   const RowScatter* scatter) {
   const int wsets = weight_sets > 0 ? weight_sets : experts;
   EncodeTiledFn encode = encode_fn();
   if (encode == nullptr || !kernel_configured()) return cudaErrorNotSupported;
@@ -517,20 +526,21 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
     if (tiles < grid) grid = static_cast<int>(tiles);
   }
   grouped_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word());
+      ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(),
+      scatter != nullptr ? *scatter : RowScatter{});
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets, float* y,
                                 int experts, int rows, int hidden, int output,
-                                cudaStream_t stream, int weight_sets) {
+                                cudaStream_t stream, int weight_sets, const RowScatter* scatter) {
   if (tc_gemm_supported(x, w, y, hidden, output)) {
     return launch_grouped_gemm_tc(x, w, offsets, y, experts, rows, hidden, output, stream,
-                                  weight_sets);
+                                  weight_sets, scatter);
   }
   return launch_grouped_gemm_simt(x, w, offsets, y, experts, rows, hidden, output, stream,
-                                  weight_sets);
+                                  weight_sets, scatter);
 }
 
 }  // namespace rrb

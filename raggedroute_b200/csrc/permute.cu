@@ -163,18 +163,63 @@ __device__ __forceinline__ void copy_row_warp(const float* __restrict__ src, flo
   }
 }
 
+// Copy a row to up to 8 destination rows given as pointers (nullptr = skip);
+// the destinations may be another rank's memory. One warp.
+template <bool kVec>
+__device__ __forceinline__ void copy_row_warp_to(const float* __restrict__ src, float* const* dst,
+                                                 int n, int hidden) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (kVec) {
+    const int n4 = hidden >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    int i = lane;
+    for (; i + 96 < n4; i += 128) {
+      const float4 a = __ldg(s4 + i);
+      const float4 b = __ldg(s4 + i + 32);
+      const float4 c = __ldg(s4 + i + 64);
+      const float4 d = __ldg(s4 + i + 96);
+      for (int k = 0; k < n; ++k) {
+        if (dst[k] == nullptr) continue;
+        float4* d4 = reinterpret_cast<float4*>(dst[k]);
+        d4[i] = a;
+        d4[i + 32] = b;
+        d4[i + 64] = c;
+        d4[i + 96] = d;
+      }
+    }
+    for (; i < n4; i += 32) {
+      const float4 a = __ldg(s4 + i);
+      for (int k = 0; k < n; ++k) {
+        if (dst[k] != nullptr) reinterpret_cast<float4*>(dst[k])[i] = a;
+      }
+    }
+  } else {
+    for (int i = lane; i < hidden; i += 32) {
+      const float a = __ldg(src + i);
+      for (int k = 0; k < n; ++k) {
+        if (dst[k] != nullptr) dst[k][i] = a;
+      }
+    }
+  }
+}
+
 // Place + copy. chunk_base == nullptr means a single chunk seeded by offsets
 // (and this kernel then also writes the cursor post-state).
-template <bool kVec>
+// With kPeer the rows go to the owners' receive buffers (PeerDispatch) and
+// xp / sorted_route are unused.
+template <bool kVec, bool kPeer>
 __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ offsets, const int32_t* __restrict__ chunk_base,
     float* __restrict__ xp, int32_t* __restrict__ route_pos, int32_t* __restrict__ sorted_route,
     int32_t* __restrict__ cursors, int tokens, int experts, int top_k, int hidden,
-    int tokens_per_chunk) {
+    int tokens_per_chunk, const PeerDispatch peer) {
   extern __shared__ int smem[];
   int* warp_base = smem;                            // [kPlaceWarps][experts]
   int* pos = smem + kPlaceWarps * experts;          // [routes in chunk]
+  // Peer mode: packed (owner << 40 | receive row) per route, -1 = dropped.
+  long long* remote = reinterpret_cast<long long*>(
+      smem + ((kPlaceWarps * experts + kMaxChunkRoutes + 1) & ~1));
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * tokens_per_chunk;
@@ -241,12 +286,50 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
       if (local < nr && e != -1) {
         pos[local] = p;
         route_pos[r0 + local] = p;
-        if (sorted_route != nullptr && p >= 0) sorted_route[p] = static_cast<int32_t>(r0 + local);
+        if constexpr (kPeer) {
+          long long packed = -1;
+          if (p >= 0) {
+            const int owner = e / peer.local;
+            const long long row = static_cast<long long>(__ldg(peer.dest_off + e)) +
+                                  (p - __ldg(offsets + e));
+            if (row < peer.capacity) {
+              peer.ret_base[owner][row] =
+                  (static_cast<long long>(peer.me) << kPeerRankShift) | static_cast<long long>(p);
+              packed = (static_cast<long long>(owner) << kPeerRankShift) | row;
+            } else {
+              raise_device_error(peer.err, kErrEpCapacity);
+            }
+          }
+          remote[local] = packed;
+        } else {
+          if (sorted_route != nullptr && p >= 0) {
+            sorted_route[p] = static_cast<int32_t>(r0 + local);
+          }
+        }
       }
     }
   }
   __syncthreads();
 
+  if constexpr (kPeer) {
+    for (int t = t0 + warp; t < t1; t += kPlaceWarps) {
+      const long long* d = remote + static_cast<long long>(t - t0) * top_k;
+      for (int k0 = 0; k0 < top_k; k0 += 8) {
+        const int kn = min(8, top_k - k0);
+        float* dst[8];
+        for (int k = 0; k < kn; ++k) {
+          const long long v = d[k0 + k];
+          dst[k] = v < 0 ? nullptr
+                         : peer.x_base[v >> kPeerRankShift] + (v & kPeerRowMask) * hidden;
+        }
+        copy_row_warp_to<kVec>(x + static_cast<long long>(t) * hidden, dst, kn, hidden);
+      }
+    }
+    // Make this thread's stores to other ranks' memory complete before the
+    // kernel ends (the barrier that follows then publishes them).
+    __threadfence_system();
+    return;
+  }
   if (hidden <= 0) return;
   // Copy: one warp per token row, read once, written top_k times.
   for (int t = t0 + warp; t < t1; t += kPlaceWarps) {
@@ -338,10 +421,13 @@ std::size_t permute_workspace_bytes(int tokens, int experts, int top_k) {
   return align256(cursors) + static_cast<std::size_t>(p.chunks) * experts * sizeof(int32_t);
 }
 
-cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32_t* offsets,
-                                 float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
-                                 int tokens, int experts, int top_k, int hidden, void* workspace,
-                                 cudaStream_t stream) {
+namespace {
+
+template <bool kPeer>
+cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offsets,
+                         float* x_permuted, int32_t* route_pos, int32_t* sorted_route, int tokens,
+                         int experts, int top_k, int hidden, void* workspace,
+                         const PeerDispatch& peer, cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
   const ChunkPlan p = plan_chunks(tokens, top_k);
   int32_t* cursors = static_cast<int32_t*>(workspace);
@@ -357,30 +443,58 @@ cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32
                                                                       p.chunks, experts);
     note_launch(2);
   }
-  const bool vec = hidden % 4 == 0 && aligned_to(x, 16) && aligned_to(x_permuted, 16);
-  const std::size_t smem = (static_cast<std::size_t>(kPlaceWarps) * experts + routes_per_chunk) *
-                           sizeof(int);
+  // Peer mode keeps pos[] at its full size so the int64 table that follows is
+  // at a fixed, 8-byte aligned offset.
+  const std::size_t ints = static_cast<std::size_t>(kPlaceWarps) * experts +
+                           (kPeer ? kMaxChunkRoutes + 1 : routes_per_chunk);
+  const std::size_t smem = kPeer ? ((ints & ~static_cast<std::size_t>(1)) * sizeof(int) +
+                                    static_cast<std::size_t>(kMaxChunkRoutes) * sizeof(long long))
+                                 : ints * sizeof(int);
+  const bool vec = hidden % 4 == 0 && aligned_to(x, 16) &&
+                   (kPeer || aligned_to(x_permuted, 16));
   if (smem > 48 * 1024) {
-    cudaError_t e1 = cudaFuncSetAttribute(permute_place_kernel<true>,
+    cudaError_t e1 = cudaFuncSetAttribute(permute_place_kernel<true, kPeer>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(smem));
-    cudaError_t e2 = cudaFuncSetAttribute(permute_place_kernel<false>,
+    cudaError_t e2 = cudaFuncSetAttribute(permute_place_kernel<false, kPeer>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(smem));
     if (e1 != cudaSuccess) return e1;
     if (e2 != cudaSuccess) return e2;
   }
   if (vec) {
-    permute_place_kernel<true><<<p.chunks, kPlaceThreads, smem, stream>>>(
+    permute_place_kernel<true, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
         x, ids, offsets, chunk_base, x_permuted, route_pos, sorted_route, cursors, tokens,
-        experts, top_k, hidden, p.tokens_per_chunk);
+        experts, top_k, hidden, p.tokens_per_chunk, peer);
   } else {
-    permute_place_kernel<false><<<p.chunks, kPlaceThreads, smem, stream>>>(
+    permute_place_kernel<false, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
         x, ids, offsets, chunk_base, x_permuted, route_pos, sorted_route, cursors, tokens,
-        experts, top_k, hidden, p.tokens_per_chunk);
+        experts, top_k, hidden, p.tokens_per_chunk, peer);
   }
   note_launch();
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32_t* offsets,
+                                 float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
+                                 int tokens, int experts, int top_k, int hidden, void* workspace,
+                                 cudaStream_t stream) {
+  return permute_impl<false>(x, ids, offsets, x_permuted, route_pos, sorted_route, tokens,
+                             experts, top_k, hidden, workspace, PeerDispatch{}, stream);
+}
+
+cudaError_t launch_token_permute_peer(const float* x, const int32_t* ids, const int32_t* offsets,
+                                      int32_t* route_pos, int tokens, int experts, int top_k,
+                                      int hidden, void* workspace, const PeerDispatch& peer,
+                                      cudaStream_t stream) {
+  if (peer.x_base == nullptr || peer.ret_base == nullptr || peer.dest_off == nullptr ||
+      peer.local < 1) {
+    return cudaErrorInvalidValue;
+  }
+  return permute_impl<true>(x, ids, offsets, nullptr, route_pos, nullptr, tokens, experts, top_k,
+                            hidden, workspace, peer, stream);
 }
 
 cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,

@@ -234,6 +234,43 @@ __global__ void __launch_bounds__(1024) ep_recv_offsets_kernel(const int32_t* __
   if (q == 0) recv_offsets[groups] = total;
 }
 
+// Peer-transport layout. Rank d's receive buffer holds its local experts in
+// order and, inside an expert, the rows of source ranks 0..G-1 in order, so
+// its grouped GEMM sees plain contiguous expert segments. One CTA, one
+// thread per (virtual) expert.
+__global__ void __launch_bounds__(1024) ep_peer_layout_kernel(
+    const int32_t* __restrict__ count_all, int32_t* __restrict__ dest_off,
+    int32_t* __restrict__ recv_offsets, int nranks, int experts, int rank, int local,
+    long long capacity, unsigned* err) {
+  __shared__ long long column[kMaxExperts];  // rows of expert v over all sources
+  const int v = threadIdx.x;
+  long long col = 0, before = 0;
+  if (v < experts) {
+    for (int s = 0; s < nranks; ++s) {
+      const int c = count_all[static_cast<long long>(s) * experts + v];
+      if (s < rank) before += c;
+      col += c;
+    }
+    column[v] = col;
+  }
+  __syncthreads();
+  if (v >= experts) return;
+  const int owner = v / local;
+  const int le = v - owner * local;
+  long long base = 0;
+  for (int j = owner * local; j < v; ++j) base += column[j];
+  const long long off = base + before;
+  dest_off[v] = static_cast<int32_t>(off < capacity ? off : capacity);
+  if (owner == rank) {
+    recv_offsets[le] = static_cast<int32_t>(base < capacity ? base : capacity);
+    if (le == local - 1) {
+      const long long end = base + col;
+      if (end > capacity) raise_device_error(err, kErrEpCapacity);
+      recv_offsets[local] = static_cast<int32_t>(end < capacity ? end : capacity);
+    }
+  }
+}
+
 int hist_grid(long long routes) {
   const int want = ceil_div(routes, kHistThreads * 16LL);
   const int cap = 2 * sm_count();
@@ -283,6 +320,17 @@ cudaError_t launch_ep_recv_offsets(const int32_t* count_all, int32_t* recv_offse
                                    int experts, int rank, int local, cudaStream_t stream) {
   ep_recv_offsets_kernel<<<1, 1024, 0, stream>>>(count_all, recv_offsets, nranks, experts, rank,
                                                  local);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_peer_layout(const int32_t* count_all, int32_t* dest_off,
+                                  int32_t* recv_offsets, int nranks, int experts, int rank,
+                                  int local, long long capacity, unsigned* err,
+                                  cudaStream_t stream) {
+  if (experts > kMaxExperts || local < 1) return cudaErrorInvalidValue;
+  ep_peer_layout_kernel<<<1, 1024, 0, stream>>>(count_all, dest_off, recv_offsets, nranks,
+                                                experts, rank, local, capacity, err);
   note_launch();
   return cudaGetLastError();
 }

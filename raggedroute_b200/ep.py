@@ -15,16 +15,20 @@ from raggedroute_b200._lib import Context, check, lib
 from raggedroute_b200.ops import ChainBuffers, _ctx, _ptr
 
 UNIQUE_ID_BYTES = 128
+TRANSPORTS = {"auto": 0, "nccl": 1, "peer": 2}
 
 
 class ExpertParallel:
     """`experts` virtual experts (V) are split evenly over the ranks; the
     router scores `router_experts` real experts (R, default V) and
-    chain_from_tokens takes this rank's remap table R -> V when they differ."""
+    chain_from_tokens takes this rank's remap table R -> V when they differ.
+    transport: "auto" (peer memory when every rank maps every other rank's
+    buffers, else NCCL), "peer" or "nccl"; `self.transport` is the one used."""
 
     def __init__(self, experts: int, max_tokens: int, hidden: int, output: int,
                  rank: int | None = None, world: int | None = None, group=None,
-                 timeout_s: float = 120.0, router_experts: int | None = None):
+                 timeout_s: float = 120.0, router_experts: int | None = None,
+                 transport: str = "auto"):
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
         self.experts, self.hidden, self.output = experts, hidden, output
@@ -44,15 +48,20 @@ class ExpertParallel:
         handle = ctypes.c_void_p()
         check(lib().rr_ep_create(ctypes.cast(raw, ctypes.c_void_p), self.world, self.rank,
                                  self.router_experts, experts, max_tokens, hidden, output,
-                                 timeout_s, ctypes.byref(handle)), "rr_ep_create")
+                                 timeout_s, TRANSPORTS[transport], ctypes.byref(handle)),
+              "rr_ep_create")
         self._h = handle
+        t = ctypes.c_int()
+        check(lib().rr_ep_transport(self._h, ctypes.byref(t)), "rr_ep_transport")
+        self.transport = {v: k for k, v in TRANSPORTS.items()}[t.value]
 
     def chain_from_tokens(self, x: torch.Tensor, router_weights: torch.Tensor,
                           local_expert_weights: torch.Tensor, buf: ChainBuffers,
                           logit_bias: torch.Tensor | None = None,
                           expert_remap: torch.Tensor | None = None,
                           ctx: Context | None = None) -> torch.Tensor:
-        """buf must be allocated for V virtual experts with logits [T, R]."""
+        """buf must be allocated for V virtual experts with logits [T, R]. The
+        peer transport leaves buf.x_permuted / buf.y_permuted unwritten."""
         tokens = x.shape[0]
         check(lib().rr_ep_chain_from_tokens(
             self._h, _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(expert_remap),

@@ -2,9 +2,11 @@
 
 * One rank (no communicator): rr_ep_chain_from_tokens equals
   rr_chain_from_tokens bit for bit.
-* Two or more GPUs: tests/ep_worker.py under torchrun; every rank's EP output
-  must equal its single-GPU chain bit for bit (LPT-relabelled experts, Zipf
-  logit bias). Skipped, with the reason, when fewer than two GPUs are visible.
+* Two or more GPUs: tests/ep_worker.py under torchrun, for both transports
+  (peer memory and NCCL) and with equal or ragged per-rank token counts
+  (one rank idle); every rank's EP output must equal its single-GPU chain bit
+  for bit (replicated hot experts, Zipf logit bias). Skipped, with the
+  reason, when fewer than two GPUs are visible.
 """
 from __future__ import annotations
 
@@ -41,11 +43,13 @@ def test_ep_single_rank_matches_chain(rrlib, cuda):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
-def test_ep_multi_gpu_matches_single_gpu_chain(rrlib, cuda):
+@pytest.mark.parametrize("transport,ragged,port", [("peer", "0", 29531), ("peer", "1", 29532),
+                                                   ("nccl", "0", 29533), ("nccl", "1", 29534)])
+def test_ep_multi_gpu_matches_single_gpu_chain(rrlib, cuda, transport, ragged, port):
     world = min(torch.cuda.device_count(), 8)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TRANSPORT=transport, EP_RAGGED=ragged)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
-           "--master-port=29531", os.path.join(ROOT, "tests", "ep_worker.py")]
+           f"--master-port={port}", os.path.join(ROOT, "tests", "ep_worker.py")]
     res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert res.returncode == 0, res.stdout[-4000:] + res.stderr[-4000:]
