@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=None, help="override T per GPU (testing)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=8192,
+                    help="tokens per chunk of the host-memory chain (e2e, one GPU)")
     ap.add_argument("--ep-transport", choices=["auto", "peer", "nccl"], default="auto",
                     help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--stages", action="store_true", help="print the per-stage table to stderr")
@@ -329,21 +331,28 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     counts = buf.counts.cpu()
     assert int(counts.sum()) == routes
 
-    # End-to-end through the public chain API with host buffers.
+    # End-to-end through the public API with host buffers: one GPU uses the
+    # host-memory chain (rr_chain_from_tokens_host: chunks of X in, the chain,
+    # chunks of Y out, copies overlapped with the chain); expert parallelism
+    # copies X in, runs the EP step and copies Y out.
     e2e = None
     if not args.no_e2e:
         x_host = inp.x.cpu().pin_memory()
         y_host = torch.empty(tokens, n, dtype=torch.float32).pin_memory()
-        x_dev = torch.empty_like(inp.x)
+        if ep is None:
+            host_chain = rr.HostChain(args.e2e_chunk, k, e, n)
+        else:
+            x_dev = torch.empty_like(inp.x)
+
         def e2e_step():
-            x_dev.copy_(x_host, non_blocking=True)
             if ep is None:
-                rr.chain_from_tokens(x_dev, inp.router_w, inp.expert_w, buf,
-                                     logit_bias=inp.logit_bias, ctx=ctx)
-            else:
-                ep.chain_from_tokens(x_dev, inp.router_w, local_w, ep_buf,
-                                     logit_bias=inp.logit_bias, expert_remap=remap, ctx=ctx)
-            y_host.copy_((buf if ep is None else ep_buf).y, non_blocking=True)
+                host_chain(x_host, inp.router_w, inp.expert_w, y_host,
+                           logit_bias=inp.logit_bias, ctx=ctx)
+                return
+            x_dev.copy_(x_host, non_blocking=True)
+            ep.chain_from_tokens(x_dev, inp.router_w, local_w, ep_buf,
+                                 logit_bias=inp.logit_bias, expert_remap=remap, ctx=ctx)
+            y_host.copy_(ep_buf.y, non_blocking=True)
 
         with torch.cuda.stream(stream):
             for _ in range(max(1, args.warmup)):
@@ -364,7 +373,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": tokens * world * args.steps / (float(te.item()) * 1e-3), "unit": UNIT,
                "h2d_bytes_per_step": x_host.numel() * 4,
-               "d2h_bytes_per_step": y_host.numel() * 4}
+               "d2h_bytes_per_step": y_host.numel() * 4,
+               "api": ("rr_chain_from_tokens_host, chunk %d tokens" % args.e2e_chunk
+                       if ep is None else "copy in + rr_ep_chain_from_tokens + copy out")}
+        if ep is None:
+            host_chain.close()
 
     if ep is not None:
         ep.close()

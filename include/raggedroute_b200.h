@@ -181,6 +181,30 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
                                int output, const rr_context* ctx);
 size_t rr_chain_workspace_size(int tokens, int hidden, int experts, int output);
 
+/* ---- chain over host memory (new: no reference counterpart) --------------
+ * chain_from_tokens for tokens that live in host memory. The batch is cut
+ * into chunks of chunk_tokens; each chunk's X is copied in on one copy
+ * stream, runs the seven-stage chain on ctx->stream and its Y is copied out
+ * on another, with two device slots, so the copies of neighbouring chunks
+ * overlap the chain. Y is bit-identical to rr_chain_from_tokens over the
+ * whole batch. Plan-time allocation only (two slots of chain buffers). */
+typedef struct rr_host_chain rr_host_chain;
+rr_status rr_host_chain_create(int chunk_tokens, int hidden, int experts, int output,
+                               rr_host_chain** out);
+rr_status rr_host_chain_destroy(rr_host_chain* plan);
+/* x_host [tokens, K] and y_host [tokens, N] should be pinned (pageable
+ * memory works but serialises the copies). router_weights, logit_bias
+ * (optional) and expert_weights are device buffers as for
+ * rr_chain_from_tokens. expert_ids_host / route_weights_host ([tokens, 2],
+ * optional) receive the routing decisions. Enqueue only; completion is
+ * ordered on ctx->stream (ctx->workspace is not used). One call at a time
+ * per plan. */
+rr_status rr_chain_from_tokens_host(rr_host_chain* plan, const float* x_host,
+                                    const float* router_weights, const float* logit_bias,
+                                    const float* expert_weights, float* y_host,
+                                    int32_t* expert_ids_host, float* route_weights_host,
+                                    int tokens, const rr_context* ctx);
+
 /* ---- expert parallelism (new: the reference is single-GPU) ----------------
  * One process per GPU. The router scores R real experts; the gate maps each
  * selected id through a per-rank remap table to one of V virtual experts

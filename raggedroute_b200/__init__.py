@@ -44,6 +44,7 @@ from raggedroute_b200.ops import (  # noqa: F401
     chain_from_logits,
     chain_workspace_size,
     ChainBuffers,
+    HostChain,
     kernel_launch_count,
     grouped_gemm_engine,
 )
@@ -51,5 +52,5 @@ from raggedroute_b200.ops import (  # noqa: F401
 __all__ = [
     "dense_gemm", "topk_gate", "histogram", "exclusive_scan", "histogram_exclusive_scan",
     "token_permute", "grouped_gemm", "unpermute", "chain_from_tokens", "chain_from_logits",
-    "Context", "RaggedRouteError", "StatusCode", "lib",
+    "HostChain", "Context", "RaggedRouteError", "StatusCode", "lib",
 ]

@@ -106,6 +106,9 @@ SIGNATURES = {
     "rr_consume_device_error": (RRStatus, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "rr_grouped_gemm_engine": (_I, [_P, _P, _P, _I, _I]),
     "rr_version": (ctypes.c_char_p, []),
+    "rr_host_chain_create": (RRStatus, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
+    "rr_host_chain_destroy": (RRStatus, [_P]),
+    "rr_chain_from_tokens_host": (RRStatus, [_P] * 8 + [_I, _CTX]),
     "rr_ep_get_unique_id": (RRStatus, [_P]),
     "rr_ep_create": (RRStatus, [_P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_double, _I,
                                  ctypes.POINTER(ctypes.c_void_p)]),

@@ -219,6 +219,51 @@ def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights: tor
     return buf.y
 
 
+class HostChain:
+    """chain_from_tokens over host memory (rr_chain_from_tokens_host): chunks
+    of `chunk_tokens` stream host -> device, through the chain and back on
+    separate copy streams, overlapping the copies with the chain. Y is
+    bit-identical to chain_from_tokens over the whole batch."""
+
+    def __init__(self, chunk_tokens: int, hidden: int, experts: int, output: int):
+        self.chunk_tokens, self.hidden, self.experts, self.output = (chunk_tokens, hidden,
+                                                                     experts, output)
+        h = ctypes.c_void_p()
+        check(lib().rr_host_chain_create(chunk_tokens, hidden, experts, output, ctypes.byref(h)),
+              "rr_host_chain_create")
+        self._h = h
+
+    def __call__(self, x_host: torch.Tensor, router_weights: torch.Tensor,
+                 expert_weights: torch.Tensor, y_host: torch.Tensor,
+                 logit_bias: torch.Tensor | None = None,
+                 expert_ids_host: torch.Tensor | None = None,
+                 route_weights_host: torch.Tensor | None = None,
+                 ctx: Context | None = None) -> torch.Tensor:
+        """x_host [T, K] / y_host [T, N] float32 host tensors (pin them for
+        overlap); weights on the device. Enqueues; completion is ordered on
+        ctx.stream (the default stream when ctx is None)."""
+        for t, name in ((x_host, "x_host"), (y_host, "y_host")):
+            if t.device.type != "cpu" or t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous float32 host tensor")
+        tokens = x_host.shape[0]
+        check(lib().rr_chain_from_tokens_host(
+            self._h, _ptr(x_host), _ptr(router_weights), _ptr(logit_bias),
+            _ptr(expert_weights), _ptr(y_host), _ptr(expert_ids_host), _ptr(route_weights_host),
+            tokens, _ctx(ctx)), "rr_chain_from_tokens_host")
+        return y_host
+
+    def close(self) -> None:
+        if self._h:
+            lib().rr_host_chain_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
 def kernel_launch_count() -> int:
     return int(lib().rr_kernel_launch_count())
 
