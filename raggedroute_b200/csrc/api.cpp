@@ -1131,6 +1131,8 @@ int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
   return rrb::tc_gemm_supported(x_permuted, expert_weights, y_permuted, hidden, output) ? 1 : 2;
 }
 
+int rr_grouped_gemm_cta_pairs(void) { return rrb::grouped_gemm_tc_pairs(); }
+
 const char* rr_version(void) { return "raggedroute_b200 0.1.0 (sm_100a)"; }
 
 }  // extern "C"

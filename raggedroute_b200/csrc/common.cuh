@@ -161,6 +161,8 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
                                      cudaStream_t stream, int weight_sets = 0,
                                      const RowScatter* scatter = nullptr);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
+// CTA pairs the tcgen05 engine runs on (cta_group::2); 0 = single CTAs.
+int grouped_gemm_tc_pairs();
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
                                    cudaStream_t stream, int weight_sets = 0,

@@ -1,6 +1,7 @@
 // Thin inline-PTX wrappers for the sm_100a features the GEMM engine uses:
-// mbarriers (with bounded waits), TMA tensor loads (no multicast), and the
-// tcgen05 tensor-memory / MMA instructions. Written from the PTX ISA.
+// mbarriers (with bounded waits, local and across a CTA pair), TMA tensor
+// loads (no multicast), and the tcgen05 tensor-memory / MMA instructions for
+// one CTA and for a CTA pair. Written from the PTX ISA.
 #pragma once
 
 #include <cuda.h>
@@ -21,6 +22,12 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
+// Every wait gives up after this much wall time (see mbar_wait).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Suspend-time hint of a blocking try_wait: the thread sleeps until the phase
+// completes or this much time passes, then re-checks (and the time limit).
+constexpr uint32_t kSuspendHintNs = 1000000u;  // 1 ms
 
 // ---- mbarrier ------------------------------------------------------------------
 
@@ -71,19 +78,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete. Gives up after
-// `limit_ns` of wall time: raises kErrMbarTimeout in *err_word, sets *failed
-// and returns false. No wait in this library can spin forever.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-
+// Waits for the phase with the given parity to complete, sleeping in a
+// suspend-hinted try_wait between checks. Gives up after kWaitLimitNs of wall
+// time: raises kErrMbarTimeout in *err_word, sets *failed and returns false.
+// No wait in this library can spin forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err_word,
-                                          volatile int* failed, uint32_t sleep_ns = 0) {
+                                          volatile int* failed) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-    if (sleep_ns != 0 ? mbar_try_wait_sleep(bar, parity, sleep_ns) : mbar_try_wait(bar, parity)) {
-      return true;
-    }
+    if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (*failed) return false;
     if (global_timer_ns() - start > kWaitLimitNs) {
       raise_device_error(err_word, kErrMbarTimeout);
@@ -91,6 +95,76 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
       return false;
     }
   }
+}
+
+// ---- clusters (CTA pairs) ---------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster
+// address, which may belong to another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// try_wait with acquire at cluster scope (for phases completed by arrivals
+// from the other CTA of a pair).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t* bar, uint32_t parity,
+                                                            uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  unsigned* err_word, volatile int* failed) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster_sleep(bar, parity, kSuspendHintNs)) return true;
+    if (*failed) return false;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      raise_device_error(err_word, kErrMbarTimeout);
+      *failed = 1;
+      return false;
+    }
+  }
+}
+
+// Every thread of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
 }
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) --------------
@@ -163,6 +237,24 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                : "memory");
 }
 
+// CTA-pair forms: issued by the same warp in both CTAs of the pair, with the
+// same destination offset; both CTAs then own the same columns.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -179,6 +271,31 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// CTA pair (issued by the even CTA): D rows 0..M/2-1 land in this CTA's
+// TMEM and rows M/2..M-1 in the odd CTA's; A rows and B columns are read half
+// from each CTA's shared memory at the same offsets.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair form of the commit: arrives once on the mbarrier at the same offset in
+// both CTAs of the pair (mask 0b11) when the pair's MMAs issued so far by
+// this thread have completed. This is the tcgen05 completion signal, not a
+// memory copy.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n\t}" ::"r"(smem_u32(bar))
       : "memory");
 }
 

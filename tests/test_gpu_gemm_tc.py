@@ -6,7 +6,9 @@ elementwise, AND a normwise relative error <= 1e-5.
 Shapes cover ragged and empty groups, partial m/n/k tiles, groups shorter than
 one tile at the start of the buffer, N > 256 and K up to 4096. Every case also
 asserts that the engine selected was tcgen05 and that no bounded wait timed
-out (device error word 0).
+out (device error word 0). Every case runs twice: on single CTAs (128-row
+tiles, the default) and on CTA pairs (cta_group::2, 256-row tiles,
+RAGGEDROUTE_B200_GEMM_PAIRS=1).
 """
 from __future__ import annotations
 
@@ -18,6 +20,17 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True, params=["pairs", "single"])
+def cta_mode(request, monkeypatch, rrlib):
+    if request.param == "single":
+        monkeypatch.delenv("RAGGEDROUTE_B200_GEMM_PAIRS", raising=False)
+        assert rrlib.lib().rr_grouped_gemm_cta_pairs() == 0
+    else:
+        monkeypatch.setenv("RAGGEDROUTE_B200_GEMM_PAIRS", "1")
+        assert rrlib.lib().rr_grouped_gemm_cta_pairs() > 0
+    return request.param
 
 
 def dev(a, device):
