@@ -308,14 +308,16 @@ uint64_t rr_kernel_launch_count(void);
 /* Reads and clears the device-side error word set by bounded waits in the
  * library's kernels (0 = no error). Synchronizes the given stream. */
 rr_status rr_consume_device_error(void* stream, uint32_t* error_word);
-/* Number of CTA pairs (cta_group::2, 256-row tiles) the tcgen05 engine runs
- * on for the current device; 0 when it runs one CTA per 128-row tile (the
- * default). RAGGEDROUTE_B200_GEMM_PAIRS=1 in the environment selects pairs. */
-int rr_grouped_gemm_cta_pairs(void);
 /* Which grouped-GEMM engine a shape takes: 1 = tcgen05 3xTF32, 2 = FP32 SIMT. */
 int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
                            float* y_permuted, int hidden, int output);
 const char* rr_version(void);
+/* Device self-check of the GEMM's TF32 split (no reference counterpart):
+ * adds to *mismatches (device, caller-zeroed) the number of the n bit
+ * patterns (device) whose integer round-to-nearest-away TF32 rounding
+ * differs from the cvt.rna.tf32.f32 instruction; NaN patterns are skipped. */
+rr_status rr_tf32_rounding_selfcheck(const uint32_t* bits, int64_t n,
+                                     unsigned long long* mismatches, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

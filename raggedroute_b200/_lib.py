@@ -105,7 +105,7 @@ SIGNATURES = {
     "rr_kernel_launch_count": (ctypes.c_uint64, []),
     "rr_consume_device_error": (RRStatus, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "rr_grouped_gemm_engine": (_I, [_P, _P, _P, _I, _I]),
-    "rr_grouped_gemm_cta_pairs": (_I, []),
+    "rr_tf32_rounding_selfcheck": (RRStatus, [_P, ctypes.c_int64, _P, _P]),
     "rr_version": (ctypes.c_char_p, []),
     "rr_host_chain_create": (RRStatus, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
     "rr_host_chain_destroy": (RRStatus, [_P]),

@@ -1131,7 +1131,18 @@ int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
   return rrb::tc_gemm_supported(x_permuted, expert_weights, y_permuted, hidden, output) ? 1 : 2;
 }
 
-int rr_grouped_gemm_cta_pairs(void) { return rrb::grouped_gemm_tc_pairs(); }
+rr_status rr_tf32_rounding_selfcheck(const uint32_t* bits, int64_t n,
+                                     unsigned long long* mismatches, void* stream) {
+  if (n < 0 || (n > 0 && (bits == nullptr || mismatches == nullptr))) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "rr_tf32_rounding_selfcheck requires device buffers"});
+  }
+  const cudaError_t err = rrb::launch_tf32_round_check(bits, n, mismatches, as_stream(stream));
+  if (err != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, err, "TF32 rounding self-check failed"});
+  }
+  return to_c(raggedroute::success_status());
+}
 
 const char* rr_version(void) { return "raggedroute_b200 0.1.0 (sm_100a)"; }
 

@@ -161,8 +161,6 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
                                      cudaStream_t stream, int weight_sets = 0,
                                      const RowScatter* scatter = nullptr);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
-// CTA pairs the tcgen05 engine runs on (cta_group::2); 0 = single CTAs.
-int grouped_gemm_tc_pairs();
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
                                    cudaStream_t stream, int weight_sets = 0,
@@ -170,5 +168,9 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
 
 // misc.cu
 cudaError_t launch_cache_scrub(uint32_t* buffer, std::size_t elements, cudaStream_t stream);
+// Adds to *mismatches (device) the number of non-NaN inputs whose integer
+// TF32 rounding differs from the conversion instruction.
+cudaError_t launch_tf32_round_check(const uint32_t* bits, long long n,
+                                    unsigned long long* mismatches, cudaStream_t stream);
 
 }  // namespace rrb

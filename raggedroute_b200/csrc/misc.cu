@@ -4,7 +4,7 @@
 #include <atomic>
 #include <mutex>
 
-#include "common.cuh"
+#include "sm100.cuh"
 
 namespace rrb {
 namespace {
@@ -21,7 +21,29 @@ __global__ void cache_scrub_kernel(uint32_t* buffer, std::size_t elements) {
   }
 }
 
+// Counts inputs whose integer TF32 rounding differs from cvt.rna.tf32.f32
+// (NaN inputs are skipped: the two may pick different NaN/inf patterns).
+__global__ void tf32_round_check_kernel(const uint32_t* __restrict__ bits, long long n,
+                                        unsigned long long* __restrict__ mismatches) {
+  unsigned long long local = 0;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float x = __uint_as_float(bits[i]);
+    if (x != x) continue;
+    if (__float_as_uint(sm100::tf32_rna(x)) != __float_as_uint(sm100::tf32_rna_cvt(x))) ++local;
+  }
+  if (local != 0) atomicAdd(mismatches, local);
+}
+
 }  // namespace
+
+cudaError_t launch_tf32_round_check(const uint32_t* bits, long long n,
+                                    unsigned long long* mismatches, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  tf32_round_check_kernel<<<2 * sm_count(), 256, 0, stream>>>(bits, n, mismatches);
+  note_launch();
+  return cudaGetLastError();
+}
 
 void note_launch(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n)); }
 

@@ -1,7 +1,6 @@
 // Thin inline-PTX wrappers for the sm_100a features the GEMM engine uses:
-// mbarriers (with bounded waits, local and across a CTA pair), TMA tensor
-// loads (no multicast), and the tcgen05 tensor-memory / MMA instructions for
-// one CTA and for a CTA pair. Written from the PTX ISA.
+// mbarriers (with bounded waits), TMA tensor loads (no multicast), and the
+// tcgen05 tensor-memory / MMA instructions. Written from the PTX ISA.
 #pragma once
 
 #include <cuda.h>
@@ -97,76 +96,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
-// ---- clusters (CTA pairs) ---------------------------------------------------------
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
-  return r;
-}
-
-// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster
-// address, which may belong to another CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
-// try_wait with acquire at cluster scope (for phases completed by arrivals
-// from the other CTA of a pair).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t* bar, uint32_t parity,
-                                                            uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  unsigned* err_word, volatile int* failed) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t start = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait_cluster_sleep(bar, parity, kSuspendHintNs)) return true;
-    if (*failed) return false;
-    if (global_timer_ns() - start > kWaitLimitNs) {
-      raise_device_error(err_word, kErrMbarTimeout);
-      *failed = 1;
-      return false;
-    }
-  }
-}
-
-// Every thread of every CTA of the cluster.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
-
 // ---- explicit shared-memory accesses (32-bit shared addresses) --------------
 
 __device__ __forceinline__ float lds_f32(uint32_t addr) {
@@ -237,24 +166,6 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                : "memory");
 }
 
-// CTA-pair forms: issued by the same warp in both CTAs of the pair, with the
-// same destination offset; both CTAs then own the same columns.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -274,28 +185,16 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
-// CTA pair (issued by the even CTA): D rows 0..M/2-1 land in this CTA's
-// TMEM and rows M/2..M-1 in the odd CTA's; A rows and B columns are read half
-// from each CTA's shared memory at the same offsets.
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] x B[smem desc], kind::tf32, one CTA. A is M rows (one
+// per lane) x K 32-bit columns starting at a_tmem; it is K-major by
+// definition (the transpose-A bit of idesc must be 0).
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Pair form of the commit: arrives once on the mbarrier at the same offset in
-// both CTAs of the pair (mask 0b11) when the pair's MMAs issued so far by
-// this thread have completed. This is the tcgen05 completion signal, not a
-// memory copy.
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], m;\n\t}" ::"r"(smem_u32(bar))
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -345,6 +244,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// 32 lanes x 4 columns store: thread i writes 4 consecutive columns of lane i.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, float4 v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w))
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -385,7 +292,21 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn_major,
 
 // ---- TF32 split --------------------------------------------------------------------
 
+// Round to TF32 precision (10 explicit mantissa bits), to nearest with ties
+// away from zero, on the bit pattern: adding half of the dropped 13-bit
+// field to the magnitude bits and clearing the field rounds the magnitude
+// half-up, and a carry into the exponent is the correct rounding up to the
+// next binade. Identical to cvt.rna.tf32.f32 for finite inputs (checked
+// against it on the device); integer adds issue at the full rate, the
+// conversion does not. A NaN whose payload sits only in the dropped bits
+// becomes infinity here; the 3xTF32 split still yields NaN for it because
+// lo = v - hi is NaN.
 __device__ __forceinline__ float tf32_rna(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// The conversion instruction, kept for the device check of tf32_rna.
+__device__ __forceinline__ float tf32_rna_cvt(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);

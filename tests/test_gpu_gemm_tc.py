@@ -6,9 +6,7 @@ elementwise, AND a normwise relative error <= 1e-5.
 Shapes cover ragged and empty groups, partial m/n/k tiles, groups shorter than
 one tile at the start of the buffer, N > 256 and K up to 4096. Every case also
 asserts that the engine selected was tcgen05 and that no bounded wait timed
-out (device error word 0). Every case runs twice: on single CTAs (128-row
-tiles, the default) and on CTA pairs (cta_group::2, 256-row tiles,
-RAGGEDROUTE_B200_GEMM_PAIRS=1).
+out (device error word 0).
 """
 from __future__ import annotations
 
@@ -20,17 +18,6 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-
-
-@pytest.fixture(autouse=True, params=["pairs", "single"])
-def cta_mode(request, monkeypatch, rrlib):
-    if request.param == "single":
-        monkeypatch.delenv("RAGGEDROUTE_B200_GEMM_PAIRS", raising=False)
-        assert rrlib.lib().rr_grouped_gemm_cta_pairs() == 0
-    else:
-        monkeypatch.setenv("RAGGEDROUTE_B200_GEMM_PAIRS", "1")
-        assert rrlib.lib().rr_grouped_gemm_cta_pairs() > 0
-    return request.param
 
 
 def dev(a, device):
@@ -149,3 +136,27 @@ def test_grouped_tc_c4_full_size_sampled(rrlib, oracle, cuda):
                                                    for j in range(len(rows))])) <= 1e-5
     assert not torch.isnan(y).any()
     assert device_error_word(rrlib) == 0
+
+
+def test_integer_tf32_rounding_matches_cvt(rrlib, cuda):
+    """The split rounds to TF32 with integer adds on the bit pattern; it must
+    equal cvt.rna.tf32.f32 for every non-NaN input: random bit patterns over
+    the whole range plus the edge values (zeros, denormals, ties, the
+    largest finite values, infinities)."""
+    rng = np.random.default_rng(5)
+    rnd = rng.integers(0, 2**32, 1 << 22, dtype=np.uint64)
+    edges = []
+    for m in (0, 1, 0xFFF, 0x1000, 0x1001, 0x1FFF, 0x2000, 0x3000, 0x7FF000, 0x7FFFFF):
+        for e in (0, 1, 0x7E, 0x7F, 0x80, 0xFE):
+            for sgn in (0, 1):
+                edges.append((sgn << 31) | (e << 23) | m)
+    edges += [0x7F800000, 0xFF800000, 0x7F7FFFFF, 0xFF7FFFFF, 0x7F7FF000, 0x7F7FEFFF]
+    bits = np.concatenate([rnd, np.array(edges, dtype=np.uint64)]).astype(np.uint32)
+    dbits = torch.from_numpy(bits.view(np.int32)).to(cuda)
+    count = torch.zeros(1, dtype=torch.int64, device=cuda)
+    st = rrlib.lib().rr_tf32_rounding_selfcheck(
+        ctypes.c_void_p(dbits.data_ptr()), dbits.numel(), ctypes.c_void_p(count.data_ptr()),
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st.code == 0
+    torch.cuda.synchronize()
+    assert int(count.item()) == 0
