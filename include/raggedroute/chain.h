@@ -47,10 +47,43 @@ struct ChainFromLogitsArgs {
   int output = 0;
 };
 
+// Buffers of the post-route chain (top_k routes per token, R = T * top_k).
+struct RouteChainBuffers {
+  std::int32_t* counts = nullptr;        // [E]
+  std::int32_t* offsets = nullptr;       // [E + 1]
+  float* x_permuted = nullptr;           // [R, K]
+  std::int32_t* route_pos = nullptr;     // [R]
+  std::int32_t* sorted_route = nullptr;  // optional [R]: route held by each permuted row
+  float* y_permuted = nullptr;           // [R, N]
+  float* y = nullptr;                    // [T, N]  (the output)
+};
+
+// chain_from_route_ids (benchmarks/adapters/postroute_chain_adapter.cpp:
+// 240-354 of the reference): routing decided elsewhere; histogram + scan ->
+// stable token_permute -> grouped_gemm -> unpermute for top_k in [1, 8].
+struct ChainFromRouteIdsArgs {
+  const float* x = nullptr;                 // [T, K]
+  const std::int32_t* expert_ids = nullptr;  // [T, top_k], ids in [0, E)
+  const float* route_weights = nullptr;     // [T, top_k]
+  const float* expert_weights = nullptr;    // [E, K, N]
+  RouteChainBuffers buffers;
+  int tokens = 0;
+  int top_k = 0;
+  int hidden = 0;
+  int experts = 0;
+  int output = 0;
+};
+
 // Workspace (bytes) for either chain: the token_permute workspace at 2T routes.
 std::size_t get_chain_workspace_size(int tokens, int hidden, int experts, int output) noexcept;
 
 Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& context) noexcept;
 Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& context) noexcept;
+
+// Workspace (bytes) for chain_from_route_ids: the token_permute workspace at
+// T * top_k routes.
+std::size_t get_route_chain_workspace_size(int tokens, int top_k, int experts) noexcept;
+Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
+                            const RuntimeContext& context) noexcept;
 
 }  // namespace raggedroute

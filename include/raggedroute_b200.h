@@ -181,6 +181,21 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
                                int output, const rr_context* ctx);
 size_t rr_chain_workspace_size(int tokens, int hidden, int experts, int output);
 
+/* chain_from_route_ids (benchmarks/adapters/postroute_chain_adapter.cpp:
+ * 240-354): routing already decided, R = T*top_k routes with 1 <= top_k <=
+ * min(8, E). histogram + scan -> stable token_permute (route_pos, and
+ * sorted_route when non-NULL) -> grouped_gemm -> unpermute. expert_ids and
+ * route_weights are [T, top_k]; x_permuted [R, K], y_permuted [R, N], y
+ * [T, N]; ctx->workspace holds rr_route_chain_workspace_size(T, top_k, E)
+ * bytes. */
+rr_status rr_chain_from_route_ids(const float* x, const int32_t* expert_ids,
+                                  const float* route_weights, const float* expert_weights,
+                                  int32_t* counts, int32_t* offsets, float* x_permuted,
+                                  int32_t* route_pos, int32_t* sorted_route, float* y_permuted,
+                                  float* y, int tokens, int top_k, int hidden, int experts,
+                                  int output, const rr_context* ctx);
+size_t rr_route_chain_workspace_size(int tokens, int top_k, int experts);
+
 /* ---- chain over host memory (new: no reference counterpart) --------------
  * chain_from_tokens for tokens that live in host memory. The batch is cut
  * into chunks of chunk_tokens; each chunk's X is copied in on one copy

@@ -55,6 +55,8 @@ def _load_port() -> ctypes.CDLL:
         "rr_oracle_unpermute_f64": [_f32p, _i32p, _f32p, _int, _int, _int, _f64p],
         "rr_oracle_chain_logits_f32": [_f32p, _f32p, _int, _int, _int, _f32p],
         "rr_oracle_chain_output_f32": [_f32p, _f32p, _i32p, _f32p, _int, _int, _int, _int, _f32p],
+        "rr_oracle_route_chain_output_f32": [_f32p, _f32p, _i32p, _f32p, _int, _int, _int, _int,
+                                             _int, _f32p],
     }
     for name, argtypes in sigs.items():
         fn = getattr(lib, name)
@@ -243,6 +245,37 @@ def chain_output_f32(x, expert_w, ids, weights):
                                            _p(weights, _f32p), t, k, n, e, _p(y, _f32p)),
            "chain_output")
     return y
+
+
+def route_chain_output_f32(x, expert_w, ids, weights):
+    """Post-route chain output in float, rank order (postroute_chain_adapter.cpp:654-675)."""
+    x = _f32(x)
+    expert_w = _f32(expert_w)
+    ids = _i32(ids)
+    top_k = ids.shape[1]
+    ids = ids.reshape(-1)
+    weights = _f32(weights).reshape(-1)
+    t, k = x.shape
+    e, _, n = expert_w.shape
+    y = np.empty((t, n), np.float32)
+    _check(port.rr_oracle_route_chain_output_f32(_p(x, _f32p), _p(expert_w, _f32p),
+                                                 _p(ids, _i32p), _p(weights, _f32p), t, top_k,
+                                                 k, n, e, _p(y, _f32p)), "route_chain_output")
+    return y
+
+
+def route_chain_f64(x, expert_w, ids, weights, experts: int):
+    """Post-route chain composed from the stage oracles (histogram, scan,
+    stable permute, grouped GEMM and unpermute in double): returns counts,
+    offsets, x_permuted, route_pos, sorted_route and y (float64)."""
+    ids = _i32(ids)
+    top_k = ids.shape[1]
+    counts = histogram(ids.reshape(-1), experts)
+    offsets = exclusive_scan(counts)
+    xp, pos, sr, _ = stable_permute(x, ids, offsets, experts, top_k)
+    yp = grouped_gemm_f64(xp, expert_w, offsets).astype(np.float32)
+    y = unpermute_f64(yp, pos, weights, top_k)
+    return counts, offsets, xp, pos, sr, y
 
 
 # --------------------------------------------------------------------------

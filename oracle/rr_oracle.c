@@ -301,15 +301,22 @@ int rr_oracle_chain_logits_f32(const float* x, const float* router_w, int tokens
 /* Final chain output in float: for each token and column, the sum over the two
  * ranks of weight * (sequential float projection of x through the expert).
  * benchmarks/adapters/chain_adapter.cpp:858-879. */
-int rr_oracle_chain_output_f32(const float* x, const float* expert_w, const int32_t* ids,
-                               const float* weights, int tokens, int hidden, int output,
-                               int experts, float* y) {
-  if (tokens < 0 || hidden < 0 || output < 0 || experts < 1) return RR_ORACLE_BAD_SHAPE;
+/* Output of the post-route chain for top_k routes per token
+ * (benchmarks/adapters/postroute_chain_adapter.cpp:654-675): per token and
+ * column, combined += w[route] * projection in rank order, projection the
+ * float sum over hidden in order. With top_k = 2 this is also the L3 chain
+ * oracle's output half (chain_adapter.cpp:858-879). */
+int rr_oracle_route_chain_output_f32(const float* x, const float* expert_w, const int32_t* ids,
+                                     const float* weights, int tokens, int top_k, int hidden,
+                                     int output, int experts, float* y) {
+  if (tokens < 0 || top_k < 1 || hidden < 0 || output < 0 || experts < 1) {
+    return RR_ORACLE_BAD_SHAPE;
+  }
   for (int t = 0; t < tokens; ++t) {
     for (int c = 0; c < output; ++c) {
       float combined = 0.0f;
-      for (int k = 0; k < 2; ++k) {
-        const size_t r = (size_t)t * 2 + k;
+      for (int k = 0; k < top_k; ++k) {
+        const size_t r = (size_t)t * top_k + k;
         const int e = ids[r];
         if (e < 0 || e >= experts) return RR_ORACLE_ID_RANGE;
         float projection = 0.0f;
@@ -325,4 +332,11 @@ int rr_oracle_chain_output_f32(const float* x, const float* expert_w, const int3
     }
   }
   return RR_ORACLE_OK;
+}
+
+int rr_oracle_chain_output_f32(const float* x, const float* expert_w, const int32_t* ids,
+                               const float* weights, int tokens, int hidden, int output,
+                               int experts, float* y) {
+  return rr_oracle_route_chain_output_f32(x, expert_w, ids, weights, tokens, 2, hidden, output,
+                                          experts, y);
 }

@@ -44,6 +44,8 @@ from raggedroute_b200.ops import (  # noqa: F401
     chain_from_logits,
     chain_workspace_size,
     ChainBuffers,
+    RouteChainBuffers,
+    chain_from_route_ids,
     HostChain,
     kernel_launch_count,
     grouped_gemm_engine,
@@ -52,5 +54,6 @@ from raggedroute_b200.ops import (  # noqa: F401
 __all__ = [
     "dense_gemm", "topk_gate", "histogram", "exclusive_scan", "histogram_exclusive_scan",
     "token_permute", "grouped_gemm", "unpermute", "chain_from_tokens", "chain_from_logits",
+    "chain_from_route_ids",
     "HostChain", "Context", "RaggedRouteError", "StatusCode", "lib",
 ]

@@ -712,6 +712,72 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
                             args.tokens, args.hidden, args.experts, args.output, context);
 }
 
+std::size_t get_route_chain_workspace_size(int tokens, int top_k, int experts) noexcept {
+  if (tokens <= 0 || top_k <= 0 || experts <= 0) return 0;
+  return rrb::permute_workspace_bytes(tokens, experts, top_k);
+}
+
+// Post-route chain: benchmarks/adapters/postroute_chain_adapter.cpp:240-354
+// (histogram + scan, token_permute with sorted_route, grouped GEMM,
+// unpermute) with the B200 kernels. top_k in [1, 8] (the reference's suite
+// runs 2, 4 and 8); route ids outside [0, E) are outside the contract and
+// are skipped by every stage.
+Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
+                            const RuntimeContext& context) noexcept {
+  if (args.top_k < 1 || args.top_k > 8 || args.top_k > args.experts) {
+    return detail::invalid_argument("chain_from_route_ids requires 1<=top_k<=min(8,E)");
+  }
+  if (args.tokens < 0 || args.hidden < 0 || args.output < 0 || args.experts < 2 ||
+      args.experts > kMaxExperts) {
+    return detail::invalid_argument("chain requires T,K,N>=0 and 2<=E<=1024");
+  }
+  const long long routes = static_cast<long long>(args.tokens) * args.top_k;
+  if (routes > std::numeric_limits<int>::max() ||
+      routes * std::max(args.hidden, args.output) > std::numeric_limits<int>::max() * 4LL) {
+    return detail::invalid_argument("chain tensor exceeds the supported size");
+  }
+  Status s = resolve_chain_architecture(context);
+  if (!s.ok()) return s;
+  const RouteChainBuffers& b = args.buffers;
+  if (b.counts == nullptr || b.offsets == nullptr) {
+    return detail::invalid_argument("chain received a null device buffer");
+  }
+  if (args.tokens > 0) {
+    if (args.expert_ids == nullptr || args.route_weights == nullptr ||
+        b.route_pos == nullptr || (args.hidden > 0 && (args.x == nullptr || b.x_permuted == nullptr)) ||
+        (args.output > 0 && (b.y == nullptr || b.y_permuted == nullptr)) ||
+        (args.hidden > 0 && args.output > 0 && args.expert_weights == nullptr)) {
+      return detail::invalid_argument("chain received a null device buffer");
+    }
+  }
+  const std::size_t need = get_route_chain_workspace_size(args.tokens, args.top_k, args.experts);
+  if (need > 0 && (context.workspace == nullptr || context.workspace_bytes < need)) {
+    return detail::make_status(StatusCode::kInsufficientWorkspace,
+                               "chain requires the queried workspace");
+  }
+  cudaStream_t stream = context.stream;
+  const int r = static_cast<int>(routes);
+  s = detail::cuda_status(rrb::launch_histogram_exclusive_scan(args.expert_ids, b.counts,
+                                                               b.offsets, r, args.experts, stream),
+                          "chain histogram_exclusive_scan launch failed");
+  if (!s.ok() || args.tokens == 0) return s;
+  s = detail::cuda_status(
+      rrb::launch_token_permute(args.x, args.expert_ids, b.offsets, b.x_permuted, b.route_pos,
+                                b.sorted_route, args.tokens, args.experts, args.top_k,
+                                args.hidden, context.workspace, stream),
+      "chain token_permute launch failed");
+  if (!s.ok() || args.output == 0) return s;
+  s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, args.expert_weights, b.offsets,
+                                                   b.y_permuted, args.experts, r, args.hidden,
+                                                   args.output, stream),
+                          "chain grouped_gemm launch failed");
+  if (!s.ok()) return s;
+  return detail::cuda_status(rrb::launch_unpermute(b.y_permuted, b.route_pos, args.route_weights,
+                                                   b.y, args.tokens, args.top_k, args.output,
+                                                   stream),
+                             "chain unpermute launch failed");
+}
+
 // ---- low-level launchers (include/raggedroute/baseline_ops.h:14-42) ----------
 
 namespace ops {
@@ -1030,6 +1096,31 @@ rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
   args.experts = experts;
   args.output = output;
   return to_c(raggedroute::chain_from_tokens(args, to_runtime(ctx)));
+}
+
+rr_status rr_chain_from_route_ids(const float* x, const int32_t* expert_ids,
+                                  const float* route_weights, const float* expert_weights,
+                                  int32_t* counts, int32_t* offsets, float* x_permuted,
+                                  int32_t* route_pos, int32_t* sorted_route, float* y_permuted,
+                                  float* y, int tokens, int top_k, int hidden, int experts,
+                                  int output, const rr_context* ctx) {
+  if (ctx == nullptr) return null_context();
+  raggedroute::ChainFromRouteIdsArgs args;
+  args.x = x;
+  args.expert_ids = expert_ids;
+  args.route_weights = route_weights;
+  args.expert_weights = expert_weights;
+  args.buffers = {counts, offsets, x_permuted, route_pos, sorted_route, y_permuted, y};
+  args.tokens = tokens;
+  args.top_k = top_k;
+  args.hidden = hidden;
+  args.experts = experts;
+  args.output = output;
+  return to_c(raggedroute::chain_from_route_ids(args, to_runtime(ctx)));
+}
+
+size_t rr_route_chain_workspace_size(int tokens, int top_k, int experts) {
+  return raggedroute::get_route_chain_workspace_size(tokens, top_k, experts);
 }
 
 rr_status rr_chain_from_logits(const float* logits, const float* x, const float* expert_weights,

@@ -219,6 +219,53 @@ def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights: tor
     return buf.y
 
 
+@dataclasses.dataclass
+class RouteChainBuffers:
+    """Caller-owned buffers of chain_from_route_ids (R = T * top_k routes)."""
+    counts: torch.Tensor
+    offsets: torch.Tensor
+    x_permuted: torch.Tensor
+    route_pos: torch.Tensor
+    sorted_route: torch.Tensor | None
+    y_permuted: torch.Tensor
+    y: torch.Tensor
+    workspace: torch.Tensor
+
+    @staticmethod
+    def allocate(tokens: int, top_k: int, hidden: int, experts: int, output: int,
+                 device: torch.device | str = "cuda",
+                 with_sorted_route: bool = True) -> "RouteChainBuffers":
+        f32, i32 = torch.float32, torch.int32
+        r = tokens * top_k
+        ws = max(1, int(lib().rr_route_chain_workspace_size(tokens, top_k, experts)))
+        return RouteChainBuffers(
+            counts=torch.empty(experts, dtype=i32, device=device),
+            offsets=torch.empty(experts + 1, dtype=i32, device=device),
+            x_permuted=torch.empty(r, hidden, dtype=f32, device=device),
+            route_pos=torch.empty(r, dtype=i32, device=device),
+            sorted_route=torch.empty(r, dtype=i32, device=device) if with_sorted_route else None,
+            y_permuted=torch.empty(r, output, dtype=f32, device=device),
+            y=torch.empty(tokens, output, dtype=f32, device=device),
+            workspace=torch.empty((ws + 255) // 256 * 256, dtype=torch.uint8, device=device),
+        )
+
+
+def chain_from_route_ids(x: torch.Tensor, expert_ids: torch.Tensor,
+                         route_weights: torch.Tensor, expert_weights: torch.Tensor,
+                         buf: RouteChainBuffers, ctx: Context | None = None) -> torch.Tensor:
+    """Post-route chain (benchmarks/adapters/postroute_chain_adapter.cpp:240-354):
+    expert_ids / route_weights [T, top_k] -> Y [T, N]."""
+    tokens, hidden = x.shape
+    top_k = expert_ids.shape[1]
+    experts, _, output = expert_weights.shape
+    check(lib().rr_chain_from_route_ids(
+        _ptr(x), _ptr(expert_ids), _ptr(route_weights), _ptr(expert_weights), _ptr(buf.counts),
+        _ptr(buf.offsets), _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.sorted_route),
+        _ptr(buf.y_permuted), _ptr(buf.y), tokens, top_k, hidden, experts, output,
+        _ctx(ctx, buf.workspace)), "chain_from_route_ids")
+    return buf.y
+
+
 class HostChain:
     """chain_from_tokens over host memory (rr_chain_from_tokens_host): chunks
     of `chunk_tokens` stream host -> device, through the chain and back on

@@ -260,3 +260,30 @@ def test_golden_permute(oracle):
     assert np.array_equal(pos, g["route_pos"])
     assert np.array_equal(sr, g["sorted_route"])
     assert np.array_equal(cur, g["cursors"])
+
+
+@pytest.mark.parametrize("top_k", [1, 2, 4, 8])
+@pytest.mark.parametrize("dist", ["uniform", "zipf", "duplicate_route", "single_hot",
+                                  "round_robin"])
+def test_route_chain_oracle_matches_reference_formula(oracle, top_k, dist):
+    """The post-route chain composed from the stage oracles equals the
+    reference's float restatement (postroute_chain_adapter.cpp:654-675)
+    within its tolerance (atol 1e-4, rtol 4e-5*K*top_k), and its routing
+    metadata is the stable bijection onto expert segments."""
+    from route_ids import make_route_ids, make_route_weights
+    t, k, e, n = 17, 64, 16, 64
+    rng = np.random.default_rng(top_k)
+    x = rng.uniform(-1, 1, (t, k)).astype(np.float32)
+    w = rng.normal(0, 1 / 8, (e, k, n)).astype(np.float32)
+    ids = make_route_ids(t, top_k, e, dist, 1.4, seed=top_k)
+    rw = make_route_weights(t, top_k, seed=top_k)
+    counts, offsets, xp, pos, sr, y = oracle.route_chain_f64(x, w, ids, rw, e)
+    ref = oracle.route_chain_output_f32(x, w, ids, rw)
+    ok, _, _ = oracle.compare_floating(y.astype(np.float32), ref, 1e-4, 4e-5 * k * top_k)
+    assert ok
+    flat = ids.reshape(-1)
+    assert np.array_equal(counts, np.bincount(flat, minlength=e))
+    for r in range(flat.size):
+        assert offsets[flat[r]] <= pos[r] < offsets[flat[r] + 1]
+        assert sr[pos[r]] == r
+        assert np.array_equal(xp[pos[r]], x[r // top_k])
