@@ -10,14 +10,20 @@ expert weights 2.95 GB), so no L2 flush is needed between steps.
 One step = the seven-stage chain over one batch: dense_gemm -> topk_gate ->
 histogram_exclusive_scan -> token_permute -> grouped_gemm -> unpermute, all
 through libraggedroute_b200's C ABI on one stream. `value` is device-timed
-(CUDA events, inputs resident in HBM, max over ranks); `e2e` is the same chain
-through rr_chain_from_tokens with the step's X copied in from pinned host
-memory and Y copied back inside the timed region.
+(CUDA events, inputs resident in HBM, max over ranks); `e2e` is the same
+metric with X in pinned host memory and Y returned to host memory every step
+(one GPU: rr_chain_from_tokens_host, which overlaps the PCIe copies of
+token chunks with the chain; expert parallelism: copy in, EP step, copy out).
+Extra keys on one GPU: `cold_scrub` (the C5 step with 256 MiB written to
+flush L2 before every step) and `small_configs` (C1 chain_from_tokens and C2
+chain_from_logits latency, eager and replayed from a captured CUDA graph).
 
 Multi-GPU (torchrun): expert parallelism -- every rank runs its own T=65536
-tokens (weak scaling) and owns E/N experts (LPT placement on the expected
-router load, experts relabelled contiguously); dispatch and combine are NCCL
-all-to-all-v inside libraggedroute_b200 (rr_ep_chain_from_tokens).
+tokens (weak scaling); hot experts are replicated into virtual experts placed
+by LPT on the measured loads, and rows move through the peer-memory
+transport of rr_ep_chain_from_tokens (dispatch fused into the permute,
+combine fused into the grouped GEMM epilogue; NCCL carries only the counts
+and two one-word barriers per step).
 --impl reference: times the reference's own CPU implementation of the path
 (oracle/_ref, compiled from the reference sources) on bounded token samples of
 the same workload, with every host thread; rank 0 only.
@@ -25,6 +31,7 @@ the same workload, with every host thread; rank 0 only.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 
 import numpy as np
@@ -52,6 +59,8 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=None, help="override T per GPU (testing)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the cold-L2 C5 pass and the C1/C2 eager-vs-graph latencies")
     ap.add_argument("--e2e-chunk", type=int, default=8192,
                     help="tokens per chunk of the host-memory chain (e2e, one GPU)")
     ap.add_argument("--ep-transport", choices=["auto", "peer", "nccl"], default="auto",
@@ -381,6 +390,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if ep is not None:
         ep.close()
+    extras = {}
+    if world == 1 and not args.no_extras:
+        cold = cold_scrub_step(torch, rr, stream, step, max(3, args.steps))
+        cold["tokens_per_s"] = round(tokens / (cold["ms_per_step"] * 1e-3), 1)
+        extras["cold_scrub"] = cold
+        extras["small_configs"] = small_config_latency(torch, rr, device)
     if rank != 0:
         return None
 
@@ -430,6 +445,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "gpu_launches": int(launches),
         "e2e": e2e,
     }
+    line.update(extras)
     if ep_info is not None:
         line["ep"] = ep_info
         line["roofline"]["note"] = ("per-GPU stage pass of the single-GPU chain on rank 0's "
@@ -457,6 +473,66 @@ def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) 
         times.append(evs[idx].elapsed_time(evs[idx + 1]))
     return {"stage": args.only_stage, "tokens": tokens, "ms": statistics.mean(times),
             "ms_min": min(times)}
+
+
+def small_config_latency(torch, rr, device, iters: int = 200) -> dict:
+    """C1 (chain_from_tokens) and C2 (chain_from_logits) per-call latency,
+    launched eagerly and as a captured CUDA graph (rr_graph_*), CUDA events
+    over `iters` back-to-back calls on one stream."""
+    from raggedroute_b200.workloads import C1, C2, c1_inputs, c2_inputs
+    out = {}
+    for cfg, make, logits_mode in ((C1, c1_inputs, False), (C2, c2_inputs, True)):
+        inp = make(device)
+        t, k, e, n = cfg["tokens"], cfg["hidden"], cfg["experts"], cfg["output"]
+        buf = rr.ChainBuffers.allocate(t, k, e, n, device)
+        stream = torch.cuda.Stream(device)
+        if logits_mode:
+            call = lambda ctx: rr.chain_from_logits(inp.logits, inp.x, inp.expert_w, buf,  # noqa: E731
+                                                    ctx=ctx)
+        else:
+            call = lambda ctx: rr.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf,  # noqa: E731
+                                                    logit_bias=inp.logit_bias, ctx=ctx)
+        ctx = rr.Context(stream=stream.cuda_stream)
+        for _ in range(20):
+            call(ctx)
+        graph = rr.Graph.capture(call, stream)
+        res = {}
+        for mode in ("eager", "graph"):
+            for _ in range(20):
+                call(ctx) if mode == "eager" else graph.launch(stream)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(iters):
+                call(ctx) if mode == "eager" else graph.launch(stream)
+            b.record(stream)
+            b.synchronize()
+            res[mode + "_us"] = round(a.elapsed_time(b) * 1e3 / iters, 2)
+        res["graph_tokens_per_s"] = round(t / (res["graph_us"] * 1e-6), 1)
+        res["graph_nodes"] = graph.nodes
+        graph.close()
+        out[cfg["name"]] = res
+    return out
+
+
+def cold_scrub_step(torch, rr, stream, step, steps: int) -> dict:
+    """The C5 chain with the L2 scrubbed (256 MiB written) before every step;
+    only the chain is inside the timed events."""
+    scrub = torch.empty(64 << 20, dtype=torch.int32, device=stream.device)
+    ctx_s = rr.Context(stream=stream.cuda_stream)
+    total = 0.0
+    for _ in range(steps):
+        rr.lib().rr_launch_cache_scrub(ctypes.c_void_p(scrub.data_ptr()), scrub.numel(),
+                                       ctypes.c_void_p(ctx_s.stream))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            step()
+            b.record(stream)
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return {"ms_per_step": round(total / steps, 3), "scrub_bytes": scrub.numel() * 4}
 
 
 # ---------------------------------------------------------------------------
@@ -506,9 +582,17 @@ def cpu_baseline(inp, steps: int = 1, sample_tokens: int = 32) -> dict:
     for _ in range(steps):
         _run_ref_chain(ref, x, wr, bias, we, threads)
     dt = (time.perf_counter() - t0) / steps
+    # The reference oracle as shipped is single-threaded: the same chain on
+    # one host thread, on a smaller sample.
+    one = max(1, sample_tokens // 8)
+    t1 = time.perf_counter()
+    _run_ref_chain(ref, x[:one].contiguous(), wr, bias, we, 1)
+    dt1 = time.perf_counter() - t1
     return {"value": sample_tokens / dt, "unit": UNIT, "cores": threads, "kind": "reference",
             "sample": f"{sample_tokens} tokens of C5 per step through the reference's CPU "
-                      f"functions (oracle/_ref), {threads} host threads"}
+                      f"functions (oracle/_ref), {threads} host threads",
+            "one_core": {"value": one / dt1, "unit": UNIT, "cores": 1,
+                         "sample": f"{one} tokens of C5, 1 host thread"}}
 
 
 C5_TOKENS = 65536

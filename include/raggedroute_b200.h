@@ -196,6 +196,21 @@ rr_status rr_chain_from_route_ids(const float* x, const int32_t* expert_ids,
                                   int output, const rr_context* ctx);
 size_t rr_route_chain_workspace_size(int tokens, int top_k, int experts);
 
+/* ---- CUDA-graph capture (new: no reference counterpart) -------------------
+ * Every rr_* operator and chain above enqueues without host synchronisation,
+ * allocation or host reads of device data, and the grouped GEMM reads its
+ * tile schedule from offsets on the device, so a sequence of calls can be
+ * captured once and replayed with one launch: write new inputs into the
+ * captured buffers (any routing, same shapes) and call rr_graph_launch.
+ * Capture runs on a created stream in relaxed mode. The expert-parallel and
+ * host-memory chains are not capturable (they synchronise with the host). */
+typedef struct rr_graph rr_graph;
+rr_status rr_graph_capture_begin(void* stream /* cudaStream_t, not NULL */);
+rr_status rr_graph_capture_end(void* stream, rr_graph** out);
+rr_status rr_graph_launch(rr_graph* graph, void* stream);
+int rr_graph_node_count(const rr_graph* graph);
+rr_status rr_graph_destroy(rr_graph* graph);
+
 /* ---- chain over host memory (new: no reference counterpart) --------------
  * chain_from_tokens for tokens that live in host memory. The batch is cut
  * into chunks of chunk_tokens; each chunk's X is copied in on one copy

@@ -47,6 +47,7 @@ from raggedroute_b200.ops import (  # noqa: F401
     RouteChainBuffers,
     chain_from_route_ids,
     HostChain,
+    Graph,
     kernel_launch_count,
     grouped_gemm_engine,
 )

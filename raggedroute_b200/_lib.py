@@ -109,6 +109,11 @@ SIGNATURES = {
     "rr_grouped_gemm_engine": (_I, [_P, _P, _P, _I, _I]),
     "rr_tf32_rounding_selfcheck": (RRStatus, [_P, ctypes.c_int64, _P, _P]),
     "rr_version": (ctypes.c_char_p, []),
+    "rr_graph_capture_begin": (RRStatus, [_P]),
+    "rr_graph_capture_end": (RRStatus, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "rr_graph_launch": (RRStatus, [_P, _P]),
+    "rr_graph_node_count": (_I, [_P]),
+    "rr_graph_destroy": (RRStatus, [_P]),
     "rr_host_chain_create": (RRStatus, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
     "rr_host_chain_destroy": (RRStatus, [_P]),
     "rr_chain_from_tokens_host": (RRStatus, [_P] * 8 + [_I, _CTX]),

@@ -266,6 +266,52 @@ def chain_from_route_ids(x: torch.Tensor, expert_ids: torch.Tensor,
     return buf.y
 
 
+class Graph:
+    """A captured sequence of operator calls (rr_graph_*), replayed with one
+    launch. Usage::
+
+        g = Graph.capture(lambda ctx: chain_from_tokens(x, wr, we, buf, ctx=ctx), stream)
+        x.copy_(next_tokens); g.launch(stream)
+
+    `stream` is a torch.cuda.Stream (not the default stream); the callable
+    receives the Context to pass to every call it makes."""
+
+    def __init__(self, handle: ctypes.c_void_p):
+        self._h = handle
+
+    @staticmethod
+    def capture(fn, stream: torch.cuda.Stream) -> "Graph":
+        ctx = Context(stream=stream.cuda_stream)
+        check(lib().rr_graph_capture_begin(ctypes.c_void_p(stream.cuda_stream)),
+              "rr_graph_capture_begin")
+        try:
+            fn(ctx)
+        finally:
+            h = ctypes.c_void_p()
+            st = lib().rr_graph_capture_end(ctypes.c_void_p(stream.cuda_stream), ctypes.byref(h))
+        check(st, "rr_graph_capture_end")
+        return Graph(h)
+
+    @property
+    def nodes(self) -> int:
+        return int(lib().rr_graph_node_count(self._h))
+
+    def launch(self, stream: torch.cuda.Stream) -> None:
+        check(lib().rr_graph_launch(self._h, ctypes.c_void_p(stream.cuda_stream)),
+              "rr_graph_launch")
+
+    def close(self) -> None:
+        if self._h:
+            lib().rr_graph_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
 class HostChain:
     """chain_from_tokens over host memory (rr_chain_from_tokens_host): chunks
     of `chunk_tokens` stream host -> device, through the chain and back on
