@@ -196,6 +196,28 @@ rr_status rr_chain_from_route_ids(const float* x, const int32_t* expert_ids,
                                   int output, const rr_context* ctx);
 size_t rr_route_chain_workspace_size(int tokens, int top_k, int experts);
 
+/* ---- route traces (include/raggedroute/benchmark/adapter_utils.h:250-322) --
+ * Reads frame `frame` of a "raggedroute.route_trace.v1" text file (.rrtrace)
+ * with the reference loader's validation (header, portable ids, source kind,
+ * ids in [0, E) and distinct within a token, no trailing data; E <= 1024
+ * here). expert_ids (host, may be NULL to read the header only) receives
+ * tokens*top_k ids. */
+typedef struct rr_route_trace_info {
+  int32_t tokens;
+  int32_t experts;
+  int32_t top_k;
+  int32_t frame_count;
+  char trace_id[128];
+  char source_kind[32];
+  char frame_id[128];
+} rr_route_trace_info;
+rr_status rr_route_trace_read(const char* path, int frame, rr_route_trace_info* info,
+                              int32_t* expert_ids, int64_t ids_capacity);
+/* Host logits [tokens, experts] that make the top-2 gate pick a top-2
+ * frame's ids in order (benchmarks/adapters/chain_adapter.cpp:222-228). */
+rr_status rr_route_trace_logits(const int32_t* expert_ids, int tokens, int experts,
+                                float* logits);
+
 /* ---- CUDA-graph capture (new: no reference counterpart) -------------------
  * Every rr_* operator and chain above enqueues without host synchronisation,
  * allocation or host reads of device data, and the grouped GEMM reads its

@@ -50,6 +50,13 @@ class RRContext(ctypes.Structure):
                 ("kernel_family", ctypes.c_int32), ("implementation_id", ctypes.c_uint32)]
 
 
+class RRRouteTraceInfo(ctypes.Structure):
+    _fields_ = [("tokens", ctypes.c_int32), ("experts", ctypes.c_int32),
+                ("top_k", ctypes.c_int32), ("frame_count", ctypes.c_int32),
+                ("trace_id", ctypes.c_char * 128), ("source_kind", ctypes.c_char * 32),
+                ("frame_id", ctypes.c_char * 128)]
+
+
 @dataclasses.dataclass
 class Context:
     """Mirror of raggedroute::RuntimeContext plus the KernelSelection."""
@@ -109,6 +116,9 @@ SIGNATURES = {
     "rr_grouped_gemm_engine": (_I, [_P, _P, _P, _I, _I]),
     "rr_tf32_rounding_selfcheck": (RRStatus, [_P, ctypes.c_int64, _P, _P]),
     "rr_version": (ctypes.c_char_p, []),
+    "rr_route_trace_read": (RRStatus, [ctypes.c_char_p, _I, ctypes.POINTER(RRRouteTraceInfo),
+                                          _P, ctypes.c_int64]),
+    "rr_route_trace_logits": (RRStatus, [_P, _I, _I, _P]),
     "rr_graph_capture_begin": (RRStatus, [_P]),
     "rr_graph_capture_end": (RRStatus, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "rr_graph_launch": (RRStatus, [_P, _P]),

@@ -67,3 +67,36 @@ def test_route_chain_rejects_bad_top_k(rrlib, cuda):
         buf = rrlib.RouteChainBuffers.allocate(4, top_k, 8, 4, 8, cuda)
         with pytest.raises(RaggedRouteError):
             rrlib.chain_from_route_ids(x, ids, rw, w, buf)
+
+
+@pytest.mark.parametrize("frame", [0, 1, 2])
+def test_route_trace_frames_through_both_chains(rrlib, oracle, cuda, frame):
+    """A committed route-trace frame drives chain_from_logits (through the
+    trace logits, chain_adapter.cpp:207-228) and chain_from_route_ids; both
+    route exactly the frame's ids and match the oracle."""
+    import os
+    from raggedroute_b200.route_trace import load_route_trace_frame, trace_logits
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                        "fixture_t24_e16_top2.rrtrace")
+    fr = load_route_trace_frame(path, frame)
+    t, e, k, n = fr.tokens, fr.experts, 64, 32
+    rng = np.random.default_rng(frame)
+    x = rng.uniform(-1, 1, (t, k)).astype(np.float32)
+    w = rng.normal(0, 1 / 8, (e, k, n)).astype(np.float32)
+    logits = trace_logits(fr.expert_ids, e)
+    buf = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    rrlib.chain_from_logits(torch.from_numpy(logits).to(cuda), torch.from_numpy(x).to(cuda),
+                            torch.from_numpy(w).to(cuda), buf)
+    torch.cuda.synchronize()
+    assert np.array_equal(buf.expert_ids.cpu().numpy(), fr.expert_ids)
+    ids, rw = oracle.top2_f32(logits)
+    _, _, _, _, _, y = oracle.route_chain_f64(x, w, ids.reshape(-1, 2), rw.reshape(-1, 2), e)
+    ok, _, _ = oracle.compare_floating(buf.y.cpu().numpy(), y.astype(np.float32), 1e-4, 4e-5 * k * 2)
+    assert ok
+    # The same frame as route ids.
+    rbuf = rrlib.RouteChainBuffers.allocate(t, 2, k, e, n, cuda)
+    rrlib.chain_from_route_ids(torch.from_numpy(x).to(cuda), torch.from_numpy(fr.expert_ids).to(cuda),
+                               torch.from_numpy(rw.reshape(-1, 2)).to(cuda),
+                               torch.from_numpy(w).to(cuda), rbuf)
+    torch.cuda.synchronize()
+    assert torch.equal(rbuf.y.view(torch.int32), buf.y.view(torch.int32))
