@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--tokens", type=int, default=None, help="override T per GPU (testing)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gather-rows", action="store_true",
+                    help="time the chain with the row-gathering grouped GEMM (no x_permuted)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the cold-L2 C5 pass and the C1/C2 eager-vs-graph latencies")
     ap.add_argument("--e2e-chunk", type=int, default=8192,
@@ -249,6 +251,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     stage_names = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
                    "grouped_gemm", "unpermute"]
+    # --gather-rows: the permute only ranks (route_pos, sorted_route) and the
+    # grouped GEMM gathers its rows from X; x_permuted is never written.
+    sorted_route = torch.empty(routes, dtype=torch.int32, device=device)
 
     def step(events=None, only=None):
         """One chain step, stage by stage; `only` runs just that stage index."""
@@ -258,11 +263,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                                         buf.route_weights, tokens, e, ctx=ctx),
             lambda: rr.histogram_exclusive_scan(buf.expert_ids, buf.counts, buf.offsets, routes,
                                                 e, ctx=ctx),
-            lambda: rr.token_permute(inp.x, buf.expert_ids, buf.offsets, buf.x_permuted,
-                                     buf.route_pos, None, tokens, e, 2, k, buf.workspace,
-                                     ctx=ctx),
-            lambda: rr.grouped_gemm(buf.x_permuted, inp.expert_w, buf.offsets, buf.y_permuted,
-                                    e, k, n, routes, ctx=ctx),
+            (lambda: rr.token_permute(inp.x, buf.expert_ids, buf.offsets, buf.x_permuted,
+                                      buf.route_pos, None, tokens, e, 2, k, buf.workspace,
+                                      ctx=ctx)) if not args.gather_rows else
+            (lambda: rr.token_permute(None, buf.expert_ids, buf.offsets, None, buf.route_pos,
+                                      sorted_route, tokens, e, 2, 0, buf.workspace, ctx=ctx)),
+            (lambda: rr.grouped_gemm(buf.x_permuted, inp.expert_w, buf.offsets, buf.y_permuted,
+                                     e, k, n, routes, ctx=ctx)) if not args.gather_rows else
+            (lambda: rr.grouped_gemm_gather(inp.x, sorted_route, 2, inp.expert_w, buf.offsets,
+                                            buf.y_permuted, routes, ctx=ctx)),
             lambda: rr.unpermute(buf.y_permuted, buf.route_pos, buf.route_weights, buf.y, tokens,
                                  2, n, ctx=ctx),
         ]
@@ -414,6 +423,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "grouped_gemm": 4.0 * (routes * k + e * k * n + routes * n),
         "unpermute": 4.0 * routes * n + 8.0 * routes + 4.0 * tokens * n,
     }
+    if args.gather_rows:
+        # ranks only: ids read, route_pos and sorted_route written
+        stage_bytes["token_permute"] = 12.0 * routes + 4.0 * (e + 1)
     stages = {}
     for nm in stage_names:
         ms = stage_ms[nm]

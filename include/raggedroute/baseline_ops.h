@@ -42,4 +42,14 @@ cudaError_t launch_unpermute_naive(const float* y_permuted, const std::int32_t* 
 cudaError_t launch_cache_scrub(std::uint32_t* buffer, std::size_t elements,
                                cudaStream_t caller_stream);
 
+// The reference's research entry point of its post-route gather chain
+// (src/grouped_gemm/cuda_candidate/grouped_optimized_internal.h:105-109),
+// same signature so its adapters link unchanged: row r of segment e is
+// x[sorted_route[r] / top_k] . W[e]. The workspace is accepted and unused.
+cudaError_t launch_grouped_gemm_sm86_fp32_gather_v1(
+    const float* x, const std::int32_t* sorted_route, int top_k, const float* expert_weights,
+    const std::int32_t* offsets, float* y_permuted, int experts, int hidden, int output,
+    int max_expert_tokens, void* workspace, std::size_t workspace_bytes,
+    cudaStream_t caller_stream);
+
 }  // namespace raggedroute::ops

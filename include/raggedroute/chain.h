@@ -34,6 +34,9 @@ struct ChainFromTokensArgs {
   int hidden = 0;
   int experts = 0;
   int output = 0;
+  // The grouped GEMM gathers its rows from x through sorted_route (kept in
+  // the workspace); buffers.x_permuted is not written and may be null.
+  bool gather_rows = false;
 };
 
 struct ChainFromLogitsArgs {
@@ -45,6 +48,7 @@ struct ChainFromLogitsArgs {
   int hidden = 0;
   int experts = 0;
   int output = 0;
+  bool gather_rows = false;  // as in ChainFromTokensArgs
 };
 
 // Buffers of the post-route chain (top_k routes per token, R = T * top_k).
@@ -72,9 +76,13 @@ struct ChainFromRouteIdsArgs {
   int hidden = 0;
   int experts = 0;
   int output = 0;
+  // The grouped GEMM gathers its rows from x through buffers.sorted_route
+  // (then required); buffers.x_permuted is not written and may be null.
+  bool gather_rows = false;
 };
 
-// Workspace (bytes) for either chain: the token_permute workspace at 2T routes.
+// Workspace (bytes) for either chain: the token_permute workspace at 2T
+// routes plus room for sorted_route [2T] (used when gather_rows is set).
 std::size_t get_chain_workspace_size(int tokens, int hidden, int experts, int output) noexcept;
 
 Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& context) noexcept;

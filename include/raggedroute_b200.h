@@ -158,6 +158,14 @@ size_t rr_unpermute_workspace_size(int tokens, int top_k, int output);
 
 /* ---- L3 chains (benchmarks/adapters/chain_adapter.cpp:263-467) ----------- */
 
+/* Chains read ctx->implementation_id: 0 (default) materialises x_permuted;
+ * RR_CHAIN_IMPL_GATHER_ROWS has the grouped GEMM gather its rows from x
+ * through sorted_route (the permute only ranks), so x_permuted is not
+ * written (may be NULL) and the permute's row copy and the GEMM's re-read
+ * of it disappear; outputs are bit-identical. Any other id is
+ * RR_UNSUPPORTED_KERNEL_VARIANT. */
+#define RR_CHAIN_IMPL_GATHER_ROWS 1u
+
 /* chain_from_tokens: dense_gemm -> topk_gate -> histogram_exclusive_scan ->
  * token_permute -> grouped_gemm -> unpermute on ctx->stream, no host sync.
  * Intermediate buffers are caller-owned and are left holding each stage's
@@ -174,6 +182,15 @@ rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
                                int hidden, int experts, int output, const rr_context* ctx);
 
 /* chain_from_logits: the same chain starting from caller-provided logits. */
+/* Grouped GEMM with row gather (the reference's research entry point
+ * launch_grouped_gemm_sm86_fp32_gather_v1, src/grouped_gemm/cuda_candidate/
+ * grouped_optimized_internal.h:105-109): row r of segment e is
+ * x[sorted_route[r] / top_k] . W[e]; y_permuted [R, N]. */
+rr_status rr_grouped_gemm_gather(const float* x, const int32_t* sorted_route, int top_k,
+                                 const float* expert_weights, const int32_t* offsets,
+                                 float* y_permuted, int route_pairs, int hidden, int experts,
+                                 int output, const rr_context* ctx);
+
 rr_status rr_chain_from_logits(const float* logits, const float* x, const float* expert_weights,
                                int32_t* expert_ids, float* route_weights, int32_t* counts,
                                int32_t* offsets, float* x_permuted, int32_t* route_pos,

@@ -39,6 +39,7 @@ from raggedroute_b200.ops import (  # noqa: F401
     token_permute,
     token_permute_workspace_size,
     grouped_gemm,
+    grouped_gemm_gather,
     unpermute,
     chain_from_tokens,
     chain_from_logits,

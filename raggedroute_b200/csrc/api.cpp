@@ -584,9 +584,16 @@ Status unpermute(const UnpermuteArgs& args, const RuntimeContext& context) noexc
 
 // ---- L3 chains (benchmarks/adapters/chain_adapter.cpp:263-467) --------------
 
+// Permute workspace, then (256-byte aligned) room for sorted_route [2T],
+// which the row-gathering chains keep there.
+std::size_t chain_sorted_route_offset(int tokens, int experts) noexcept {
+  const std::size_t p = rrb::permute_workspace_bytes(tokens, experts, 2);
+  return (p + 255) & ~static_cast<std::size_t>(255);
+}
+
 std::size_t get_chain_workspace_size(int tokens, int, int experts, int) noexcept {
   if (tokens <= 0 || experts <= 0) return 0;
-  return rrb::permute_workspace_bytes(tokens, experts, 2);
+  return chain_sorted_route_offset(tokens, experts) + static_cast<std::size_t>(tokens) * 2 * 4;
 }
 
 namespace {
@@ -607,7 +614,8 @@ Status validate_chain_shape(int tokens, int hidden, int experts, int output) noe
 
 Status chain_after_logits(const float* logits, const float* logit_bias, const float* x,
                           const float* expert_w, const ChainBuffers& b, int tokens, int hidden,
-                          int experts, int output, const RuntimeContext& context) noexcept {
+                          int experts, int output, const RuntimeContext& context,
+                          bool gather_rows) noexcept {
   cudaStream_t stream = context.stream;
   Status s = detail::cuda_status(
       rrb::launch_topk_gate(logits, logit_bias, b.expert_ids, b.route_weights, tokens, experts,
@@ -619,15 +627,32 @@ Status chain_after_logits(const float* logits, const float* logit_bias, const fl
                                                                routes, experts, stream),
                           "chain histogram_exclusive_scan launch failed");
   if (!s.ok()) return s;
-  s = detail::cuda_status(
-      rrb::launch_token_permute(x, b.expert_ids, b.offsets, b.x_permuted, b.route_pos, nullptr,
-                                tokens, experts, 2, hidden, context.workspace, stream),
-      "chain token_permute launch failed");
-  if (!s.ok()) return s;
-  s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, expert_w, b.offsets,
-                                                   b.y_permuted, experts, routes, hidden, output,
-                                                   stream),
-                          "chain grouped_gemm launch failed");
+  if (gather_rows) {
+    // Ranks only (no row copy); the grouped GEMM gathers its rows from x
+    // through sorted_route, kept in the workspace.
+    int32_t* sorted_route = reinterpret_cast<int32_t*>(
+        static_cast<char*>(context.workspace) + chain_sorted_route_offset(tokens, experts));
+    s = detail::cuda_status(
+        rrb::launch_token_permute(x, b.expert_ids, b.offsets, nullptr, b.route_pos, sorted_route,
+                                  tokens, experts, 2, 0, context.workspace, stream),
+        "chain token_permute launch failed");
+    if (!s.ok()) return s;
+    const rrb::RowGather gather{x, sorted_route, 2};
+    s = detail::cuda_status(rrb::launch_grouped_gemm(x, expert_w, b.offsets, b.y_permuted,
+                                                     experts, routes, hidden, output, stream, 0,
+                                                     nullptr, &gather),
+                            "chain grouped_gemm launch failed");
+  } else {
+    s = detail::cuda_status(
+        rrb::launch_token_permute(x, b.expert_ids, b.offsets, b.x_permuted, b.route_pos, nullptr,
+                                  tokens, experts, 2, hidden, context.workspace, stream),
+        "chain token_permute launch failed");
+    if (!s.ok()) return s;
+    s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, expert_w, b.offsets,
+                                                     b.y_permuted, experts, routes, hidden,
+                                                     output, stream),
+                            "chain grouped_gemm launch failed");
+  }
   if (!s.ok()) return s;
   return detail::cuda_status(rrb::launch_unpermute(b.y_permuted, b.route_pos, b.route_weights,
                                                    b.y, tokens, 2, output, stream),
@@ -635,11 +660,11 @@ Status chain_after_logits(const float* logits, const float* logit_bias, const fl
 }
 
 Status validate_chain_buffers(const ChainBuffers& b, bool need_logits, int hidden,
-                              int output) noexcept {
+                              int output, bool gather_rows) noexcept {
   if ((need_logits && b.logits == nullptr) || b.expert_ids == nullptr ||
       b.route_weights == nullptr || b.counts == nullptr || b.offsets == nullptr ||
       b.route_pos == nullptr || (output > 0 && (b.y == nullptr || b.y_permuted == nullptr)) ||
-      (hidden > 0 && b.x_permuted == nullptr)) {
+      (hidden > 0 && !gather_rows && b.x_permuted == nullptr)) {
     return detail::invalid_argument("chain received a null device buffer");
   }
   return success_status();
@@ -658,6 +683,12 @@ Status resolve_chain_architecture(const RuntimeContext& context) noexcept {
 
 }  // namespace
 
+// Architecture check shared by the library's own (non-reference) entry
+// points: B200 (CC 10.0) only.
+Status detail_resolve_sm100(const RuntimeContext& context) noexcept {
+  return resolve_chain_architecture(context);
+}
+
 Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& context) noexcept {
   Status s = validate_chain_shape(args.tokens, args.hidden, args.experts, args.output);
   if (!s.ok()) return s;
@@ -671,7 +702,7 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
   if (args.expert_weights == nullptr && args.hidden > 0 && args.output > 0) {
     return detail::invalid_argument("chain expert weights are null");
   }
-  s = validate_chain_buffers(args.buffers, true, args.hidden, args.output);
+  s = validate_chain_buffers(args.buffers, true, args.hidden, args.output, args.gather_rows);
   if (!s.ok()) return s;
   const std::size_t need = get_chain_workspace_size(args.tokens, args.hidden, args.experts,
                                                     args.output);
@@ -686,7 +717,7 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
   if (!s.ok()) return s;
   return chain_after_logits(args.buffers.logits, args.logit_bias, args.x, args.expert_weights,
                             args.buffers, args.tokens, args.hidden, args.experts, args.output,
-                            context);
+                            context, args.gather_rows);
 }
 
 Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& context) noexcept {
@@ -700,7 +731,7 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
   if (args.expert_weights == nullptr && args.hidden > 0 && args.output > 0) {
     return detail::invalid_argument("chain expert weights are null");
   }
-  s = validate_chain_buffers(args.buffers, false, args.hidden, args.output);
+  s = validate_chain_buffers(args.buffers, false, args.hidden, args.output, args.gather_rows);
   if (!s.ok()) return s;
   const std::size_t need = get_chain_workspace_size(args.tokens, args.hidden, args.experts,
                                                     args.output);
@@ -709,7 +740,8 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
                                "chain requires the queried workspace");
   }
   return chain_after_logits(args.logits, nullptr, args.x, args.expert_weights, args.buffers,
-                            args.tokens, args.hidden, args.experts, args.output, context);
+                            args.tokens, args.hidden, args.experts, args.output, context,
+                            args.gather_rows);
 }
 
 std::size_t get_route_chain_workspace_size(int tokens, int top_k, int experts) noexcept {
@@ -744,7 +776,10 @@ Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
   }
   if (args.tokens > 0) {
     if (args.expert_ids == nullptr || args.route_weights == nullptr ||
-        b.route_pos == nullptr || (args.hidden > 0 && (args.x == nullptr || b.x_permuted == nullptr)) ||
+        b.route_pos == nullptr ||
+        (args.hidden > 0 &&
+         (args.x == nullptr || (!args.gather_rows && b.x_permuted == nullptr) ||
+          (args.gather_rows && b.sorted_route == nullptr))) ||
         (args.output > 0 && (b.y == nullptr || b.y_permuted == nullptr)) ||
         (args.hidden > 0 && args.output > 0 && args.expert_weights == nullptr)) {
       return detail::invalid_argument("chain received a null device buffer");
@@ -761,16 +796,25 @@ Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
                                                                b.offsets, r, args.experts, stream),
                           "chain histogram_exclusive_scan launch failed");
   if (!s.ok() || args.tokens == 0) return s;
+  const bool gather = args.gather_rows && args.hidden > 0;
   s = detail::cuda_status(
-      rrb::launch_token_permute(args.x, args.expert_ids, b.offsets, b.x_permuted, b.route_pos,
-                                b.sorted_route, args.tokens, args.experts, args.top_k,
-                                args.hidden, context.workspace, stream),
+      rrb::launch_token_permute(args.x, args.expert_ids, b.offsets, gather ? nullptr : b.x_permuted,
+                                b.route_pos, b.sorted_route, args.tokens, args.experts,
+                                args.top_k, gather ? 0 : args.hidden, context.workspace, stream),
       "chain token_permute launch failed");
   if (!s.ok() || args.output == 0) return s;
-  s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, args.expert_weights, b.offsets,
-                                                   b.y_permuted, args.experts, r, args.hidden,
-                                                   args.output, stream),
-                          "chain grouped_gemm launch failed");
+  if (gather) {
+    const rrb::RowGather g{args.x, b.sorted_route, args.top_k};
+    s = detail::cuda_status(rrb::launch_grouped_gemm(args.x, args.expert_weights, b.offsets,
+                                                     b.y_permuted, args.experts, r, args.hidden,
+                                                     args.output, stream, 0, nullptr, &g),
+                            "chain grouped_gemm launch failed");
+  } else {
+    s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, args.expert_weights,
+                                                     b.offsets, b.y_permuted, args.experts, r,
+                                                     args.hidden, args.output, stream),
+                            "chain grouped_gemm launch failed");
+  }
   if (!s.ok()) return s;
   return detail::cuda_status(rrb::launch_unpermute(b.y_permuted, b.route_pos, args.route_weights,
                                                    b.y, args.tokens, args.top_k, args.output,
@@ -856,6 +900,28 @@ cudaError_t launch_grouped_gemm_naive(const float* x_permuted, const float* expe
   }
   return rrb::launch_grouped_gemm(x_permuted, expert_weights, offsets, y_permuted, experts, 0,
                                   hidden, output, caller_stream);
+}
+
+// Research entry point of the reference's post-route gather chain
+// (src/grouped_gemm/cuda_candidate/grouped_optimized_internal.h:105-109):
+// row r of segment e is x[sorted_route[r] / top_k] . W[e]. The workspace is
+// not needed here (accepted and ignored).
+cudaError_t launch_grouped_gemm_sm86_fp32_gather_v1(
+    const float* x, const std::int32_t* sorted_route, int top_k, const float* expert_weights,
+    const std::int32_t* offsets, float* y_permuted, int experts, int hidden, int output,
+    int max_expert_tokens, void*, std::size_t, cudaStream_t caller_stream) {
+  if (experts <= 0 || experts > kMaxExperts || hidden < 0 || output < 0 ||
+      max_expert_tokens < 0 || top_k < 1) {
+    return cudaErrorInvalidValue;
+  }
+  if (output == 0 || max_expert_tokens == 0) return cudaSuccess;
+  if (offsets == nullptr || y_permuted == nullptr ||
+      (hidden > 0 && (x == nullptr || sorted_route == nullptr || expert_weights == nullptr))) {
+    return cudaErrorInvalidValue;
+  }
+  const rrb::RowGather gather{x, sorted_route, top_k};
+  return rrb::launch_grouped_gemm(x, expert_weights, offsets, y_permuted, experts, 0, hidden,
+                                  output, caller_stream, 0, nullptr, hidden > 0 ? &gather : nullptr);
 }
 
 // src/unpermute/cuda_naive/baseline.cu:33-50.
@@ -1060,6 +1126,26 @@ rr_status rr_grouped_gemm(const float* x_permuted, const float* expert_weights,
 }
 size_t rr_grouped_gemm_workspace_size(int, int, int) { return 0; }
 
+rr_status rr_grouped_gemm_gather(const float* x, const int32_t* sorted_route, int top_k,
+                                 const float* expert_weights, const int32_t* offsets,
+                                 float* y_permuted, int route_pairs, int hidden, int experts,
+                                 int output, const rr_context* ctx) {
+  if (ctx == nullptr) return null_context();
+  const raggedroute::Status a = raggedroute::detail_resolve_sm100(to_runtime(ctx));
+  if (!a.ok()) return to_c(a);
+  const cudaError_t e = raggedroute::ops::launch_grouped_gemm_sm86_fp32_gather_v1(
+      x, sorted_route, top_k, expert_weights, offsets, y_permuted, experts, hidden, output,
+      route_pairs, nullptr, 0, as_stream(ctx->stream));
+  if (e == cudaErrorInvalidValue) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, e,
+                 "grouped_gemm_gather requires 1<=E<=1024, top_k>=1 and device buffers"});
+  }
+  if (e != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, e, "grouped_gemm_gather launch failed"});
+  }
+  return to_c(raggedroute::success_status());
+}
+
 rr_status rr_unpermute(const float* y_permuted, const int32_t* route_pos,
                        const float* route_weights, float* y, int tokens, int top_k, int output,
                        const rr_context* ctx) {
@@ -1076,6 +1162,17 @@ rr_status rr_unpermute(const float* y_permuted, const int32_t* route_pos,
   return to_c(raggedroute::unpermute(args, to_runtime(ctx)));
 }
 size_t rr_unpermute_workspace_size(int, int, int) { return 0; }
+
+// Chains read ctx->implementation_id: 0 materialises x_permuted,
+// RR_CHAIN_IMPL_GATHER_ROWS gathers the grouped GEMM's rows from x.
+rr_status chain_impl(const rr_context* ctx, bool* gather_rows) {
+  *gather_rows = ctx->implementation_id == RR_CHAIN_IMPL_GATHER_ROWS;
+  if (ctx->implementation_id != 0 && !*gather_rows) {
+    return to_c({raggedroute::StatusCode::kUnsupportedKernelVariant, cudaSuccess,
+                 "unknown chain implementation id"});
+  }
+  return to_c(raggedroute::success_status());
+}
 
 rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
                                const float* logit_bias, const float* expert_weights,
@@ -1095,6 +1192,8 @@ rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
+  const rr_status impl = chain_impl(ctx, &args.gather_rows);
+  if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_tokens(args, to_runtime(ctx)));
 }
 
@@ -1116,6 +1215,8 @@ rr_status rr_chain_from_route_ids(const float* x, const int32_t* expert_ids,
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
+  const rr_status impl = chain_impl(ctx, &args.gather_rows);
+  if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_route_ids(args, to_runtime(ctx)));
 }
 
@@ -1139,6 +1240,8 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
+  const rr_status impl = chain_impl(ctx, &args.gather_rows);
+  if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_logits(args, to_runtime(ctx)));
 }
 

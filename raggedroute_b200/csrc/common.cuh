@@ -47,6 +47,15 @@ __device__ __forceinline__ float* scatter_row(const RowScatter& sc, long long ro
   return sc.base[rank] + r * output;
 }
 
+// Row gather for a GEMM's A operand: row r of the problem is row
+// route[r] / div of x (the token matrix), so no permuted copy of x is
+// materialised (route = sorted_route of the stable permute, div = top_k).
+struct RowGather {
+  const float* x = nullptr;
+  const int32_t* route = nullptr;
+  int div = 1;
+};
+
 // Dispatch side of the peer transport, used by the token permute: a route to
 // virtual expert e (owner rank e / local) is copied to
 // x_base[owner] + (dest_off[e] + rank of the route inside e) * hidden, and
@@ -151,20 +160,24 @@ cudaError_t launch_unpermute(const float* y_permuted, const int32_t* route_pos,
 // expert-parallel runtime uses weight_sets < experts for its
 // (source rank, local expert) groups. scatter (optional) redirects every
 // stored output row (peer transport combine); y is then only an alignment
-// witness for the engine choice.
+// witness for the engine choice. gather (optional, gather->x == x) reads A
+// row r from x[route[r] / div] instead of x[r].
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets,
                                 float* y, int experts, int rows, int hidden, int output,
                                 cudaStream_t stream, int weight_sets = 0,
-                                const RowScatter* scatter = nullptr);
+                                const RowScatter* scatter = nullptr,
+                                const RowGather* gather = nullptr);
 cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,
                                      cudaStream_t stream, int weight_sets = 0,
-                                     const RowScatter* scatter = nullptr);
+                                     const RowScatter* scatter = nullptr,
+                                     const RowGather* gather = nullptr);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
                                    cudaStream_t stream, int weight_sets = 0,
-                                   const RowScatter* scatter = nullptr);
+                                   const RowScatter* scatter = nullptr,
+                                   const RowGather* gather = nullptr);
 
 // misc.cu
 cudaError_t launch_cache_scrub(uint32_t* buffer, std::size_t elements, cudaStream_t stream);

@@ -21,7 +21,7 @@ constexpr int kThreads = 256;
 __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const int32_t* __restrict__ offsets,
     float* __restrict__ y, int experts, int rows, int hidden, int output, int wsets,
-    const RowScatter scatter) {
+    const RowScatter scatter, const RowGather gather) {
   __shared__ int prefix[kMaxExperts + 1];
   __shared__ int scratch[33];
   __shared__ float as[kBK][kBM + 4];
@@ -45,8 +45,9 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
         const int kk = i % kBK;
         const int r = tc.row0 + m;
         const int k = k0 + kk;
-        as[kk][m] = (r < tc.row_end && k < hidden) ? __ldg(x + static_cast<long long>(r) * hidden + k)
-                                                   : 0.0f;
+        long long src_row = r;
+        if (gather.route != nullptr && r < tc.row_end) src_row = __ldg(gather.route + r) / gather.div;
+        as[kk][m] = (r < tc.row_end && k < hidden) ? __ldg(x + src_row * hidden + k) : 0.0f;
       }
       // B stage: 16 k x 64 columns.
       for (int i = threadIdx.x; i < kBK * kBN; i += kThreads) {
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
 cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,
                                      cudaStream_t stream, int weight_sets,
-                                     const RowScatter* scatter) {
+                                     const RowScatter* scatter, const RowGather* gather) {
   const int wsets = weight_sets > 0 ? weight_sets : experts;
   if (output <= 0) return cudaSuccess;
   int grid = 4 * sm_count();
@@ -109,7 +110,9 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
   grouped_gemm_simt_kernel<<<grid, kThreads, 0, stream>>>(x, w, offsets, y, experts, rows, hidden,
                                                           output, wsets,
                                                           scatter != nullptr ? *scatter
-                                                                             : RowScatter{});
+                                                                             : RowScatter{},
+                                                          gather != nullptr ? *gather
+                                                                            : RowGather{});
   note_launch();
   return cudaGetLastError();
 }

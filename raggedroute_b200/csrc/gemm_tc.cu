@@ -148,10 +148,15 @@ __device__ __forceinline__ int nmajor128_offset(int k, int n) {
   return (n >> 5) * kBChunkBytes + k * 128 + ((((n & 31) >> 2) ^ (k & 7)) << 4) + ((n & 3) << 2);
 }
 
+// kGather: A rows come from x through a row map (RowGather) instead of a TMA
+// tile of a materialised x_permuted; a separate instantiation so the default
+// kernel carries none of it.
+template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
     const int32_t* __restrict__ offsets, float* __restrict__ y, int experts, int rows,
-    int hidden, int output, int wsets, unsigned* err, const RowScatter scatter) {
+    int hidden, int output, int wsets, unsigned* err, const RowScatter scatter,
+    const RowGather gather) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
@@ -162,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRawStages; ++i) {
-      mbar_init(&s.raw_full[i], 1);
+      // Gathering: the producer's expect_tx plus one cp.async arrival per lane.
+      mbar_init(&s.raw_full[i], kGather ? 33 : 1);
       mbar_init(&s.raw_empty[i], kWorkerWarps);
       s.issued[i] = 0;
     }
@@ -187,7 +193,59 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
   const uint32_t tmem = s.tmem_base;
   volatile int* failed = &s.failed;
 
-  if (warp == 0) {
+  if (kGather && warp == 0) {
+    // ---------------- producer with row gather (whole warp) ----------------
+    // A rows come from x[route[row] / div]: per k-block each lane issues 16
+    // cp.async of 16 bytes (instruction j: rows 8j..8j+7, lane l copying
+    // chunk l%4 of row 8j + l/4, so a warp instruction fills 512 contiguous
+    // bytes), stored unswizzled (row-contiguous, 64 B per row); the workers
+    // apply the operand swizzle. Each lane then arrives on raw_full when its
+    // copies have landed (32 arrivals + lane 0's expect_tx for B). Rows
+    // before 0 (shifted first tile) are not fetched; they feed only output
+    // rows that are never stored. Lane 0 waits and issues B by TMA.
+    if (lane == 0) tma_prefetch_desc(&tma_b);
+    int stage = 0;
+    uint32_t phase = 0;
+    const int chunk = lane & 3;
+    for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
+      const TileGeom g = geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
+      const int nchunks = (g.ncols + 31) >> 5;
+      int tok[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int row = g.base + 8 * j + (lane >> 2);
+        tok[j] = row >= 0 ? __ldg(gather.route + row) / gather.div : -1;
+      }
+      const uint32_t bbytes = nchunks * kBChunkBytes;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&s.raw_empty[stage], phase ^ 1u, err, failed);
+        if (__shfl_sync(0xffffffffu, ok, 0) == 0) break;
+        uint8_t* st = s.raw[stage];
+        const uint32_t dst = smem_u32(st) + (lane >> 2) * (kBK * 4) + chunk * 16;
+        const float* col = gather.x + kb * kBK + chunk * 4;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (tok[j] >= 0) {
+            cp_async_16(dst + j * 8 * (kBK * 4), col + static_cast<long long>(tok[j]) * hidden);
+          }
+        }
+        cp_async_arrive(&s.raw_full[stage]);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&s.raw_full[stage], bbytes);
+          for (int j = 0; j < nchunks; ++j) {
+            tma_load_3d(st + kOffBRaw + j * kBChunkBytes, &tma_b, &s.raw_full[stage],
+                        g.col0 + 32 * j, kb * kBK, g.expert % wsets);
+          }
+          s.issued[stage] += 1;
+        }
+        if (++stage == kRawStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&tma_a);
@@ -281,6 +339,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const int cgroup = ew >> 2;    // 64-column group of the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const bool vec = (output & 3) == 0;
+    // A chunk of this thread: 16 bytes at tid*16 of the raw tile (row tid/4,
+    // chunk tid%4 as TMA stored it, swizzled, or unswizzled when gathered),
+    // written to its K-major operand position.
+    const uint32_t a_dst = kGather ? static_cast<uint32_t>(kmajor64_offset(tid >> 2, tid & 3))
+                                   : static_cast<uint32_t>(tid * 16);
     int rstage = 0, ostage = 0;
     uint32_t rphase = 0, ophase = 0, acc_phase = 0;
     // The chunk awaiting promotion (tile geometry + whether it ends its tile).
@@ -346,8 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         }
         float4 h, l;
         split4(av, h, l);
-        sts_v4(op + kOffAHi + tid * 16, h);
-        sts_v4(op + kOffALo + tid * 16, l);
+        sts_v4(op + kOffAHi + a_dst, h);
+        sts_v4(op + kOffALo + a_dst, l);
 #pragma unroll
         for (int i = 0; i < kBItems; ++i) {
           if (i < b_items) {
@@ -495,7 +558,11 @@ bool kernel_configured() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [] {
-    ok = cudaFuncSetAttribute(grouped_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ok = cudaFuncSetAttribute(grouped_gemm_tc_kernel<false>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSmemBytes)) == cudaSuccess &&
+         cudaFuncSetAttribute(grouped_gemm_tc_kernel<true>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kSmemBytes)) == cudaSuccess;
     if (!ok) cudaGetLastError();
   });
@@ -518,7 +585,7 @@ bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidde
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
                                    cudaStream_t stream, int weight_sets,
-                                   const RowScatter* scatter) {
+                                   const RowScatter* scatter, const RowGather* gather) {
   const int wsets = weight_sets > 0 ? weight_sets : experts;
   EncodeTiledFn encode = encode_fn();
   if (encode == nullptr) return cudaErrorNotSupported;
@@ -527,7 +594,7 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
   // the last segment end, so the row extent only has to cover it.
   const long long a_rows = rows > 0 ? rows : (1LL << 31) - 1;
   CUtensorMap ma{}, mb{};
-  {
+  if (gather == nullptr) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(a_rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(hidden) * 4};
     const cuuint32_t box[2] = {kBK, kBM};
@@ -561,22 +628,33 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
     if (tiles <= 0) return cudaSuccess;
     if (tiles < grid) grid = static_cast<int>(tiles);
   }
-  grouped_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(),
-      scatter != nullptr ? *scatter : RowScatter{});
+  const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
+  if (gather != nullptr) {
+    grouped_gemm_tc_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(
+        ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
+        *gather);
+  } else {
+    grouped_gemm_tc_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(
+        ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
+        RowGather{});
+  }
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets, float* y,
                                 int experts, int rows, int hidden, int output,
-                                cudaStream_t stream, int weight_sets, const RowScatter* scatter) {
+                                cudaStream_t stream, int weight_sets, const RowScatter* scatter,
+                                const RowGather* gather) {
+  if (gather != nullptr && (gather->x != x || gather->route == nullptr || gather->div < 1)) {
+    return cudaErrorInvalidValue;
+  }
   if (tc_gemm_supported(x, w, y, hidden, output)) {
     return launch_grouped_gemm_tc(x, w, offsets, y, experts, rows, hidden, output, stream,
-                                  weight_sets, scatter);
+                                  weight_sets, scatter, gather);
   }
   return launch_grouped_gemm_simt(x, w, offsets, y, experts, rows, hidden, output, stream,
-                                  weight_sets, scatter);
+                                  weight_sets, scatter, gather);
 }
 
 }  // namespace rrb

@@ -142,6 +142,20 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared by this thread (L2 only).
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem),
+               "l"(reinterpret_cast<uint64_t>(src))
+               : "memory");
+}
+
+// Arrives on the mbarrier once every cp.async this thread issued so far has
+// landed; the arrival is one of the barrier's expected arrivals (noinc).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA / tensor core) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -32,6 +32,16 @@ def _ctx(ctx: Context | None, workspace: torch.Tensor | None = None) -> ctypes.P
     return ctypes.pointer(c.as_c())
 
 
+CHAIN_IMPL_GATHER_ROWS = 1
+
+
+def _chain_ctx(ctx: Context | None, workspace: torch.Tensor, gather_rows: bool):
+    c = dataclasses.replace(ctx) if ctx is not None else Context()
+    if gather_rows:
+        c.implementation_id = CHAIN_IMPL_GATHER_ROWS
+    return _ctx(c, workspace)
+
+
 def _need(t: torch.Tensor | None, dtype: torch.dtype, name: str) -> None:
     if t is None:
         return
@@ -136,6 +146,19 @@ def grouped_gemm(x_permuted: torch.Tensor | None, expert_weights: torch.Tensor |
                                 _ctx(ctx)), "grouped_gemm")
 
 
+def grouped_gemm_gather(x: torch.Tensor, sorted_route: torch.Tensor, top_k: int,
+                        expert_weights: torch.Tensor, offsets: torch.Tensor,
+                        y_permuted: torch.Tensor, route_pairs: int,
+                        ctx: Context | None = None) -> torch.Tensor:
+    """Grouped GEMM whose row r is x[sorted_route[r] // top_k]
+    (launch_grouped_gemm_sm86_fp32_gather_v1 of the reference)."""
+    experts, hidden, output = expert_weights.shape
+    check(lib().rr_grouped_gemm_gather(_ptr(x), _ptr(sorted_route), top_k, _ptr(expert_weights),
+                                       _ptr(offsets), _ptr(y_permuted), route_pairs, hidden,
+                                       experts, output, _ctx(ctx)), "grouped_gemm_gather")
+    return y_permuted
+
+
 def unpermute(y_permuted: torch.Tensor, route_pos: torch.Tensor, route_weights: torch.Tensor,
               y: torch.Tensor, tokens: int, top_k: int, output: int,
               ctx: Context | None = None) -> None:
@@ -192,8 +215,10 @@ def chain_workspace_size(tokens: int, hidden: int, experts: int, output: int) ->
 def chain_from_tokens(x: torch.Tensor, router_weights: torch.Tensor,
                       expert_weights: torch.Tensor, buf: ChainBuffers,
                       logit_bias: torch.Tensor | None = None,
-                      ctx: Context | None = None) -> torch.Tensor:
-    """Seven-stage chain X -> Y (benchmarks/adapters/chain_adapter.cpp:263-467)."""
+                      ctx: Context | None = None, gather_rows: bool = False) -> torch.Tensor:
+    """Seven-stage chain X -> Y (benchmarks/adapters/chain_adapter.cpp:263-467).
+    gather_rows: the grouped GEMM reads its rows from X (buf.x_permuted is
+    not written); results are bit-identical."""
     tokens, hidden = x.shape
     experts = router_weights.shape[1]
     output = expert_weights.shape[2]
@@ -201,12 +226,14 @@ def chain_from_tokens(x: torch.Tensor, router_weights: torch.Tensor,
         _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(expert_weights), _ptr(buf.logits),
         _ptr(buf.expert_ids), _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets),
         _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens,
-        hidden, experts, output, _ctx(ctx, buf.workspace)), "chain_from_tokens")
+        hidden, experts, output, _chain_ctx(ctx, buf.workspace, gather_rows)),
+        "chain_from_tokens")
     return buf.y
 
 
 def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights: torch.Tensor,
-                      buf: ChainBuffers, ctx: Context | None = None) -> torch.Tensor:
+                      buf: ChainBuffers, ctx: Context | None = None,
+                      gather_rows: bool = False) -> torch.Tensor:
     """Six-stage chain logits -> Y."""
     tokens, hidden = x.shape
     experts = logits.shape[1]
@@ -215,7 +242,7 @@ def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights: tor
         _ptr(logits), _ptr(x), _ptr(expert_weights), _ptr(buf.expert_ids),
         _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets), _ptr(buf.x_permuted),
         _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens, hidden, experts, output,
-        _ctx(ctx, buf.workspace)), "chain_from_logits")
+        _chain_ctx(ctx, buf.workspace, gather_rows)), "chain_from_logits")
     return buf.y
 
 
@@ -252,7 +279,8 @@ class RouteChainBuffers:
 
 def chain_from_route_ids(x: torch.Tensor, expert_ids: torch.Tensor,
                          route_weights: torch.Tensor, expert_weights: torch.Tensor,
-                         buf: RouteChainBuffers, ctx: Context | None = None) -> torch.Tensor:
+                         buf: RouteChainBuffers, ctx: Context | None = None,
+                         gather_rows: bool = False) -> torch.Tensor:
     """Post-route chain (benchmarks/adapters/postroute_chain_adapter.cpp:240-354):
     expert_ids / route_weights [T, top_k] -> Y [T, N]."""
     tokens, hidden = x.shape
@@ -262,7 +290,7 @@ def chain_from_route_ids(x: torch.Tensor, expert_ids: torch.Tensor,
         _ptr(x), _ptr(expert_ids), _ptr(route_weights), _ptr(expert_weights), _ptr(buf.counts),
         _ptr(buf.offsets), _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.sorted_route),
         _ptr(buf.y_permuted), _ptr(buf.y), tokens, top_k, hidden, experts, output,
-        _ctx(ctx, buf.workspace)), "chain_from_route_ids")
+        _chain_ctx(ctx, buf.workspace, gather_rows)), "chain_from_route_ids")
     return buf.y
 
 

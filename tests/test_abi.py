@@ -90,8 +90,13 @@ def test_workspace_queries(rrlib):
     assert lib.rr_token_permute_workspace_size(2, 2, 2, 2) == 8
     big = lib.rr_token_permute_workspace_size(1 << 19, 256, 2, 128)
     assert big > 256 * 4
+    # The chain workspace: the permute workspace at 2T routes, 256-byte
+    # aligned, then sorted_route [2T] for the row-gathering variant.
+    perm = lib.rr_token_permute_workspace_size(65536, 128, 2, 4096)
     assert lib.rr_chain_workspace_size(65536, 4096, 128, 1408) == \
-        lib.rr_token_permute_workspace_size(65536, 128, 2, 4096)
+        (perm + 255) // 256 * 256 + 2 * 65536 * 4
+    assert lib.rr_route_chain_workspace_size(1000, 4, 16) == \
+        lib.rr_token_permute_workspace_size(1000, 16, 4, 0)
     for fn in ("rr_histogram_exclusive_scan_workspace_size", "rr_histogram_workspace_size"):
         assert getattr(lib, fn)(1 << 20, 64) == 0
 

@@ -93,10 +93,9 @@ def test_route_trace_frames_through_both_chains(rrlib, oracle, cuda, frame):
     _, _, _, _, _, y = oracle.route_chain_f64(x, w, ids.reshape(-1, 2), rw.reshape(-1, 2), e)
     ok, _, _ = oracle.compare_floating(buf.y.cpu().numpy(), y.astype(np.float32), 1e-4, 4e-5 * k * 2)
     assert ok
-    # The same frame as route ids.
+    # The same frame as route ids, with the gate's own (device) weights.
     rbuf = rrlib.RouteChainBuffers.allocate(t, 2, k, e, n, cuda)
     rrlib.chain_from_route_ids(torch.from_numpy(x).to(cuda), torch.from_numpy(fr.expert_ids).to(cuda),
-                               torch.from_numpy(rw.reshape(-1, 2)).to(cuda),
-                               torch.from_numpy(w).to(cuda), rbuf)
+                               buf.route_weights, torch.from_numpy(w).to(cuda), rbuf)
     torch.cuda.synchronize()
     assert torch.equal(rbuf.y.view(torch.int32), buf.y.view(torch.int32))
