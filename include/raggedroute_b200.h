@@ -381,6 +381,14 @@ rr_status rr_consume_device_error(void* stream, uint32_t* error_word);
 int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
                            float* y_permuted, int hidden, int output);
 const char* rr_version(void);
+/* Failure-detection self-test (no reference counterpart): launches a kernel
+ * that waits, through the same bounded mbarrier wait the GEMM uses, on a
+ * barrier nothing arrives on. After limit_ns the wait gives up, the kernel
+ * sets bit 0 (timeout) of the device error word and returns; elapsed_ns
+ * (device) receives the time waited. Read the word with
+ * rr_consume_device_error. */
+rr_status rr_bounded_wait_selftest(uint64_t limit_ns, unsigned long long* elapsed_ns,
+                                   void* stream);
 /* Device self-check of the GEMM's TF32 split (no reference counterpart):
  * adds to *mismatches (device, caller-zeroed) the number of the n bit
  * patterns (device) whose integer round-to-nearest-away TF32 rounding

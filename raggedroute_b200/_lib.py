@@ -116,6 +116,7 @@ SIGNATURES = {
     "rr_consume_device_error": (RRStatus, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "rr_grouped_gemm_engine": (_I, [_P, _P, _P, _I, _I]),
     "rr_tf32_rounding_selfcheck": (RRStatus, [_P, ctypes.c_int64, _P, _P]),
+    "rr_bounded_wait_selftest": (RRStatus, [ctypes.c_uint64, _P, _P]),
     "rr_version": (ctypes.c_char_p, []),
     "rr_route_trace_read": (RRStatus, [ctypes.c_char_p, _I, ctypes.POINTER(RRRouteTraceInfo),
                                           _P, ctypes.c_int64]),

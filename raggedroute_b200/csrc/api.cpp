@@ -1325,6 +1325,20 @@ int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
   return rrb::tc_gemm_supported(x_permuted, expert_weights, y_permuted, hidden, output) ? 1 : 2;
 }
 
+rr_status rr_bounded_wait_selftest(uint64_t limit_ns, unsigned long long* elapsed_ns,
+                                   void* stream) {
+  if (elapsed_ns == nullptr || limit_ns == 0 || limit_ns > 10000000000ull) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "rr_bounded_wait_selftest requires a device result and 0 < limit <= 10 s"});
+  }
+  const cudaError_t err = rrb::launch_bounded_wait_selftest(limit_ns, elapsed_ns,
+                                                            as_stream(stream));
+  if (err != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, err, "bounded wait self-test failed"});
+  }
+  return to_c(raggedroute::success_status());
+}
+
 rr_status rr_tf32_rounding_selfcheck(const uint32_t* bits, int64_t n,
                                      unsigned long long* mismatches, void* stream) {
   if (n < 0 || (n > 0 && (bits == nullptr || mismatches == nullptr))) {

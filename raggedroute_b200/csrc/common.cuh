@@ -36,6 +36,9 @@ struct RowScatter {
   float* const* base = nullptr;
   int nranks = 0;
   long long row_limit = 0;
+  // Abort fence (optional, host memory mapped into the device): read once at
+  // kernel start; when non-zero no row is stored.
+  const volatile int* abort = nullptr;
 };
 
 // Resolves a packed row address, or nullptr when it is out of range.
@@ -70,6 +73,9 @@ struct PeerDispatch {
   int me = 0;
   long long capacity = 0;
   unsigned* err = nullptr;
+  // Abort fence, as in RowScatter: when set at kernel start, nothing is
+  // written to any rank's buffers.
+  const volatile int* abort = nullptr;
 };
 
 // Counts every kernel this library launches (for the bench's launch claim).
@@ -181,6 +187,10 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
 
 // misc.cu
 cudaError_t launch_cache_scrub(uint32_t* buffer, std::size_t elements, cudaStream_t stream);
+// Bounded-wait self-test: a kernel waits on an mbarrier nothing arrives on;
+// after limit_ns it sets kErrMbarTimeout and returns (*elapsed_ns, device).
+cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns,
+                                         unsigned long long* elapsed_ns, cudaStream_t stream);
 // Adds to *mismatches (device) the number of non-NaN inputs whose integer
 // TF32 rounding differs from the conversion instruction.
 cudaError_t launch_tf32_round_check(const uint32_t* bits, long long n,

@@ -42,12 +42,15 @@
 //   6'. local unpermute once every combine round has landed.
 // The communicator is non-blocking; every host wait on NCCL or the stream has
 // a deadline, after which the communicator is aborted and RR_COMM_ERROR is
-// returned, so a lost peer cannot hang the caller forever. Plan-time
+// returned, so a lost peer cannot hang the caller forever; before the abort a
+// host-set fence tells every kernel still queued to store nothing into
+// other ranks' memory (peer transport). Plan-time
 // allocation only: receive buffers are sized for the worst case
 // (nranks * 2 * max_tokens rows).
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdint>
 #include <cstring>
@@ -99,6 +102,12 @@ struct rr_ep {
   unsigned* h_err = nullptr;        // pinned [2]
   int32_t* h_recv_total = nullptr;  // pinned [2]
   cudaEvent_t step_done[2] = {nullptr, nullptr};
+  // Abort fence: host memory mapped into the device, set before the
+  // communicator is aborted. Kernels of a step that was already queued
+  // behind a collective that the abort ends read it and then store nothing
+  // into other ranks' memory (a lost rank's buffers may be gone).
+  volatile int* h_abort = nullptr;
+  int* d_abort = nullptr;
   bool step_pending[2] = {false, false};
   long long step_sent[2] = {0, 0};
   int next_slot = 0;
@@ -118,6 +127,17 @@ rr_status ok() { return st(RR_SUCCESS, "success"); }
 
 using Clock = std::chrono::steady_clock;
 
+// Raises the abort fence, then aborts the communicator.
+void abort_comm(rr_ep* ep) {
+  ep->broken = true;
+  if (ep->h_abort != nullptr) {
+    *ep->h_abort = 1;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+  }
+  if (ep->comm != nullptr) ncclCommAbort(ep->comm);
+  ep->comm = nullptr;
+}
+
 // Waits until a non-blocking communicator leaves ncclInProgress.
 rr_status wait_comm(rr_ep* ep, const char* what) {
   const auto deadline = Clock::now() + std::chrono::duration<double>(ep->timeout_s);
@@ -125,16 +145,12 @@ rr_status wait_comm(rr_ep* ep, const char* what) {
     ncclResult_t async = ncclSuccess;
     const ncclResult_t r = ncclCommGetAsyncError(ep->comm, &async);
     if (r != ncclSuccess || (async != ncclSuccess && async != ncclInProgress)) {
-      ep->broken = true;
-      ncclCommAbort(ep->comm);
-      ep->comm = nullptr;
+      abort_comm(ep);
       return st(RR_COMM_ERROR, what);
     }
     if (async == ncclSuccess) return ok();
     if (Clock::now() > deadline) {
-      ep->broken = true;
-      ncclCommAbort(ep->comm);
-      ep->comm = nullptr;
+      abort_comm(ep);
       return st(RR_COMM_ERROR, "NCCL did not finish before the deadline; communicator aborted");
     }
     std::this_thread::sleep_for(std::chrono::microseconds(20));
@@ -144,9 +160,7 @@ rr_status wait_comm(rr_ep* ep, const char* what) {
 rr_status check_nccl(rr_ep* ep, ncclResult_t r, const char* what) {
   if (r == ncclSuccess) return ok();
   if (r == ncclInProgress) return wait_comm(ep, what);
-  ep->broken = true;
-  ncclCommAbort(ep->comm);
-  ep->comm = nullptr;
+  abort_comm(ep);
   return st(RR_COMM_ERROR, what);
 }
 
@@ -161,16 +175,12 @@ rr_status wait_stream(rr_ep* ep, cudaStream_t stream) {
       ncclResult_t async = ncclSuccess;
       ncclCommGetAsyncError(ep->comm, &async);
       if (async != ncclSuccess && async != ncclInProgress) {
-        ep->broken = true;
-        ncclCommAbort(ep->comm);
-        ep->comm = nullptr;
+        abort_comm(ep);
         return st(RR_COMM_ERROR, "NCCL reported an asynchronous error");
       }
     }
     if (Clock::now() > deadline) {
-      ep->broken = true;
-      if (ep->comm != nullptr) ncclCommAbort(ep->comm);
-      ep->comm = nullptr;
+      abort_comm(ep);
       return st(RR_COMM_ERROR, "EP step did not finish before the deadline; communicator aborted");
     }
     std::this_thread::sleep_for(std::chrono::microseconds(10));
@@ -190,6 +200,7 @@ void free_ep(rr_ep* ep) {
   cudaFree(ep->d_ret_base);
   cudaFree(ep->d_y_base);
   cudaFreeHost(ep->h_err);
+  if (ep->h_abort != nullptr) cudaFreeHost(const_cast<int*>(ep->h_abort));
   cudaFreeHost(ep->h_recv_total);
   for (cudaEvent_t ev : ep->step_done) {
     if (ev != nullptr) cudaEventDestroy(ev);
@@ -219,16 +230,12 @@ rr_status wait_event(rr_ep* ep, cudaEvent_t ev) {
       ncclResult_t async = ncclSuccess;
       ncclCommGetAsyncError(ep->comm, &async);
       if (async != ncclSuccess && async != ncclInProgress) {
-        ep->broken = true;
-        ncclCommAbort(ep->comm);
-        ep->comm = nullptr;
+        abort_comm(ep);
         return st(RR_COMM_ERROR, "NCCL reported an asynchronous error");
       }
     }
     if (Clock::now() > deadline) {
-      ep->broken = true;
-      if (ep->comm != nullptr) ncclCommAbort(ep->comm);
-      ep->comm = nullptr;
+      abort_comm(ep);
       return st(RR_COMM_ERROR, "EP step did not finish before the deadline; communicator aborted");
     }
     std::this_thread::sleep_for(std::chrono::microseconds(10));
@@ -501,6 +508,15 @@ rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int router_e
   if (e == cudaSuccess) e = cudaMallocHost(&ep->h_count_all, sizeof(int32_t) * nranks * experts);
   if (e == cudaSuccess) e = cudaMallocHost(&ep->h_err, 2 * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMallocHost(&ep->h_recv_total, 2 * sizeof(int32_t));
+  if (e == cudaSuccess) {
+    void* h = nullptr;
+    e = cudaHostAlloc(&h, sizeof(int), cudaHostAllocMapped);
+    if (e == cudaSuccess) {
+      ep->h_abort = static_cast<volatile int*>(h);
+      *ep->h_abort = 0;
+      e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&ep->d_abort), h, 0);
+    }
+  }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ep->comm_stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->local_ready, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->combine_done, cudaEventDisableTiming);
@@ -675,6 +691,7 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
       pd.me = ep->rank;
       pd.capacity = ep->capacity_rows;
       pd.err = ep->d_err;
+      pd.abort = ep->d_abort;
       e = rrb::launch_token_permute_peer(x, expert_ids, offsets, route_pos, tokens, E, 2, K,
                                          ctx->workspace, pd, stream);
     }
@@ -688,6 +705,7 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     sc.base = ep->d_y_base;
     sc.nranks = G;
     sc.row_limit = 2LL * ep->max_tokens;
+    sc.abort = ep->d_abort;
     e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets, ep->y_back,
                                  ep->local, static_cast<int>(ep->capacity_rows), K, N, stream, 0,
                                  &sc);

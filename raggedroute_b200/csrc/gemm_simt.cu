@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
       if (r >= tc.row_end) continue;
       float* out = y + static_cast<long long>(r) * output;
       if (scatter.dst != nullptr) {
+        if (scatter.abort != nullptr && *scatter.abort != 0) continue;
         out = scatter_row(scatter, r, output);
         if (out == nullptr) continue;
       }

@@ -100,6 +100,7 @@ struct alignas(1024) Smem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int failed;
+  int no_scatter;  // abort fence read at start: scattered rows are not stored
   int issued[kRawStages];
   int prefix[kMaxExperts + 1];
   int scratch[33];
@@ -180,6 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     mbar_init(&s.tmem_empty, kWorkerWarps);
     mbar_init(&s.mma_done, 1);
     s.failed = 0;
+    s.no_scatter = (scatter.abort != nullptr) ? *scatter.abort : 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -445,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         bool store_row = pending_last && row >= pg.row0 && row < pg.row_end;
         float* out = y + static_cast<long long>(row) * output + pg.col0 + c_begin;
         if (scatter.dst != nullptr && store_row) {
-          float* dst_row = scatter_row(scatter, row, output);
+          float* dst_row = s.no_scatter ? nullptr : scatter_row(scatter, row, output);
           store_row = dst_row != nullptr;
           out = dst_row + pg.col0 + c_begin;
         }

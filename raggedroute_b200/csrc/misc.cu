@@ -35,7 +35,36 @@ __global__ void tf32_round_check_kernel(const uint32_t* __restrict__ bits, long 
   if (local != 0) atomicAdd(mismatches, local);
 }
 
+// Failure-path self-test of the bounded waits: one CTA waits, with the
+// library's mbar_wait, on an mbarrier that nothing arrives on. After
+// limit_ns the wait gives up, sets kErrMbarTimeout in the device error word
+// and the kernel returns normally; *elapsed_ns records how long it waited.
+__global__ void bounded_wait_selftest_kernel(unsigned long long limit_ns, unsigned* err,
+                                             unsigned long long* elapsed_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int failed;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    failed = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = sm100::global_timer_ns();
+    volatile int* f = &failed;
+    const bool ok = sm100::mbar_wait(&bar, 0, err, f, limit_ns);
+    *elapsed_ns = ok ? 0ull : static_cast<unsigned long long>(sm100::global_timer_ns() - t0);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns,
+                                         unsigned long long* elapsed_ns, cudaStream_t stream) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, device_error_word(), elapsed_ns);
+  note_launch();
+  return cudaGetLastError();
+}
 
 cudaError_t launch_tf32_round_check(const uint32_t* bits, long long n,
                                     unsigned long long* mismatches, cudaStream_t stream) {

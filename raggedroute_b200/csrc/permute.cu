@@ -231,6 +231,8 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
   const int w0 = warp * per_warp;
   const int steps = per_warp >> 5;  // <= kMaxPerLane
 
+  __shared__ int aborted;
+  if (threadIdx.x == 0) aborted = (kPeer && peer.abort != nullptr) ? *peer.abort : 0;
   for (int i = threadIdx.x; i < kPlaceWarps * experts; i += blockDim.x) warp_base[i] = 0;
   __syncthreads();
 
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
         route_pos[r0 + local] = p;
         if constexpr (kPeer) {
           long long packed = -1;
-          if (p >= 0) {
+          if (p >= 0 && !aborted) {
             const int owner = e / peer.local;
             const long long row = static_cast<long long>(__ldg(peer.dest_off + e)) +
                                   (p - __ldg(offsets + e));

@@ -82,13 +82,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // time: raises kErrMbarTimeout in *err_word, sets *failed and returns false.
 // No wait in this library can spin forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err_word,
-                                          volatile int* failed) {
+                                          volatile int* failed,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (*failed) return false;
-    if (global_timer_ns() - start > kWaitLimitNs) {
+    if (global_timer_ns() - start > limit_ns) {
       raise_device_error(err_word, kErrMbarTimeout);
       *failed = 1;
       return false;

@@ -53,3 +53,19 @@ def test_ep_multi_gpu_matches_single_gpu_chain(rrlib, cuda, transport, ragged, p
            f"--master-port={port}", os.path.join(ROOT, "tests", "ep_worker.py")]
     res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert res.returncode == 0, res.stdout[-4000:] + res.stderr[-4000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
+def test_ep_lost_rank_returns_comm_error(rrlib, cuda):
+    """tests/ep_fail_worker.py: a rank leaves between steps; the other's next
+    step returns RR_COMM_ERROR within its deadline (no hang, no GPU fault)
+    and its device stays usable. NCCL transport (no peer-memory stores),
+    NVLS off, gloo bootstrap."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "180", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           "--master-port=29541", os.path.join(ROOT, "tests", "ep_fail_worker.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    out = res.stdout + res.stderr
+    assert res.returncode == 0, out[-4000:]
+    assert "rank 0: ok=True" in out, out[-4000:]
