@@ -138,6 +138,26 @@ def test_grouped_tc_c4_full_size_sampled(rrlib, oracle, cuda):
     assert device_error_word(rrlib) == 0
 
 
+@pytest.mark.parametrize("m,n,k", [(40000, 128, 256), (37999, 100, 64), (65536, 128, 128)])
+def test_dense_tc_two_tiles_per_cta(rrlib, oracle, cuda, m, n, k):
+    """Router-shaped GEMMs (N <= 128, at least one wave of 256-row tiles) run
+    two 128-row m-tiles per CTA sharing each B tile; ragged row counts leave
+    a shifted last tile."""
+    rng = np.random.default_rng(m + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.normal(0, 1 / math.sqrt(k), (k, n)).astype(np.float32)
+    da, db = dev(a, cuda), dev(b, cuda)
+    c = torch.full((m, n), float("nan"), device=cuda)
+    rrlib.dense_gemm(da, db, c, m, n, k)
+    got = host(c)
+    ref = oracle.dense_gemm_f64(a, b)
+    rows = rng.choice(m, 2048, replace=False)
+    rows[:2] = [0, m - 1]
+    check(oracle, got[rows], a[rows], b, ref[rows], k)
+    assert oracle.normwise_rel_error(got, ref) <= 1e-5
+    assert device_error_word(rrlib) == 0
+
+
 def test_integer_tf32_rounding_matches_cvt(rrlib, cuda):
     """The split rounds to TF32 with integer adds on the bit pattern; it must
     equal cvt.rna.tf32.f32 for every non-NaN input: random bit patterns over
