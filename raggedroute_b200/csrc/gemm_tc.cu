@@ -27,7 +27,14 @@
 //
 // Structure: a persistent CTA per SM walks the device-side tile schedule
 // (tile_sched.cuh, read from offsets, no host sync). Tiles are 128 rows x 256
-// columns; warps are specialised:
+// columns, or, for one group with N <= 128 (the router GEMM), two 128-row
+// m-tiles sharing a 128-column B tile with one accumulator each (kMT = 2;
+// same shared-memory and TMEM footprint). Options that are separate
+// instantiations, so the default kernel carries none of them: row gather
+// (kGather, A rows fetched from x through a row map by the producer warp
+// with cp.async) and, at run time, an output-row scatter to other ranks'
+// memory (expert-parallel combine, skipped once the abort fence is set).
+// Warps are specialised:
 //   warp 0     TMA producer: A (x rows, K-major, 64-byte swizzle) and B (the
 //              expert's [K, N] weights, N-major, 128-byte swizzle) per 16-wide
 //              k-block into a 4-slot raw ring; no multicast.
