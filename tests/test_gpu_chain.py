@@ -99,3 +99,41 @@ def test_chain_repeatable(rrlib, cuda):
     rrlib.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf)
     torch.cuda.synchronize()
     assert torch.equal(y1, buf.y) and torch.equal(pos1, buf.route_pos)
+
+
+def test_chain_from_tokens_c5_full_size_sampled(rrlib, oracle, cuda):
+    """C5 at full size (T=65536, K=4096, E=128, N=1408, log-Zipf bias),
+    through the same chain call as the benchmark: routing checked exactly
+    against the oracle applied to the device logits for every token (ids,
+    counts, offsets, stable route_pos), device logits and final rows of 64
+    sampled tokens (including the first and last) against the float64
+    oracle within the reference's tolerances."""
+    from raggedroute_b200.workloads import C5, c5_inputs
+    t, k, e, n = C5["tokens"], C5["hidden"], C5["experts"], C5["output"]
+    inp = c5_inputs(cuda)
+    buf = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    rrlib.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf, logit_bias=inp.logit_bias)
+    torch.cuda.synchronize()
+    logits = host(buf.logits)
+    bias = inp.logit_bias.cpu().numpy()
+    ids_ref, w_ref = oracle.top2_f32(logits, bias)
+    assert np.array_equal(host(buf.expert_ids), ids_ref)
+    assert oracle.compare_floating(host(buf.route_weights), w_ref, 1e-6, 1e-6)[0]
+    counts_ref = oracle.histogram(ids_ref, e)
+    offsets_ref = oracle.exclusive_scan(counts_ref)
+    assert np.array_equal(host(buf.counts), counts_ref)
+    assert np.array_equal(host(buf.offsets), offsets_ref)
+    assert counts_ref.sum() == 2 * t
+    pos_ref = oracle.stable_route_pos(ids_ref.reshape(-1), offsets_ref, e)
+    assert np.array_equal(host(buf.route_pos), pos_ref)
+    rng = np.random.default_rng(5)
+    sample = np.concatenate([[0, t - 1], rng.choice(np.arange(1, t - 1), 62, replace=False)])
+    xs = inp.x[torch.from_numpy(sample).to(cuda)].cpu().numpy()
+    wr = inp.router_w.cpu().numpy()
+    lg_ref = oracle.dense_gemm_f64(xs, wr)
+    bound = oracle.gemm_error_bound(xs, wr, k)
+    assert np.all(np.abs(logits[sample].astype(np.float64) - lg_ref) <= bound)
+    we = inp.expert_w.cpu().numpy()
+    y_s = oracle.chain_output_f32(xs, we, ids_ref[sample], w_ref[sample])
+    ok, err, rel = oracle.compare_floating(host(buf.y)[sample], y_s, 1e-4, 4e-5 * k)
+    assert ok, (err, rel)
