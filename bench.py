@@ -426,6 +426,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if args.gather_rows:
         # ranks only: ids read, route_pos and sorted_route written
         stage_bytes["token_permute"] = 12.0 * routes + 4.0 * (e + 1)
+    if world == 1 and not args.no_extras:
+        extras["configs"] = config_sweep(torch, rr, device, hbm, peak_3x)
     stages = {}
     for nm in stage_names:
         ms = stage_ms[nm]
@@ -545,6 +547,114 @@ def cold_scrub_step(torch, rr, stream, step, steps: int) -> dict:
         b.synchronize()
         total += a.elapsed_time(b)
     return {"ms_per_step": round(total / steps, 3), "scrub_bytes": scrub.numel() * 4}
+
+
+def _event_us(torch, rr, stream, fn, iters: int) -> float:
+    """Mean device time of one fn(ctx) call in microseconds: `iters` calls are
+    captured into one CUDA graph (rr_graph_*), so host call overhead does not
+    starve the GPU between short kernels, and the replay is timed with CUDA
+    events after 3 untimed calls and one untimed replay."""
+    ctx = rr.Context(stream=stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn(ctx)
+    graph = rr.Graph.capture(lambda c: [fn(c) for _ in range(iters)], stream)
+    try:
+        graph.launch(stream)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        graph.launch(stream)
+        b.record(stream)
+        b.synchronize()
+    finally:
+        graph.close()
+    return a.elapsed_time(b) * 1e3 / iters
+
+
+def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float) -> dict:
+    """The BASELINE parity configs C3 and C4 timed on their own (warm L2 as in
+    the reference's protocol; device time per call from a captured graph of
+    back-to-back calls, see _event_us).
+
+    C3: 1,048,576 routes (T=524,288, K=128) for E in {1, 8, 64, 256} x ids
+    {uniform, Zipf(1.5), all-to-one}: histogram, exclusive_scan, the fused
+    histogram_exclusive_scan and the stable token_permute (with sorted_route;
+    top_k = 2, so not at E = 1).
+    Bytes per call are the algorithmic ones (ids read once; for the permute
+    X read once, Xp written, ids, route_pos and sorted_route).
+    C4: grouped_gemm over R=32768 rows, E=64 (6 empty, Zipf(1.1) sizes),
+    K=N=1024; 2*R*K*N FLOP against the 3xTF32 peak."""
+    from raggedroute_b200.workloads import C3, C4, c4_group_sizes, offsets_from_sizes, route_ids
+    stream = torch.cuda.Stream(device)
+    out = {}
+    # The gate alone at C5 shapes (logits [65536, 128] + bias -> ids, weights).
+    gt, ge = 65536, 128
+    logits = torch.randn(gt, ge, device=device)
+    bias = torch.randn(ge, device=device)
+    g_ids = torch.empty(gt, 2, dtype=torch.int32, device=device)
+    g_w = torch.empty(gt, 2, device=device)
+    gate = _event_us(torch, rr, stream, lambda c: rr.topk_gate_biased(
+        logits, bias, g_ids, g_w, gt, ge, ctx=c), 50)
+    gate_b = 4.0 * gt * ge + 16.0 * gt
+    out["C5_topk_gate"] = {"us": round(gate, 2),
+                           "hbm_frac": round(gate_b / (gate * 1e-6) / 1e9 / hbm_gbs, 3)}
+    del logits
+    routes, k = C3["routes"], C3["hidden"]
+    tokens = routes // 2
+    x = torch.rand(tokens, k, device=device) * 2 - 1
+    xp = torch.empty(routes, k, device=device)
+    pos = torch.empty(routes, dtype=torch.int32, device=device)
+    srt = torch.empty(routes, dtype=torch.int32, device=device)
+    c3 = {}
+    for e in C3["experts"]:
+        counts = torch.empty(e, dtype=torch.int32, device=device)
+        offsets = torch.empty(e + 1, dtype=torch.int32, device=device)
+        ws = torch.empty(rr.token_permute_workspace_size(tokens, e, 2, k) // 4 + 1,
+                         dtype=torch.int32, device=device)
+        for dist in ("uniform", "zipf", "one"):
+            ids = torch.as_tensor(route_ids(routes, e, dist, seed=C3["seed"]), device=device)
+            hist = _event_us(torch, rr, stream,
+                             lambda c: rr.histogram(ids, counts, routes, e, ctx=c), 50)
+            scan = _event_us(torch, rr, stream,
+                             lambda c: rr.exclusive_scan(counts, offsets, e, ctx=c), 50)
+            fused = _event_us(torch, rr, stream, lambda c: rr.histogram_exclusive_scan(
+                ids, counts, offsets, routes, e, ctx=c), 50)
+            hist_b = 4.0 * routes + 4.0 * e
+            fused_b = 4.0 * routes + 8.0 * e + 4
+            perm_b = 4.0 * tokens * k + 4.0 * routes * k + 12.0 * routes + 4.0 * (e + 1)
+
+            def frac(b, us):
+                return round(b / (us * 1e-6) / 1e9 / hbm_gbs, 3)
+
+            entry = {
+                "histogram_us": round(hist, 2), "histogram_hbm_frac": frac(hist_b, hist),
+                "exclusive_scan_us": round(scan, 2),
+                "histogram_exclusive_scan_us": round(fused, 2),
+                "histogram_exclusive_scan_hbm_frac": frac(fused_b, fused)}
+            if e >= 2:  # top_k = 2 needs two experts (the operator's top_k <= E rule)
+                perm = _event_us(torch, rr, stream, lambda c: rr.token_permute(
+                    x, ids, offsets, xp, pos, srt, tokens, e, 2, k, ws, ctx=c), 20)
+                entry["token_permute_us"] = round(perm, 2)
+                entry["token_permute_hbm_frac"] = frac(perm_b, perm)
+            c3[f"E{e}_{dist}"] = entry
+    out["C3"] = c3
+    del x, xp, pos, srt
+    r, e, k, n = C4["routes"], C4["experts"], C4["hidden"], C4["output"]
+    sizes = c4_group_sizes(r, e, C4["empty"], seed=C4["seed"])
+    offsets = torch.as_tensor(offsets_from_sizes(sizes), device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(C4["seed"])
+    a = torch.rand(r, k, device=device, generator=g) * 2 - 1
+    w = torch.randn(e, k, n, device=device, generator=g) / math.sqrt(k)
+    y = torch.empty(r, n, device=device)
+    gemm = _event_us(torch, rr, stream,
+                     lambda c: rr.grouped_gemm(a, w, offsets, y, e, k, n, r, ctx=c), 20)
+    tflops = 2.0 * r * k * n / (gemm * 1e-6) / 1e12
+    out["C4"] = {"grouped_gemm_us": round(gemm, 2), "TFLOP/s": round(tflops, 2),
+                 "tensor_frac_3xtf32": round(tflops / peak_3x, 3),
+                 "note": "W (256 MiB) and Xp (128 MiB) partly L2-resident between calls"}
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -34,7 +34,10 @@ constexpr int kPlaceThreads = 256;
 constexpr int kPlaceWarps = kPlaceThreads / 32;
 constexpr int kMaxChunkRoutes = 4096;
 constexpr int kMaxPerLane = kMaxChunkRoutes / kPlaceThreads;  // 16
-constexpr int kTargetChunks = 4 * kNumSms;
+// About one resident wave of place CTAs (8 per SM): the copy work of a chunk
+// is proportional to its tokens, so with ~7 chunks per SM the busiest SM
+// carries ~1% more than the mean (512 chunks, 3.46 per SM, cost 16%).
+constexpr int kTargetChunks = 8 * kNumSms;
 
 struct ChunkPlan {
   int tokens_per_chunk;
@@ -44,7 +47,7 @@ struct ChunkPlan {
 ChunkPlan plan_chunks(int tokens, int top_k) {
   const long long routes = static_cast<long long>(tokens) * top_k;
   long long want = (routes + kTargetChunks - 1) / kTargetChunks;
-  long long rc = 256;
+  long long rc = 128;
   while (rc < want && rc < kMaxChunkRoutes) rc <<= 1;
   int tc = static_cast<int>(rc / top_k);
   if (tc < 1) tc = 1;
@@ -93,9 +96,18 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict_
   const int per = (chunks + 31) / 32;
   const int c0 = grp * per;
   const int c1 = min(chunks, c0 + per);
+  constexpr int kBatch = 8;  // loads in flight per lane
   int sum = 0;
   if (e < experts) {
-    for (int c = c0; c < c1; ++c) sum += chunk_hist[static_cast<long long>(c) * experts + e];
+    for (int c = c0; c < c1; c += kBatch) {
+      int v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        v[u] = c + u < c1 ? chunk_hist[static_cast<long long>(c + u) * experts + e] : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) sum += v[u];
+    }
   }
   part[grp][lane] = sum;
   __syncthreads();
@@ -110,11 +122,17 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict_
   __syncthreads();
   if (e < experts) {
     int run = offsets[e] + part[grp][lane];
-    for (int c = c0; c < c1; ++c) {
-      int32_t* cell = chunk_hist + static_cast<long long>(c) * experts + e;
-      const int v = *cell;
-      *cell = run;
-      run += v;
+    for (int c = c0; c < c1; c += kBatch) {
+      int v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        v[u] = c + u < c1 ? chunk_hist[static_cast<long long>(c + u) * experts + e] : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (c + u < c1) chunk_hist[static_cast<long long>(c + u) * experts + e] = run;
+        run += v[u];
+      }
     }
     // The group that owns the last chunk holds the grand total.
     if (c1 == chunks && c0 < c1) cursors[e] = run - offsets[e];
@@ -333,6 +351,40 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
     return;
   }
   if (hidden <= 0) return;
+  if constexpr (kVec) {
+    const int n4 = hidden >> 2;
+    if (n4 <= 32 && top_k <= 8) {
+      // Short rows (hidden <= 128): one 16-byte chunk per lane and row, four
+      // rows per warp step, so every lane keeps four loads in flight.
+      constexpr int kRows = 4;
+      for (int t = t0 + warp; t < t1; t += kRows * kPlaceWarps) {
+        float4 v[kRows];
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) {
+          const int tu = t + u * kPlaceWarps;
+          if (tu < t1 && lane < n4) {
+            v[u] = __ldg(reinterpret_cast<const float4*>(x + static_cast<long long>(tu) * hidden) +
+                         lane);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) {
+          const int tu = t + u * kPlaceWarps;
+          if (tu < t1 && lane < n4) {
+            const int* d = pos + (tu - t0) * top_k;
+            for (int k = 0; k < top_k; ++k) {
+              const int dk = d[k];
+              if (dk >= 0) {
+                __stcs(reinterpret_cast<float4*>(xp + static_cast<long long>(dk) * hidden) + lane,
+                       v[u]);
+              }
+            }
+          }
+        }
+      }
+      return;
+    }
+  }
   // Copy: one warp per token row, read once, written top_k times.
   for (int t = t0 + warp; t < t1; t += kPlaceWarps) {
     int dest[8];

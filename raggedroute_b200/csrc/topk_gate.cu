@@ -51,7 +51,10 @@ __device__ __forceinline__ void insert(unsigned long long key, unsigned long lon
   }
 }
 
-template <int L, bool kVec>
+// kPer: 128-bit loads each lane issues before it ranks them (all in flight at
+// once); 8 for large batches so that one wave of CTAs keeps enough bytes in
+// flight to stream the logits at HBM speed, 2 for small latency-bound ones.
+template <int L, bool kVec, int kPer>
 __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict__ logits,
                                                         const float* __restrict__ bias,
                                                         int32_t* __restrict__ ids,
@@ -75,21 +78,33 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
       const int nvec = experts >> 2;
       const float4* src4 = reinterpret_cast<const float4*>(src);
       const float4* bias4 = reinterpret_cast<const float4*>(bias);
-#pragma unroll 4
-      for (int q = j; q < nvec; q += L) {
-        float4 v = __ldg(src4 + q);
-        if (bias != nullptr) {
-          const float4 b = __ldg(bias4 + q);
-          v.x = v.x + b.x;
-          v.y = v.y + b.y;
-          v.z = v.z + b.z;
-          v.w = v.w + b.w;
+      // Keys order candidates totally (value, then lower id), so the order
+      // in which a lane ranks its candidates does not change the result.
+      for (int q0 = j; q0 < nvec; q0 += L * kPer) {
+        float4 v[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const int q = q0 + u * L;
+          if (q < nvec) v[u] = __ldcs(src4 + q);
         }
-        const int e = q << 2;
-        insert(make_key(v.x, e, non_nan), k1, k2);
-        insert(make_key(v.y, e + 1, non_nan), k1, k2);
-        insert(make_key(v.z, e + 2, non_nan), k1, k2);
-        insert(make_key(v.w, e + 3, non_nan), k1, k2);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const int q = q0 + u * L;
+          if (q < nvec) {
+            if (bias != nullptr) {
+              const float4 b = __ldg(bias4 + q);
+              v[u].x = v[u].x + b.x;
+              v[u].y = v[u].y + b.y;
+              v[u].z = v[u].z + b.z;
+              v[u].w = v[u].w + b.w;
+            }
+            const int e = q << 2;
+            insert(make_key(v[u].x, e, non_nan), k1, k2);
+            insert(make_key(v[u].y, e + 1, non_nan), k1, k2);
+            insert(make_key(v[u].z, e + 2, non_nan), k1, k2);
+            insert(make_key(v[u].w, e + 3, non_nan), k1, k2);
+          }
+        }
       }
     } else {
 #pragma unroll 4
@@ -150,37 +165,41 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
   }
 }
 
-template <int L, bool kVec>
+template <int L, bool kVec, int kPer>
 cudaError_t launch_l(const float* logits, const float* bias, int32_t* ids, float* weights,
                      int tokens, int experts, bool pair, const int32_t* remap,
                      cudaStream_t stream) {
   constexpr int kThreads = 256;
   constexpr int kRowsPerBlock = (kThreads / 32) * (32 / L);
   const int blocks = ceil_div(tokens, kRowsPerBlock);
-  topk_gate_kernel<L, kVec><<<blocks, kThreads, 0, stream>>>(logits, bias, ids, weights, tokens,
-                                                             experts, pair, remap);
+  topk_gate_kernel<L, kVec, kPer><<<blocks, kThreads, 0, stream>>>(
+      logits, bias, ids, weights, tokens, experts, pair, remap);
   note_launch();
   return cudaGetLastError();
 }
 
-template <bool kVec>
-cudaError_t launch_vec(const float* logits, const float* bias, int32_t* ids, float* weights,
+template <bool kVec, int kPer>
+cudaError_t launch_per(const float* logits, const float* bias, int32_t* ids, float* weights,
                        int tokens, int experts, bool pair, const int32_t* remap,
                        cudaStream_t stream) {
-  // About two loads (8 candidates with 128-bit loads) per lane.
+  // About kPer loads (4 * kPer candidates with 128-bit loads) per lane.
   const int items = kVec ? (experts >> 2) : experts;
-  int want = (items + (kVec ? 1 : 3)) / (kVec ? 2 : 4);
+  const int per = kVec ? kPer : 4;
+  const int want = (items + per - 1) / per;
   int l = 1;
   while (l < want && l < 32) l <<= 1;
   switch (l) {
-    case 1: return launch_l<1, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 2: return launch_l<2, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 4: return launch_l<4, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 8: return launch_l<8, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 16: return launch_l<16, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    default: return launch_l<32, kVec>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 1: return launch_l<1, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 2: return launch_l<2, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 4: return launch_l<4, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 8: return launch_l<8, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 16: return launch_l<16, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    default: return launch_l<32, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
   }
 }
+
+// Batches from this many rows up stream the logits with 8 loads per lane.
+constexpr int kStreamingRows = 16384;
 
 }  // namespace
 
@@ -190,8 +209,12 @@ cudaError_t launch_topk_gate(const float* logits, const float* bias, int32_t* id
   const bool vec = (experts % 4 == 0) && aligned_to(logits, 16) &&
                    (bias == nullptr || aligned_to(bias, 16));
   const bool pair = aligned_to(ids, 8) && aligned_to(weights, 8);
-  return vec ? launch_vec<true>(logits, bias, ids, weights, tokens, experts, pair, remap, stream)
-             : launch_vec<false>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+  if (!vec) {
+    return launch_per<false, 1>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+  }
+  return tokens >= kStreamingRows
+             ? launch_per<true, 8>(logits, bias, ids, weights, tokens, experts, pair, remap, stream)
+             : launch_per<true, 2>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
 }
 
 }  // namespace rrb
