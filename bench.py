@@ -358,7 +358,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         x_host = inp.x.cpu().pin_memory()
         y_host = torch.empty(tokens, n, dtype=torch.float32).pin_memory()
         if ep is None:
-            host_chain = rr.HostChain(args.e2e_chunk, k, e, n)
+            # x_host is written once before timing, so back-to-back steps may
+            # overlap (the next step's copies in run while this one finishes).
+            host_chain = rr.HostChain(args.e2e_chunk, k, e, n, input_ready=True)
         else:
             x_dev = torch.empty_like(inp.x)
 
@@ -392,7 +394,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         e2e = {"value": tokens * world * args.steps / (float(te.item()) * 1e-3), "unit": UNIT,
                "h2d_bytes_per_step": x_host.numel() * 4,
                "d2h_bytes_per_step": y_host.numel() * 4,
-               "api": ("rr_chain_from_tokens_host, chunk %d tokens" % args.e2e_chunk
+               "api": ("rr_chain_from_tokens_host (input-ready plan: consecutive steps "
+                       "overlap), chunk %d tokens" % args.e2e_chunk
                        if ep is None else "copy in + rr_ep_chain_from_tokens + copy out")}
         if ep is None:
             host_chain.close()
@@ -599,6 +602,11 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float) -> dict:
     gate_b = 4.0 * gt * ge + 16.0 * gt
     out["C5_topk_gate"] = {"us": round(gate, 2),
                            "hbm_frac": round(gate_b / (gate * 1e-6) / 1e9 / hbm_gbs, 3)}
+    g_counts = torch.empty(ge, dtype=torch.int32, device=device)
+    g_offsets = torch.empty(ge + 1, dtype=torch.int32, device=device)
+    hs = _event_us(torch, rr, stream, lambda c: rr.histogram_exclusive_scan(
+        g_ids, g_counts, g_offsets, 2 * gt, ge, ctx=c), 50)
+    out["C5_histogram_exclusive_scan"] = {"us": round(hs, 2)}
     del logits
     routes, k = C3["routes"], C3["hidden"]
     tokens = routes // 2

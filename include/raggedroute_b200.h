@@ -261,6 +261,15 @@ typedef struct rr_host_chain rr_host_chain;
 rr_status rr_host_chain_create(int chunk_tokens, int hidden, int experts, int output,
                                rr_host_chain** out);
 rr_status rr_host_chain_destroy(rr_host_chain* plan);
+/* Plan flags (rr_host_chain_set_flags; 0 by default).
+ * RR_HOST_CHAIN_INPUT_READY: x_host is complete when the call is made (the
+ * caller does not produce it with work enqueued earlier on ctx->stream), so
+ * the host-to-device copies need not wait for that work. Back-to-back calls
+ * then overlap: the first copies of a call run while the previous call's
+ * last chunks compute and copy out. The chain itself and the completion of
+ * the call stay ordered on ctx->stream either way. */
+#define RR_HOST_CHAIN_INPUT_READY 1u
+rr_status rr_host_chain_set_flags(rr_host_chain* plan, uint32_t flags);
 /* x_host [tokens, K] and y_host [tokens, N] should be pinned (pageable
  * memory works but serialises the copies). router_weights, logit_bias
  * (optional) and expert_weights are device buffers as for

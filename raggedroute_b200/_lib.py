@@ -128,6 +128,7 @@ SIGNATURES = {
     "rr_graph_destroy": (RRStatus, [_P]),
     "rr_host_chain_create": (RRStatus, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p)]),
     "rr_host_chain_destroy": (RRStatus, [_P]),
+    "rr_host_chain_set_flags": (RRStatus, [_P, ctypes.c_uint32]),
     "rr_chain_from_tokens_host": (RRStatus, [_P] * 8 + [_I, _CTX]),
     "rr_ep_get_unique_id": (RRStatus, [_P]),
     "rr_ep_create": (RRStatus, [_P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_double, _I,

@@ -398,14 +398,8 @@ Status histogram(const HistogramArgs& args, const RuntimeContext& context) noexc
   if (args.counts == nullptr || (args.route_pairs != 0 && args.expert_ids == nullptr)) {
     return detail::invalid_argument("histogram received a null device pointer");
   }
-  status = detail::cuda_status(
-      cudaMemsetAsync(args.counts, 0, static_cast<std::size_t>(args.experts) * sizeof(std::int32_t),
-                      context.stream),
-      "histogram counts reset failed");
-  if (!status.ok()) return status;
-  return detail::cuda_status(rrb::launch_histogram_accumulate(args.expert_ids, args.counts,
-                                                              args.route_pairs, args.experts,
-                                                              context.stream),
+  return detail::cuda_status(rrb::launch_histogram(args.expert_ids, args.counts, args.route_pairs,
+                                                   args.experts, context.stream),
                              "histogram kernel launch failed");
 }
 

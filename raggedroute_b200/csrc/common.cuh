@@ -110,6 +110,9 @@ cudaError_t launch_topk_gate(const float* logits, const float* bias, int32_t* id
 // routing.cu
 cudaError_t launch_histogram_accumulate(const int32_t* ids, int32_t* counts, int routes,
                                         int experts, cudaStream_t stream);
+// Histogram that overwrites counts (the reset is part of the call).
+cudaError_t launch_histogram(const int32_t* ids, int32_t* counts, int routes, int experts,
+                             cudaStream_t stream);
 cudaError_t launch_exclusive_scan(const int32_t* counts, int32_t* offsets, int experts,
                                   cudaStream_t stream);
 // Fused histogram + exclusive scan; overwrites counts and offsets (reset is

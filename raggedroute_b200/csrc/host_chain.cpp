@@ -30,6 +30,7 @@ struct rr_host_chain {
   int experts = 0;
   int output = 0;
   int device = 0;
+  uint32_t flags = 0;
   void* slab[2] = {nullptr, nullptr};
   std::size_t workspace_bytes = 0;
   struct Slot {
@@ -160,6 +161,15 @@ rr_status rr_host_chain_destroy(rr_host_chain* plan) {
   return st(RR_SUCCESS, "success");
 }
 
+rr_status rr_host_chain_set_flags(rr_host_chain* plan, uint32_t flags) {
+  if (plan == nullptr) return st(RR_INVALID_ARGUMENT, "plan must not be null");
+  if ((flags & ~RR_HOST_CHAIN_INPUT_READY) != 0) {
+    return st(RR_INVALID_ARGUMENT, "unknown host chain flag");
+  }
+  plan->flags = flags;
+  return st(RR_SUCCESS, "success");
+}
+
 rr_status rr_chain_from_tokens_host(rr_host_chain* plan, const float* x_host,
                                     const float* router_weights, const float* logit_bias,
                                     const float* expert_weights, float* y_host,
@@ -177,10 +187,15 @@ rr_status rr_chain_from_tokens_host(rr_host_chain* plan, const float* x_host,
   }
   cudaStream_t s = static_cast<cudaStream_t>(ctx->stream);
   const int K = plan->hidden, E = plan->experts, N = plan->output;
-  // The call's work is ordered after the caller's earlier work on ctx->stream.
-  cudaError_t e = cudaEventRecord(plan->entry, s);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(plan->h2d, plan->entry, 0);
-  if (e != cudaSuccess) return st(RR_CUDA_ERROR, "host chain ordering failed", e);
+  // The call's work is ordered after the caller's earlier work on ctx->stream
+  // (the copies in too, unless the caller declared its input ready; slot
+  // reuse across calls is ordered by the per-slot events either way).
+  cudaError_t e = cudaSuccess;
+  if ((plan->flags & RR_HOST_CHAIN_INPUT_READY) == 0) {
+    e = cudaEventRecord(plan->entry, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(plan->h2d, plan->entry, 0);
+    if (e != cudaSuccess) return st(RR_CUDA_ERROR, "host chain ordering failed", e);
+  }
   const int chunks = tokens == 0 ? 0 : (tokens + plan->chunk - 1) / plan->chunk;
   for (int c = 0; c < chunks; ++c) {
     const int i = c & 1;

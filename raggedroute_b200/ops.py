@@ -344,15 +344,22 @@ class HostChain:
     """chain_from_tokens over host memory (rr_chain_from_tokens_host): chunks
     of `chunk_tokens` stream host -> device, through the chain and back on
     separate copy streams, overlapping the copies with the chain. Y is
-    bit-identical to chain_from_tokens over the whole batch."""
+    bit-identical to chain_from_tokens over the whole batch.
 
-    def __init__(self, chunk_tokens: int, hidden: int, experts: int, output: int):
+    input_ready=True (RR_HOST_CHAIN_INPUT_READY): x_host is complete when a
+    call is made, so its copies do not wait for earlier work on ctx.stream
+    and back-to-back calls overlap."""
+
+    def __init__(self, chunk_tokens: int, hidden: int, experts: int, output: int,
+                 input_ready: bool = False):
         self.chunk_tokens, self.hidden, self.experts, self.output = (chunk_tokens, hidden,
                                                                      experts, output)
         h = ctypes.c_void_p()
         check(lib().rr_host_chain_create(chunk_tokens, hidden, experts, output, ctypes.byref(h)),
               "rr_host_chain_create")
         self._h = h
+        if input_ready:
+            check(lib().rr_host_chain_set_flags(h, 1), "rr_host_chain_set_flags")
 
     def __call__(self, x_host: torch.Tensor, router_weights: torch.Tensor,
                  expert_weights: torch.Tensor, y_host: torch.Tensor,

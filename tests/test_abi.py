@@ -112,3 +112,9 @@ def test_cpp_contract_program(rrlib, tmp_path):
     res = subprocess.run([str(exe)], capture_output=True, text=True)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "all checks passed" in res.stdout
+
+
+def test_host_chain_flags_validation(rrlib):
+    lib = rrlib.lib()
+    st = lib.rr_host_chain_set_flags(None, 1)
+    assert st.code == rrlib.StatusCode.INVALID_ARGUMENT

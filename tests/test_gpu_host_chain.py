@@ -2,7 +2,8 @@
 memory must give the same Y (and routing decisions) bit for bit as
 rr_chain_from_tokens over the whole batch on the device: several chunks with
 a ragged last one, a batch smaller than one chunk, an empty batch, pageable
-host memory, and a plan reused across calls."""
+host memory, and a plan reused across calls (with and without the
+input-ready flag that lets back-to-back calls overlap)."""
 from __future__ import annotations
 
 import pytest
@@ -52,10 +53,13 @@ def test_host_chain_matches_device_chain(rrlib, cuda, tokens, chunk, pinned):
     assert torch.equal(y.view(torch.int32), ref.y.cpu().view(torch.int32))
 
 
-def test_host_chain_plan_reused_across_calls(rrlib, cuda):
+@pytest.mark.parametrize("input_ready", [False, True])
+def test_host_chain_plan_reused_across_calls(rrlib, cuda, input_ready):
+    """Calls queued back to back; with input_ready the copies of a call may
+    start while the previous call still computes (RR_HOST_CHAIN_INPUT_READY)."""
     from raggedroute_b200.workloads import normal
     wr, we, bias = _weights(cuda)
-    hc = rrlib.HostChain(700, K, E, N)
+    hc = rrlib.HostChain(700, K, E, N, input_ready=input_ready)
     xs = [normal((2100 + 333 * i, K), 1.0, 30 + i, "cpu").pin_memory() for i in range(3)]
     ys = [torch.empty(x.shape[0], N).pin_memory() for x in xs]
     stream = torch.cuda.Stream(cuda)

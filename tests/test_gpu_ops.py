@@ -158,7 +158,7 @@ def test_histogram_reset_kat(rrlib, cuda):
 
 @pytest.mark.parametrize("experts", [1, 8, 64, 256, 1024])
 @pytest.mark.parametrize("dist", ["uniform", "zipf", "one"])
-@pytest.mark.parametrize("routes", [1, 1000, 4099, 100_003, 1 << 20])
+@pytest.mark.parametrize("routes", [1, 1000, 4099, 100_003, 1 << 18, 1 << 20])
 def test_histogram_scan_fused_exact(rrlib, oracle, cuda, experts, dist, routes):
     from raggedroute_b200.workloads import route_ids
     ids_np = route_ids(routes, experts, dist, seed=routes + experts)
@@ -181,6 +181,25 @@ def test_histogram_scan_fused_exact(rrlib, oracle, cuda, experts, dist, routes):
     off2 = torch.empty(experts + 1, dtype=torch.int32, device=cuda)
     rrlib.exclusive_scan(counts2, off2, experts)
     assert np.array_equal(host(off2), offsets_ref)
+
+
+@pytest.mark.parametrize("experts,dist", [(256, "uniform"), (1, "one"), (1024, "zipf")])
+def test_histogram_scan_many_cta_path(rrlib, oracle, cuda, experts, dist):
+    """Above 256K routes the fused operator and the histogram merge CTAs
+    through global atomics (below, through one thread-block cluster)."""
+    from raggedroute_b200.workloads import route_ids
+    routes = (1 << 20) + 4093
+    ids_np = route_ids(routes, experts, dist, seed=experts + 77)
+    counts_ref = oracle.histogram(ids_np, experts)
+    ids = dev(ids_np, cuda)
+    counts = torch.full((experts,), 3, dtype=torch.int32, device=cuda)
+    offsets = torch.full((experts + 1,), 3, dtype=torch.int32, device=cuda)
+    rrlib.histogram_exclusive_scan(ids, counts, offsets, routes, experts)
+    assert np.array_equal(host(counts), counts_ref)
+    assert np.array_equal(host(offsets), oracle.exclusive_scan(counts_ref))
+    counts2 = torch.full((experts,), 3, dtype=torch.int32, device=cuda)
+    rrlib.histogram(ids, counts2, routes, experts)
+    assert np.array_equal(host(counts2), counts_ref)
 
 
 def test_scan_in_place_alias(rrlib, oracle, cuda):
