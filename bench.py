@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--ep-transport", choices=["auto", "peer", "nccl"], default="auto",
                     help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--stages", action="store_true", help="print the per-stage table to stderr")
+    ap.add_argument("--profile-once", action="store_true",
+                    help="one warm-up chain, then one validated untimed chain_from_tokens call "
+                         "(NVTX range per stage: raggedroute_<stage>) for profilers")
     ap.add_argument("--only-stage", default=None,
                     choices=["dense_gemm", "topk_gate", "histogram_exclusive_scan",
                              "token_permute", "grouped_gemm", "unpermute"],
@@ -286,6 +289,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if args.only_stage is not None:
         return run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n)
+    if args.profile_once:
+        return run_profile_once(torch, rr, stream, ctx, inp, buf, tokens, e)
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
 
@@ -490,6 +495,27 @@ def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) 
         times.append(evs[idx].elapsed_time(evs[idx + 1]))
     return {"stage": args.only_stage, "tokens": tokens, "ms": statistics.mean(times),
             "ms_min": min(times)}
+
+
+def run_profile_once(torch, rr, stream, ctx, inp, buf, tokens: int, e: int) -> dict:
+    """One warm-up chain, then exactly one untimed chain_from_tokens call for a
+    profiler (the library brackets each stage in an NVTX range named
+    raggedroute_<stage>), validated by the routing invariants: ids in [0, E),
+    counts summing to 2T, offsets their exclusive scan, y finite."""
+    for _ in range(2):
+        with torch.cuda.stream(stream):
+            rr.chain_from_tokens(inp.x, inp.router_w, inp.expert_w, buf,
+                                 logit_bias=inp.logit_bias, ctx=ctx)
+        stream.synchronize()
+    ids = buf.expert_ids
+    counts = buf.counts.to(torch.int64)
+    ok = (bool(((ids >= 0) & (ids < e)).all()) and int(counts.sum()) == 2 * tokens
+          and int(buf.offsets[0]) == 0
+          and torch.equal(buf.offsets[1:].to(torch.int64), torch.cumsum(counts, 0))
+          and bool(torch.isfinite(buf.y).all()))
+    if not ok:
+        raise RuntimeError("profile-once chain failed its routing invariants")
+    return {"profile_once": True, "tokens": tokens, "validated": ok}
 
 
 def small_config_latency(torch, rr, device, iters: int = 200) -> dict:

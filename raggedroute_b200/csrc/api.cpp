@@ -11,6 +11,7 @@
 // experts*4 bytes for inputs larger than one CTA chunk (the size query says
 // how much) and produces the stable slot order.
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <climits>
@@ -592,6 +593,18 @@ std::size_t get_chain_workspace_size(int tokens, int, int experts, int) noexcept
 
 namespace {
 
+// One NVTX push/pop range per chain stage ("raggedroute_<stage>") around its
+// launch, so a profiler can select a stage, e.g. ncu --nvtx --nvtx-include
+// "raggedroute_grouped_gemm/" (a '/' in a range name would read as nesting).
+// Without a tool attached a range is a null check (NVTX v3, header-only).
+class StageRange {
+ public:
+  explicit StageRange(const char* name) noexcept { nvtxRangePushA(name); }
+  ~StageRange() { nvtxRangePop(); }
+  StageRange(const StageRange&) = delete;
+  StageRange& operator=(const StageRange&) = delete;
+};
+
 Status validate_chain_shape(int tokens, int hidden, int experts, int output) noexcept {
   if (tokens < 0 || hidden < 0 || output < 0 || experts < 2 || experts > kMaxExperts) {
     return detail::invalid_argument("chain requires T,K,N>=0 and 2<=E<=1024");
@@ -611,43 +624,61 @@ Status chain_after_logits(const float* logits, const float* logit_bias, const fl
                           int experts, int output, const RuntimeContext& context,
                           bool gather_rows) noexcept {
   cudaStream_t stream = context.stream;
-  Status s = detail::cuda_status(
-      rrb::launch_topk_gate(logits, logit_bias, b.expert_ids, b.route_weights, tokens, experts,
-                            stream),
-      "chain topk_gate launch failed");
+  Status s = success_status();
+  {
+    StageRange r("raggedroute_topk_gate");
+    s = detail::cuda_status(rrb::launch_topk_gate(logits, logit_bias, b.expert_ids,
+                                                  b.route_weights, tokens, experts, stream),
+                            "chain topk_gate launch failed");
+  }
   if (!s.ok()) return s;
   const int routes = 2 * tokens;
-  s = detail::cuda_status(rrb::launch_histogram_exclusive_scan(b.expert_ids, b.counts, b.offsets,
-                                                               routes, experts, stream),
-                          "chain histogram_exclusive_scan launch failed");
+  {
+    StageRange r("raggedroute_histogram_exclusive_scan");
+    s = detail::cuda_status(rrb::launch_histogram_exclusive_scan(b.expert_ids, b.counts,
+                                                                 b.offsets, routes, experts,
+                                                                 stream),
+                            "chain histogram_exclusive_scan launch failed");
+  }
   if (!s.ok()) return s;
   if (gather_rows) {
     // Ranks only (no row copy); the grouped GEMM gathers its rows from x
     // through sorted_route, kept in the workspace.
     int32_t* sorted_route = reinterpret_cast<int32_t*>(
         static_cast<char*>(context.workspace) + chain_sorted_route_offset(tokens, experts));
-    s = detail::cuda_status(
-        rrb::launch_token_permute(x, b.expert_ids, b.offsets, nullptr, b.route_pos, sorted_route,
-                                  tokens, experts, 2, 0, context.workspace, stream),
-        "chain token_permute launch failed");
+    {
+      StageRange r("raggedroute_token_permute");
+      s = detail::cuda_status(
+          rrb::launch_token_permute(x, b.expert_ids, b.offsets, nullptr, b.route_pos,
+                                    sorted_route, tokens, experts, 2, 0, context.workspace,
+                                    stream),
+          "chain token_permute launch failed");
+    }
     if (!s.ok()) return s;
     const rrb::RowGather gather{x, sorted_route, 2};
+    StageRange r("raggedroute_grouped_gemm");
     s = detail::cuda_status(rrb::launch_grouped_gemm(x, expert_w, b.offsets, b.y_permuted,
                                                      experts, routes, hidden, output, stream, 0,
                                                      nullptr, &gather),
                             "chain grouped_gemm launch failed");
   } else {
-    s = detail::cuda_status(
-        rrb::launch_token_permute(x, b.expert_ids, b.offsets, b.x_permuted, b.route_pos, nullptr,
-                                  tokens, experts, 2, hidden, context.workspace, stream),
-        "chain token_permute launch failed");
+    {
+      StageRange r("raggedroute_token_permute");
+      s = detail::cuda_status(
+          rrb::launch_token_permute(x, b.expert_ids, b.offsets, b.x_permuted, b.route_pos,
+                                    nullptr, tokens, experts, 2, hidden, context.workspace,
+                                    stream),
+          "chain token_permute launch failed");
+    }
     if (!s.ok()) return s;
+    StageRange r("raggedroute_grouped_gemm");
     s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, expert_w, b.offsets,
                                                      b.y_permuted, experts, routes, hidden,
                                                      output, stream),
                             "chain grouped_gemm launch failed");
   }
   if (!s.ok()) return s;
+  StageRange r("raggedroute_unpermute");
   return detail::cuda_status(rrb::launch_unpermute(b.y_permuted, b.route_pos, b.route_weights,
                                                    b.y, tokens, 2, output, stream),
                              "chain unpermute launch failed");
@@ -704,10 +735,13 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
     return detail::make_status(StatusCode::kInsufficientWorkspace,
                                "chain requires the queried workspace");
   }
-  s = detail::cuda_status(
-      rrb::launch_grouped_gemm(args.x, args.router_weights, nullptr, args.buffers.logits, 1,
-                               args.tokens, args.hidden, args.experts, context.stream),
-      "chain dense_gemm launch failed");
+  {
+    StageRange r("raggedroute_dense_gemm");
+    s = detail::cuda_status(
+        rrb::launch_grouped_gemm(args.x, args.router_weights, nullptr, args.buffers.logits, 1,
+                                 args.tokens, args.hidden, args.experts, context.stream),
+        "chain dense_gemm launch failed");
+  }
   if (!s.ok()) return s;
   return chain_after_logits(args.buffers.logits, args.logit_bias, args.x, args.expert_weights,
                             args.buffers, args.tokens, args.hidden, args.experts, args.output,
