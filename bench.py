@@ -13,7 +13,8 @@ through libraggedroute_b200's C ABI on one stream. `value` is device-timed
 (CUDA events, inputs resident in HBM, max over ranks); `e2e` is the same
 metric with X in pinned host memory and Y returned to host memory every step
 (one GPU: rr_chain_from_tokens_host, which overlaps the PCIe copies of
-token chunks with the chain; expert parallelism: copy in, EP step, copy out).
+token chunks with the chain; expert parallelism: ep.HostPipeline, copy in,
+EP step, copy out, with each step's copies overlapping its neighbours).
 Extra keys on one GPU: `cold_scrub` (the C5 step with 256 MiB written to
 flush L2 before every step) and `small_configs` (C1 chain_from_tokens and C2
 chain_from_logits latency, eager and replayed from a captured CUDA graph).
@@ -367,17 +368,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             # overlap (the next step's copies in run while this one finishes).
             host_chain = rr.HostChain(args.e2e_chunk, k, e, n, input_ready=True)
         else:
-            x_dev = torch.empty_like(inp.x)
+            from raggedroute_b200.ep import HostPipeline
+            ep_host = HostPipeline(ep, ep_buf, tokens, device)
 
         def e2e_step():
             if ep is None:
                 host_chain(x_host, inp.router_w, inp.expert_w, y_host,
                            logit_bias=inp.logit_bias, ctx=ctx)
                 return
-            x_dev.copy_(x_host, non_blocking=True)
-            ep.chain_from_tokens(x_dev, inp.router_w, local_w, ep_buf,
-                                 logit_bias=inp.logit_bias, expert_remap=remap, ctx=ctx)
-            y_host.copy_(ep_buf.y, non_blocking=True)
+            ep_host(x_host, inp.router_w, local_w, y_host, logit_bias=inp.logit_bias,
+                    expert_remap=remap, ctx=ctx)
 
         with torch.cuda.stream(stream):
             for _ in range(max(1, args.warmup)):
@@ -401,7 +401,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                "d2h_bytes_per_step": y_host.numel() * 4,
                "api": ("rr_chain_from_tokens_host (input-ready plan: consecutive steps "
                        "overlap), chunk %d tokens" % args.e2e_chunk
-                       if ep is None else "copy in + rr_ep_chain_from_tokens + copy out")}
+                       if ep is None else "raggedroute_b200.ep.HostPipeline: copy in, "
+                       "rr_ep_chain_from_tokens, copy out, overlapped across steps")}
         if ep is None:
             host_chain.close()
 

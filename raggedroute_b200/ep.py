@@ -7,6 +7,7 @@ its own NCCL communicator and does every exchange itself.
 from __future__ import annotations
 
 import ctypes
+import dataclasses
 
 import torch
 import torch.distributed as dist
@@ -87,6 +88,63 @@ class ExpertParallel:
             self.close()
         except Exception:  # noqa: BLE001 - interpreter shutdown
             pass
+
+
+class HostPipeline:
+    """ExpertParallel.chain_from_tokens over host memory, pipelined across
+    calls: X is copied in on one copy stream into one of two device slots,
+    the step runs on ctx.stream, and Y is copied out on another copy stream
+    from one of two output slots. A call's copy in waits only for the step two
+    calls back to have finished reading its slot, so it overlaps the previous
+    step's compute and copy out (x_host must be complete when the call is
+    made, as with RR_HOST_CHAIN_INPUT_READY). Completion, Y in y_host
+    included, is ordered on ctx.stream. All other chain buffers are shared
+    between the slots: they are used only on ctx.stream, in call order.
+    x_host / y_host should be pinned. Y equals ExpertParallel.chain_from_tokens
+    on the same tokens bit for bit."""
+
+    def __init__(self, ep: ExpertParallel, buf: ChainBuffers, max_tokens: int, device):
+        self.ep, self.buf = ep, buf
+        self.x_dev = [torch.empty(max_tokens, ep.hidden, device=device) for _ in range(2)]
+        self.y_dev = [torch.empty(max_tokens, ep.output, device=device) for _ in range(2)]
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        ev = lambda: [torch.cuda.Event() for _ in range(2)]  # noqa: E731
+        self.h2d_done, self.compute_done, self.d2h_done = ev(), ev(), ev()
+        self.calls = 0
+
+    def __call__(self, x_host: torch.Tensor, router_weights: torch.Tensor,
+                 local_expert_weights: torch.Tensor, y_host: torch.Tensor,
+                 logit_bias: torch.Tensor | None = None,
+                 expert_remap: torch.Tensor | None = None,
+                 ctx: Context | None = None) -> torch.Tensor:
+        tokens = x_host.shape[0]
+        if tokens > self.x_dev[0].shape[0]:
+            raise ValueError("more tokens than the pipeline was sized for")
+        slot = self.calls & 1
+        first_use = self.calls < 2
+        self.calls += 1
+        main = torch.cuda.ExternalStream(ctx.stream) if ctx is not None and ctx.stream \
+            else torch.cuda.current_stream()
+        x, y = self.x_dev[slot][:tokens], self.y_dev[slot][:tokens]
+        if not first_use:
+            self.h2d.wait_event(self.compute_done[slot])
+        with torch.cuda.stream(self.h2d):
+            x.copy_(x_host, non_blocking=True)
+            self.h2d_done[slot].record(self.h2d)
+        main.wait_event(self.h2d_done[slot])
+        if not first_use:
+            main.wait_event(self.d2h_done[slot])
+        buf = dataclasses.replace(self.buf, y=y)
+        self.ep.chain_from_tokens(x, router_weights, local_expert_weights, buf,
+                                  logit_bias=logit_bias, expert_remap=expert_remap, ctx=ctx)
+        self.compute_done[slot].record(main)
+        self.d2h.wait_event(self.compute_done[slot])
+        with torch.cuda.stream(self.d2h):
+            y_host.copy_(y, non_blocking=True)
+            self.d2h_done[slot].record(self.d2h)
+        main.wait_event(self.d2h_done[slot])
+        return y_host
 
 
 def plan(count_all, rank: int):

@@ -1,7 +1,8 @@
 """Expert-parallel chain on the GPU.
 
 * One rank (no communicator): rr_ep_chain_from_tokens equals
-  rr_chain_from_tokens bit for bit.
+  rr_chain_from_tokens bit for bit, also through HostPipeline (host memory,
+  calls overlapped).
 * Two or more GPUs: tests/ep_worker.py under torchrun, for both transports
   (peer memory and NCCL) and with equal or ragged per-rank token counts
   (one rank idle); every rank's EP output must equal its single-GPU chain bit
@@ -39,6 +40,33 @@ def test_ep_single_rank_matches_chain(rrlib, cuda):
     assert torch.equal(b1.route_pos, b2.route_pos)
     assert torch.equal(b1.y.view(torch.int32), b2.y.view(torch.int32))
     assert ep.last_step_rows() == (2 * t, 2 * t)
+    ep.close()
+
+
+def test_ep_host_pipeline_matches_chain(rrlib, cuda):
+    """HostPipeline: three batches of different sizes queued back to back
+    over pinned host memory; each Y equals the device chain bit for bit."""
+    from raggedroute_b200.ep import ExpertParallel, HostPipeline
+    from raggedroute_b200.workloads import normal, zipf_log_bias
+    t, k, e, n = 1500, 256, 64, 128
+    wr = normal((k, e), 1 / 16, 12, cuda)
+    we = normal((e, k, n), 1 / 16, 13, cuda)
+    bias = torch.from_numpy(zipf_log_bias(e, 1.0)).to(cuda)
+    ep = ExpertParallel(e, t, k, n, rank=0, world=1)
+    buf = rrlib.ChainBuffers.allocate(t, k, e, n, cuda)
+    stream = torch.cuda.Stream(cuda)
+    ctx = rrlib.Context(stream=stream.cuda_stream)
+    pipe = HostPipeline(ep, buf, t, cuda)
+    xs = [normal((m, k), 1.0, 40 + m, "cpu").pin_memory() for m in (1500, 999, 1300)]
+    ys = [torch.empty(x.shape[0], n).pin_memory() for x in xs]
+    for x, y in zip(xs, ys):
+        pipe(x, wr, we, y, logit_bias=bias, ctx=ctx)
+    stream.synchronize()
+    for x, y in zip(xs, ys):
+        ref = rrlib.ChainBuffers.allocate(x.shape[0], k, e, n, cuda)
+        rrlib.chain_from_tokens(x.to(cuda), wr, we, ref, logit_bias=bias)
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int32), ref.y.cpu().view(torch.int32))
     ep.close()
 
 
