@@ -36,8 +36,10 @@
 // memory (expert-parallel combine, skipped once the abort fence is set).
 // Warps are specialised:
 //   warp 0     TMA producer: A (x rows, K-major, 64-byte swizzle) and B (the
-//              expert's [K, N] weights, N-major, 128-byte swizzle) per 16-wide
-//              k-block into a 4-slot raw ring; no multicast.
+//              expert's [K, N] weights, N-major, unswizzled) per 16-wide
+//              k-block into a 5-slot raw ring, one box each (measured: eight
+//              2 KB B boxes per k-block instead of one cost 5% at C5); no
+//              multicast.
 //   warp 1     MMA issuer: 3 tcgen05.mma (M=128, N<=256, K=8) per k-step into
 //              P; it waits for P to be promoted before the next chunk.
 //   warps 2-17 workers (16 warps = 4 TMEM lane quarters x 4 column groups):
@@ -72,10 +74,9 @@ using namespace sm100;
 constexpr int kBM = 128;                           // output rows per tile = TMEM lanes
 constexpr int kBN = 256;                           // output columns per tile
 constexpr int kBK = 16;                            // fp32 elements per k-block
-constexpr int kRawStages = 4;                      // TMA ring
+constexpr int kRawStages = 5;                      // TMA ring (5 vs 4: 8.90 -> 8.52 ms at C5)
 constexpr int kOpStages = 2;                       // hi/lo operand ring
 constexpr int kABytes = kBM * kBK * 4;             // 8 KB (64 B rows)
-constexpr int kBChunkBytes = 32 * kBK * 4;         // 2 KB: 32 columns x 16 k rows
 constexpr int kBBytes = kBN * kBK * 4;             // 16 KB
 constexpr int kRawBytes = kABytes + kBBytes;       // 24 KB: A raw | B raw (N-major)
 constexpr int kOpBytes = 2 * (kABytes + kBBytes);  // 48 KB: A hi | A lo | B hi | B lo
@@ -108,6 +109,7 @@ struct alignas(1024) Smem {
 };
 
 constexpr std::size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "over the 227 KB of shared memory a CTA may use");
 
 struct TileGeom {
   int expert, row0, row_end, base, col0, ncols, n_mma;
@@ -149,10 +151,12 @@ __device__ __forceinline__ int kmajor64_offset(int r, int kc) {
   return r * 64 + ((kc ^ ((r >> 1) & 3)) << 4);
 }
 
-// Element (k, n) of the N-major raw B tile: 32-column chunks of 16 rows x
-// 128 bytes with the 128-byte swizzle.
-__device__ __forceinline__ int nmajor128_offset(int k, int n) {
-  return (n >> 5) * kBChunkBytes + k * 128 + ((((n & 31) >> 2) ^ (k & 7)) << 4) + ((n & 3) << 2);
+// Element (k, n) of the raw B tile as TMA stores it: N-major, unswizzled,
+// 16 rows of kTileN columns (a warp reading 32 consecutive n of one row
+// touches 128 contiguous bytes, so the transposing reads are conflict-free).
+template <int kTileN>
+__device__ __forceinline__ int nmajor_plain_offset(int k, int n) {
+  return k * (kTileN * 4) + n * 4;
 }
 
 // kGather: A rows come from x through a row map (RowGather) instead of a TMA
@@ -231,14 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const int chunk = lane & 3;
     for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
       const TileGeom g = geom<kMT>(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
-      const int nchunks = (g.ncols + 31) >> 5;
       int tok[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int row = g.base + 8 * j + (lane >> 2);
         tok[j] = row >= 0 ? __ldg(gather.route + row) / gather.div : -1;
       }
-      const uint32_t bbytes = nchunks * kBChunkBytes;
+      const uint32_t bbytes = kTileN * kBK * 4;
       for (int kb = 0; kb < num_kb; ++kb) {
         int ok = 1;
         if (lane == 0) ok = mbar_wait(&s.raw_empty[stage], phase ^ 1u, err, failed);
@@ -255,10 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         cp_async_arrive(&s.raw_full[stage]);
         if (lane == 0) {
           mbar_arrive_expect_tx(&s.raw_full[stage], bbytes);
-          for (int j = 0; j < nchunks; ++j) {
-            tma_load_3d(st + kOBRaw + j * kBChunkBytes, &tma_b, &s.raw_full[stage],
-                        g.col0 + 32 * j, kb * kBK, g.expert % wsets);
-          }
+          tma_load_3d(st + kOBRaw, &tma_b, &s.raw_full[stage], g.col0, kb * kBK,
+                      g.expert % wsets);
           s.issued[stage] += 1;
         }
         if (++stage == kRawStages) {
@@ -276,8 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
         const TileGeom g = geom<kMT>(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
-        const int nchunks = (g.ncols + 31) >> 5;
-        const uint32_t bytes = kAB + nchunks * kBChunkBytes;
+        // A full-width B box even for a narrow last tile: columns past N
+        // are zero-filled by TMA and still count toward the transaction bytes.
+        const uint32_t bytes = kAB + kTileN * kBK * 4;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&s.raw_empty[stage], phase ^ 1u, err, failed)) break;
           uint8_t* st = s.raw[stage];
@@ -286,10 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
           for (int m = 0; m < kMT; ++m) {
             tma_load_2d(st + m * kABytes, &tma_a, &s.raw_full[stage], kb * kBK, g.base + m * kBM);
           }
-          for (int j = 0; j < nchunks; ++j) {
-            tma_load_3d(st + kOBRaw + j * kBChunkBytes, &tma_b, &s.raw_full[stage],
-                        g.col0 + 32 * j, kb * kBK, g.expert % wsets);
-          }
+          tma_load_3d(st + kOBRaw, &tma_b, &s.raw_full[stage], g.col0, kb * kBK,
+                      g.expert % wsets);
           s.issued[stage] += 1;
           if (++stage == kRawStages) {
             stage = 0;
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         const int kc = (it >> 5) & 3;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          bsrc[i][j] = static_cast<uint32_t>(nmajor128_offset(4 * kc + j, n));
+          bsrc[i][j] = static_cast<uint32_t>(nmajor_plain_offset<kTileN>(4 * kc + j, n));
         }
         bdst[i] = static_cast<uint32_t>(kmajor64_offset(n, kc));
       }
@@ -646,16 +646,20 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
       return cudaErrorInvalidValue;
     }
   }
+  const int mt = (offsets == nullptr && output <= kBN / 2 && gather == nullptr &&
+                  scatter == nullptr && rows >= 2LL * kBM * sm_count())
+                     ? 2
+                     : 1;
   {
     // B: W [experts, hidden, output] viewed as {output, hidden, experts}.
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(output), static_cast<cuuint64_t>(hidden),
                                 static_cast<cuuint64_t>(wsets)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(output) * 4,
                                    static_cast<cuuint64_t>(output) * hidden * 4};
-    const cuuint32_t box[3] = {32, kBK, 1};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBN / mt), kBK, 1};
     const cuuint32_t elem[3] = {1, 1, 1};
     if (encode(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(w), dims, strides, box,
-               elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
       return cudaErrorInvalidValue;
@@ -665,10 +669,6 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
   // rows to fill every SM with 256-row tiles: two m-tiles per CTA share each
   // B tile (measured at C5: 0.68 -> 0.48 ms). Smaller problems keep 128-row
   // tiles for parallelism.
-  const int mt = (offsets == nullptr && output <= kBN / 2 && gather == nullptr &&
-                  scatter == nullptr && rows >= 2LL * kBM * sm_count())
-                     ? 2
-                     : 1;
   int grid = sm_count();
   if (offsets == nullptr) {
     const long long tiles = static_cast<long long>((rows + kBM * mt - 1) / (kBM * mt)) *
