@@ -6,24 +6,29 @@
 // every segment are untouched. The dense router GEMM is the same kernel with
 // one implicit group.
 //
-// 3xTF32: every operand element v is split into hi = rna_tf32(v) and
-// lo = rna_tf32(v - hi) (v - hi is exact in FP32). Per k-step the tensor core
-// accumulates lo_a*hi_b + hi_a*lo_b + hi_a*hi_b into an FP32 TMEM
-// accumulator; the dropped lo_a*lo_b term and the TF32 rounding of lo are
-// below 2^-21 relative per product. The tensor core's own accumulate step
-// loses precision with a consistent bias (measured: 2.9e-5 normwise at
-// K=4096), so the accumulator is promoted every 512 of K: each chunk is
-// accumulated from zero into the partial P (TMEM columns 0-255) and added,
-// with round-to-nearest FP32 adds on the CUDA cores, into the running sum S
-// (TMEM columns 256-511). The last chunk's S + P goes straight to global.
-// rna_tf32 is done on the bit pattern with integer adds (sm100.cuh,
-// tf32_rna): the conversion instruction issues at a fraction of the integer
-// rate and the split is on the critical path (measured: 8.8 ms -> 6.9 ms for
-// the split alone at C5, bit-identical results).
+// 3xTF32: every operand element v is split into hi and lo = v - hi (exact in
+// FP32) and per k-step the tensor core accumulates lo_a*hi_b + hi_a*lo_b +
+// hi_a*hi_b into an FP32 TMEM accumulator. B (the weights): hi =
+// rna_tf32(v), lo = rna_tf32(v - hi). A (the tokens): hi = v with its low
+// 13 mantissa bits dropped, which is exactly what a kind::tf32 MMA reads
+// from raw FP32 bits, so the MMA takes A hi straight from the TMA'd raw tile
+// and only A lo is written (the MMA keeps the top 11 of its up to 13
+// significant bits). The dropped lo_a*lo_b term and the TF32 truncation or
+// rounding of lo stay below 2^-20 relative per product (measured at C5:
+// 3.73e-6 normwise against FP64, 3.60e-6 with a rounded A hi). The tensor
+// core's own accumulate step loses precision with a consistent bias
+// (measured: 2.9e-5 normwise at K=4096), so the accumulator is promoted every
+// 512 of K: each chunk is accumulated from zero into the partial P (TMEM
+// columns 0-255) and added, with round-to-nearest FP32 adds on the CUDA
+// cores, into the running sum S (TMEM columns 256-511). The last chunk's
+// S + P goes straight to global. rna_tf32 is done on the bit pattern with
+// integer adds (sm100.cuh, tf32_rna): the conversion instruction issues at a
+// fraction of the integer rate and the split is on the critical path.
 //
-// Measured at C5 (T=65536, K=4096, E=128, N=1408) on one B200, per launch:
-// the MMAs alone (operands never loaded or split) take 6.4 ms, with TMA
-// loads 8.1 ms, the split alone 6.9 ms, everything ~9.3 ms.
+// Measured at C5 (T=65536, K=4096, E=128, N=1408) on one B200, per launch
+// (diagnostic builds of this kernel): the MMAs with TMA loads but no split
+// work 6.1 ms; the split with TMA loads but no MMAs 7.7 ms; the TMA loads
+// and barrier hand-offs alone 3.7 ms; everything 8.1 ms.
 //
 // Structure: a persistent CTA per SM walks the device-side tile schedule
 // (tile_sched.cuh, read from offsets, no host sync). Tiles are 128 rows x 256
@@ -41,13 +46,17 @@
 //              2 KB B boxes per k-block instead of one cost 5% at C5); no
 //              multicast.
 //   warp 1     MMA issuer: 3 tcgen05.mma (M=128, N<=256, K=8) per k-step into
-//              P; it waits for P to be promoted before the next chunk.
+//              P, A hi from the raw slot, the rest from the operand slot; its
+//              commit releases both slots. It waits for P to be promoted
+//              before the next chunk.
 //   warps 2-17 workers (16 warps = 4 TMEM lane quarters x 4 column groups):
-//              (a) split: hi/lo of each landed k-block into a 2-slot operand
-//              ring. kind::tf32 MMAs take K-major operands only (an N-major B
-//              reads as zeros on sm_100a), so B is transposed to K-major here
-//              with a bank-conflict-free lane mapping; the raw slot is released
-//              as soon as it has been read.
+//              (a) split: A lo and B hi/lo of each landed k-block into a
+//              2-slot operand ring. kind::tf32 MMAs take K-major operands
+//              only here (an N-major B read as zeros when tried), so B is
+//              transposed to K-major with a bank-conflict-free lane mapping.
+//              With row gathering the raw A tile is unswizzled, so A hi is
+//              written to the operand slot too and the workers release the
+//              raw slot as soon as they have read it.
 //              (b) promotion: S = P, S += P, or y = S + P for the tile's last
 //              chunk, each thread covering 64 columns of one TMEM lane.
 //              Promotion of chunk c runs after the first k-block of the next
@@ -145,6 +154,20 @@ __device__ __forceinline__ void split4(const float4 v, float4& h, float4& l) {
   l.w = tf32_rna(v.w - h.w);
 }
 
+// A operand split: hi = v with the low 13 mantissa bits cleared (the value
+// a kind::tf32 MMA reads from the raw FP32 bits), lo = v - hi (exact in FP32,
+// up to 13 significant bits, of which the MMA keeps the top 11).
+__device__ __forceinline__ void split_trunc4(const float4 v, float4& h, float4& l) {
+  h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+  h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+  h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+  h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+  l.x = v.x - h.x;
+  l.y = v.y - h.y;
+  l.z = v.z - h.z;
+  l.w = v.w - h.w;
+}
+
 // Byte offset of 16-byte chunk kc (k = 4*kc..4*kc+3) of row r in a K-major
 // tile of 16 fp32 per row with the 64-byte swizzle (TMA and UMMA agree on it).
 __device__ __forceinline__ int kmajor64_offset(int r, int kc) {
@@ -193,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     for (int i = 0; i < kRawStages; ++i) {
       // Gathering: the producer's expect_tx plus one cp.async arrival per lane.
       mbar_init(&s.raw_full[i], kGather ? 33 : 1);
-      mbar_init(&s.raw_empty[i], kWorkerWarps);
+      mbar_init(&s.raw_empty[i], kGather ? kWorkerWarps : 1);
       s.issued[i] = 0;
     }
     for (int i = 0; i < kOpStages; ++i) {
@@ -303,6 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      int rstage = 0;
+      uint32_t rphase = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok && !*failed; t += gridDim.x) {
@@ -317,12 +342,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
           const uint32_t d = tmem + kColP;
           const int kend = min(num_kb, kc + kChunkKb);
           for (int kb = kc; kb < kend; ++kb) {
-            if (!mbar_wait(&s.op_full[stage], phase, err, failed)) {
+            if (!mbar_wait(&s.op_full[stage], phase, err, failed) ||
+                (!kGather && !mbar_wait(&s.raw_full[rstage], rphase, err, failed))) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t base = smem_u32(s.op[stage]);
+            const uint32_t rawb = smem_u32(s.raw[rstage]);
             const uint32_t b_hi = base + kOBHi;
             const uint32_t b_lo = base + kOBLo;
 #pragma unroll
@@ -335,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
               const uint32_t first = (kb == kc && ks == 0) ? 0u : 1u;
 #pragma unroll
               for (int m = 0; m < kMT; ++m) {
-                const uint32_t a_hi = base + kOAHi + m * kABytes;
+                const uint32_t a_hi = kGather ? base + kOAHi + m * kABytes : rawb + m * kABytes;
                 const uint32_t a_lo = base + kOALo + m * kABytes;
                 const uint64_t ah = smem_desc(a_hi + ks * 32, 16, 512, Swizzle::k64B);
                 const uint64_t al = smem_desc(a_lo + ks * 32, 16, 512, Swizzle::k64B);
@@ -346,9 +373,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
               }
             }
             mma_commit(&s.op_empty[stage]);
+            if (!kGather) mma_commit(&s.raw_empty[rstage]);
             if (++stage == kOpStages) {
               stage = 0;
               phase ^= 1u;
+            }
+            if (++rstage == kRawStages) {
+              rstage = 0;
+              rphase ^= 1u;
             }
           }
           if (!ok) break;
@@ -442,8 +474,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         float4 h, l;
 #pragma unroll
         for (int m = 0; m < kMT; ++m) {
-          split4(av[m], h, l);
-          sts_v4(op + kOAHi + m * kABytes + a_dst, h);
+          // A: hi = v with its low 13 mantissa bits dropped, which is how the
+          // MMA reads the raw tile (so without gathering it reads hi straight
+          // from the raw slot), lo = v - hi (exact).
+          split_trunc4(av[m], h, l);
+          if constexpr (kGather) sts_v4(op + kOAHi + m * kABytes + a_dst, h);
           sts_v4(op + kOALo + m * kABytes + a_dst, l);
         }
 #pragma unroll
@@ -459,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&s.raw_empty[rstage]);
+          if (kGather) mbar_arrive(&s.raw_empty[rstage]);
           mbar_arrive(&s.op_full[ostage]);
         }
         if (++rstage == kRawStages) {
