@@ -379,8 +379,17 @@ cudaError_t launch_hist_cluster(const int32_t* ids, int32_t* counts, int32_t* of
   const cudaError_t err =
       cudaLaunchKernelEx(&cfg, hist_cluster_kernel<kScan>, ids, counts, offsets, routes, experts,
                          vec);
+  if (err != cudaSuccess) return err;
   note_launch();
-  return err != cudaSuccess ? err : cudaGetLastError();
+  return cudaGetLastError();
+}
+
+// A cluster launch the device cannot place (an MPS or MIG share with fewer
+// SMs per GPC, for instance) is refused at launch time without touching the
+// stream; the caller then takes the many-CTA path instead.
+bool cluster_launch_refused(cudaError_t e) {
+  return e == cudaErrorClusterOutOfResources || e == cudaErrorInvalidClusterSize ||
+         e == cudaErrorNotSupported || e == cudaErrorInvalidConfiguration;
 }
 
 int hist_grid(long long routes) {
@@ -404,8 +413,10 @@ cudaError_t launch_histogram_accumulate(const int32_t* ids, int32_t* counts, int
 cudaError_t launch_histogram(const int32_t* ids, int32_t* counts, int routes, int experts,
                              cudaStream_t stream) {
   if (routes > kFusedSingleCtaMaxRoutes && routes <= kClusterMaxRoutes) {
-    return launch_hist_cluster<false>(ids, counts, nullptr, routes, experts, aligned_to(ids, 16),
-                                      stream);
+    const cudaError_t e = launch_hist_cluster<false>(ids, counts, nullptr, routes, experts,
+                                                     aligned_to(ids, 16), stream);
+    if (!cluster_launch_refused(e)) return e;
+    cudaGetLastError();
   }
   cudaError_t err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * experts, stream);
   if (err != cudaSuccess) return err;
@@ -430,7 +441,10 @@ cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
     return cudaGetLastError();
   }
   if (routes <= kClusterMaxRoutes) {
-    return launch_hist_cluster<true>(ids, counts, offsets, routes, experts, vec, stream);
+    const cudaError_t e =
+        launch_hist_cluster<true>(ids, counts, offsets, routes, experts, vec, stream);
+    if (!cluster_launch_refused(e)) return e;
+    cudaGetLastError();
   }
   cudaError_t err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * experts, stream);
   if (err != cudaSuccess) return err;
