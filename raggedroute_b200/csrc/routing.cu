@@ -388,7 +388,7 @@ cudaError_t launch_hist_cluster(const int32_t* ids, int32_t* counts, int32_t* of
 // SMs per GPC, for instance) is refused at launch time without touching the
 // stream; the caller then takes the many-CTA path instead.
 bool cluster_launch_refused(cudaError_t e) {
-  return e == cudaErrorClusterOutOfResources || e == cudaErrorInvalidClusterSize ||
+  return e == cudaErrorInvalidClusterSize || e == cudaErrorLaunchOutOfResources ||
          e == cudaErrorNotSupported || e == cudaErrorInvalidConfiguration;
 }
 
