@@ -44,11 +44,16 @@ struct ChunkPlan {
   int chunks;
 };
 
-ChunkPlan plan_chunks(int tokens, int top_k) {
+// The per-chunk expert table (chunks x experts int32) is kept to 1 MB: with
+// many experts the chunks grow instead (fewer, longer chunks).
+constexpr long long kMaxChunkTable = 1 << 18;
+
+ChunkPlan plan_chunks(int tokens, int top_k, int experts) {
   const long long routes = static_cast<long long>(tokens) * top_k;
   long long want = (routes + kTargetChunks - 1) / kTargetChunks;
   long long rc = 128;
   while (rc < want && rc < kMaxChunkRoutes) rc <<= 1;
+  while (rc < kMaxChunkRoutes && ((routes + rc - 1) / rc) * experts > kMaxChunkTable) rc <<= 1;
   int tc = static_cast<int>(rc / top_k);
   if (tc < 1) tc = 1;
   ChunkPlan p;
@@ -470,7 +475,7 @@ std::size_t permute_workspace_bytes(int tokens, int experts, int top_k) {
   if (experts <= 0) return 0;
   const std::size_t cursors = static_cast<std::size_t>(experts) * sizeof(int32_t);
   if (tokens <= 0 || top_k <= 0) return cursors;
-  const ChunkPlan p = plan_chunks(tokens, top_k);
+  const ChunkPlan p = plan_chunks(tokens, top_k, experts);
   if (p.chunks <= 1) return cursors;
   return align256(cursors) + static_cast<std::size_t>(p.chunks) * experts * sizeof(int32_t);
 }
@@ -483,7 +488,7 @@ cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offs
                          int experts, int top_k, int hidden, void* workspace,
                          const PeerDispatch& peer, cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  const ChunkPlan p = plan_chunks(tokens, top_k);
+  const ChunkPlan p = plan_chunks(tokens, top_k, experts);
   int32_t* cursors = static_cast<int32_t*>(workspace);
   int32_t* chunk_base = nullptr;
   const int routes_per_chunk = p.tokens_per_chunk * top_k;
