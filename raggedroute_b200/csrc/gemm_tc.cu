@@ -89,6 +89,7 @@ constexpr int kABytes = kBM * kBK * 4;             // 8 KB (64 B rows)
 constexpr int kBBytes = kBN * kBK * 4;             // 16 KB
 constexpr int kRawBytes = kABytes + kBBytes;       // 24 KB: A raw | B raw (N-major)
 constexpr int kOpBytes = 2 * (kABytes + kBBytes);  // 48 KB: A hi | A lo | B hi | B lo
+                                                   // (A hi only used when gathering)
 constexpr int kChunkKb = 32;                       // k-blocks per promoted chunk (K = 512)
 constexpr uint32_t kColP = 0;                      // TMEM columns of the chunk partial
 constexpr uint32_t kColS = kBN;                    // TMEM columns of the running sum
@@ -193,7 +194,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const RowGather gather) {
   static_assert(kMT == 1 || (kMT == 2 && !kGather), "two m-tiles only for the plain path");
   // Layout of a raw stage: A (kMT x 8 KB) | B (kTileN columns); of an operand
-  // stage: A hi | A lo | B hi | B lo. Both total the same bytes for kMT 1, 2.
+  // stage: A hi | A lo | B hi | B lo (A hi written only when gathering; else
+  // the MMA reads A hi from the raw stage). Both total the same bytes for
+  // kMT 1, 2.
   constexpr int kTileN = kBN / kMT;
   constexpr int kAB = kABytes * kMT;
   constexpr int kOBRaw = kAB;
