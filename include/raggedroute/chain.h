@@ -37,6 +37,9 @@ struct ChainFromTokensArgs {
   // The grouped GEMM gathers its rows from x through sorted_route (kept in
   // the workspace); buffers.x_permuted is not written and may be null.
   bool gather_rows = false;
+  // expert_weights is a buffer filled by rr_prepare_expert_weights (new: no
+  // reference counterpart), not W itself; K and N multiples of 4.
+  bool prepared_weights = false;
 };
 
 struct ChainFromLogitsArgs {
@@ -48,7 +51,8 @@ struct ChainFromLogitsArgs {
   int hidden = 0;
   int experts = 0;
   int output = 0;
-  bool gather_rows = false;  // as in ChainFromTokensArgs
+  bool gather_rows = false;       // as in ChainFromTokensArgs
+  bool prepared_weights = false;  // as in ChainFromTokensArgs
 };
 
 // Buffers of the post-route chain (top_k routes per token, R = T * top_k).

@@ -162,9 +162,32 @@ size_t rr_unpermute_workspace_size(int tokens, int top_k, int output);
  * RR_CHAIN_IMPL_GATHER_ROWS has the grouped GEMM gather its rows from x
  * through sorted_route (the permute only ranks), so x_permuted is not
  * written (may be NULL) and the permute's row copy and the GEMM's re-read
- * of it disappear; outputs are bit-identical. Any other id is
+ * of it disappear; outputs are bit-identical. RR_CHAIN_IMPL_PREPARED_WEIGHTS
+ * (token and logit chains) takes expert_weights as a buffer filled by
+ * rr_prepare_expert_weights (below). Any other id is
  * RR_UNSUPPORTED_KERNEL_VARIANT. */
 #define RR_CHAIN_IMPL_GATHER_ROWS 1u
+#define RR_CHAIN_IMPL_PREPARED_WEIGHTS 2u
+
+/* ---- prepared expert weights (new: no reference counterpart) -------------
+ * For expert weights that stay fixed across calls (inference), the B side
+ * of the 3xTF32 split is done once: W [E][K][N] is written as two K-major
+ * arrays [E][N][K], hi = W and lo = W - (W with its low 13 mantissa bits
+ * cleared), into a caller buffer of rr_prepared_expert_weights_size bytes
+ * (256-byte aligned; 2x the weights). The grouped GEMM then loads both B
+ * operands ready for its MMAs and splits only the token rows. K and N must
+ * be multiples of 4. Results differ from the raw-weight path in the last
+ * bits (B hi is truncated instead of rounded); both hold the FP32 contract. */
+size_t rr_prepared_expert_weights_size(int experts, int hidden, int output);
+rr_status rr_prepare_expert_weights(const float* expert_weights, int experts, int hidden,
+                                    int output, void* prepared, size_t prepared_bytes,
+                                    const rr_context* ctx);
+/* grouped_gemm on prepared weights: y_permuted[r] = x_permuted[r] . W[e]
+ * for r in [offsets[e], offsets[e+1]). */
+rr_status rr_grouped_gemm_prepared(const float* x_permuted, const void* prepared,
+                                   const int32_t* offsets, float* y_permuted, int experts,
+                                   int hidden, int output, int route_pairs,
+                                   const rr_context* ctx);
 
 /* chain_from_tokens: dense_gemm -> topk_gate -> histogram_exclusive_scan ->
  * token_permute -> grouped_gemm -> unpermute on ctx->stream, no host sync.

@@ -622,7 +622,7 @@ Status validate_chain_shape(int tokens, int hidden, int experts, int output) noe
 Status chain_after_logits(const float* logits, const float* logit_bias, const float* x,
                           const float* expert_w, const ChainBuffers& b, int tokens, int hidden,
                           int experts, int output, const RuntimeContext& context,
-                          bool gather_rows) noexcept {
+                          bool gather_rows, bool prepared_weights) noexcept {
   cudaStream_t stream = context.stream;
   Status s = success_status();
   {
@@ -672,10 +672,21 @@ Status chain_after_logits(const float* logits, const float* logit_bias, const fl
     }
     if (!s.ok()) return s;
     StageRange r("raggedroute_grouped_gemm");
-    s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, expert_w, b.offsets,
-                                                     b.y_permuted, experts, routes, hidden,
-                                                     output, stream),
-                            "chain grouped_gemm launch failed");
+    if (prepared_weights) {
+      const float* hi = expert_w;
+      const float* lo = reinterpret_cast<const float*>(
+          reinterpret_cast<const char*>(expert_w) +
+          rrb::prepared_weights_half_bytes(experts, hidden, output));
+      s = detail::cuda_status(rrb::launch_grouped_gemm_prepared(b.x_permuted, hi, lo, b.offsets,
+                                                                b.y_permuted, experts, routes,
+                                                                hidden, output, stream),
+                              "chain grouped_gemm (prepared weights) launch failed");
+    } else {
+      s = detail::cuda_status(rrb::launch_grouped_gemm(b.x_permuted, expert_w, b.offsets,
+                                                       b.y_permuted, experts, routes, hidden,
+                                                       output, stream),
+                              "chain grouped_gemm launch failed");
+    }
   }
   if (!s.ok()) return s;
   StageRange r("raggedroute_unpermute");
@@ -691,6 +702,24 @@ Status validate_chain_buffers(const ChainBuffers& b, bool need_logits, int hidde
       b.route_pos == nullptr || (output > 0 && (b.y == nullptr || b.y_permuted == nullptr)) ||
       (hidden > 0 && !gather_rows && b.x_permuted == nullptr)) {
     return detail::invalid_argument("chain received a null device buffer");
+  }
+  return success_status();
+}
+
+// Prepared expert weights: the tcgen05 engine only (no FP32 fallback reads
+// that layout), so the shapes and buffers TMA needs are required up front.
+Status validate_prepared(bool prepared, bool gather_rows, const void* weights,
+                         const ChainBuffers& b, int hidden, int output) noexcept {
+  if (!prepared) return success_status();
+  if (gather_rows) {
+    return detail::make_status(StatusCode::kUnsupportedKernelVariant,
+                               "prepared expert weights do not combine with row gathering");
+  }
+  if (hidden % 4 != 0 || output % 4 != 0 || !rrb::aligned_to(weights, 256) ||
+      !rrb::aligned_to(b.x_permuted, 16) || !rrb::aligned_to(b.y_permuted, 16)) {
+    return detail::invalid_argument(
+        "prepared expert weights need K and N multiples of 4, a 256-byte aligned prepared "
+        "buffer and 16-byte aligned x_permuted / y_permuted");
   }
   return success_status();
 }
@@ -729,6 +758,9 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
   }
   s = validate_chain_buffers(args.buffers, true, args.hidden, args.output, args.gather_rows);
   if (!s.ok()) return s;
+  s = validate_prepared(args.prepared_weights, args.gather_rows, args.expert_weights,
+                        args.buffers, args.hidden, args.output);
+  if (!s.ok()) return s;
   const std::size_t need = get_chain_workspace_size(args.tokens, args.hidden, args.experts,
                                                     args.output);
   if (context.workspace == nullptr || context.workspace_bytes < need) {
@@ -745,7 +777,7 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
   if (!s.ok()) return s;
   return chain_after_logits(args.buffers.logits, args.logit_bias, args.x, args.expert_weights,
                             args.buffers, args.tokens, args.hidden, args.experts, args.output,
-                            context, args.gather_rows);
+                            context, args.gather_rows, args.prepared_weights);
 }
 
 Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& context) noexcept {
@@ -761,6 +793,9 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
   }
   s = validate_chain_buffers(args.buffers, false, args.hidden, args.output, args.gather_rows);
   if (!s.ok()) return s;
+  s = validate_prepared(args.prepared_weights, args.gather_rows, args.expert_weights,
+                        args.buffers, args.hidden, args.output);
+  if (!s.ok()) return s;
   const std::size_t need = get_chain_workspace_size(args.tokens, args.hidden, args.experts,
                                                     args.output);
   if (context.workspace == nullptr || context.workspace_bytes < need) {
@@ -769,7 +804,7 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
   }
   return chain_after_logits(args.logits, nullptr, args.x, args.expert_weights, args.buffers,
                             args.tokens, args.hidden, args.experts, args.output, context,
-                            args.gather_rows);
+                            args.gather_rows, args.prepared_weights);
 }
 
 std::size_t get_route_chain_workspace_size(int tokens, int top_k, int experts) noexcept {
@@ -1192,12 +1227,86 @@ rr_status rr_unpermute(const float* y_permuted, const int32_t* route_pos,
 size_t rr_unpermute_workspace_size(int, int, int) { return 0; }
 
 // Chains read ctx->implementation_id: 0 materialises x_permuted,
-// RR_CHAIN_IMPL_GATHER_ROWS gathers the grouped GEMM's rows from x.
-rr_status chain_impl(const rr_context* ctx, bool* gather_rows) {
+// RR_CHAIN_IMPL_GATHER_ROWS gathers the grouped GEMM's rows from x,
+// RR_CHAIN_IMPL_PREPARED_WEIGHTS (token and logit chains) takes
+// expert_weights as a buffer from rr_prepare_expert_weights.
+rr_status chain_impl(const rr_context* ctx, bool* gather_rows, bool* prepared = nullptr) {
   *gather_rows = ctx->implementation_id == RR_CHAIN_IMPL_GATHER_ROWS;
-  if (ctx->implementation_id != 0 && !*gather_rows) {
+  const bool prep = ctx->implementation_id == RR_CHAIN_IMPL_PREPARED_WEIGHTS;
+  if (prepared != nullptr) *prepared = prep;
+  if (ctx->implementation_id != 0 && !*gather_rows && !(prep && prepared != nullptr)) {
     return to_c({raggedroute::StatusCode::kUnsupportedKernelVariant, cudaSuccess,
                  "unknown chain implementation id"});
+  }
+  return to_c(raggedroute::success_status());
+}
+
+size_t rr_prepared_expert_weights_size(int experts, int hidden, int output) {
+  if (experts <= 0 || hidden <= 0 || output <= 0) return 0;
+  return 2 * rrb::prepared_weights_half_bytes(experts, hidden, output);
+}
+
+rr_status rr_prepare_expert_weights(const float* expert_weights, int experts, int hidden,
+                                    int output, void* prepared, size_t prepared_bytes,
+                                    const rr_context* ctx) {
+  if (ctx == nullptr) return null_context();
+  if (experts <= 0 || experts > rrb::kMaxExperts || hidden <= 0 || output <= 0 ||
+      hidden % 4 != 0 || output % 4 != 0) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "prepare_expert_weights requires 1<=E<=1024 and K, N positive multiples of 4"});
+  }
+  if (expert_weights == nullptr || prepared == nullptr || !rrb::aligned_to(prepared, 256)) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "prepare_expert_weights needs the weights and a 256-byte aligned buffer"});
+  }
+  if (prepared_bytes < rr_prepared_expert_weights_size(experts, hidden, output)) {
+    return to_c({raggedroute::StatusCode::kInsufficientWorkspace, cudaSuccess,
+                 "prepared buffer is smaller than rr_prepared_expert_weights_size"});
+  }
+  const raggedroute::Status a = raggedroute::detail_resolve_sm100(to_runtime(ctx));
+  if (!a.ok()) return to_c(a);
+  float* hi = static_cast<float*>(prepared);
+  float* lo = reinterpret_cast<float*>(static_cast<char*>(prepared) +
+                                       rrb::prepared_weights_half_bytes(experts, hidden, output));
+  const cudaError_t e = rrb::launch_prepare_weights(expert_weights, hi, lo, experts, hidden,
+                                                    output, as_stream(ctx->stream));
+  if (e != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, e, "prepare_expert_weights launch failed"});
+  }
+  return to_c(raggedroute::success_status());
+}
+
+rr_status rr_grouped_gemm_prepared(const float* x_permuted, const void* prepared,
+                                   const int32_t* offsets, float* y_permuted, int experts,
+                                   int hidden, int output, int route_pairs,
+                                   const rr_context* ctx) {
+  if (ctx == nullptr) return null_context();
+  if (experts <= 0 || experts > rrb::kMaxExperts || hidden <= 0 || output <= 0 ||
+      hidden % 4 != 0 || output % 4 != 0 || route_pairs < 0) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "grouped_gemm_prepared requires 1<=E<=1024, K, N positive multiples of 4"});
+  }
+  if (route_pairs == 0) return to_c(raggedroute::success_status());
+  if (x_permuted == nullptr || prepared == nullptr || offsets == nullptr ||
+      y_permuted == nullptr || !rrb::aligned_to(prepared, 256)) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "grouped_gemm_prepared received a null or misaligned buffer"});
+  }
+  const raggedroute::Status a = raggedroute::detail_resolve_sm100(to_runtime(ctx));
+  if (!a.ok()) return to_c(a);
+  const float* hi = static_cast<const float*>(prepared);
+  const float* lo = reinterpret_cast<const float*>(
+      static_cast<const char*>(prepared) +
+      rrb::prepared_weights_half_bytes(experts, hidden, output));
+  const cudaError_t e = rrb::launch_grouped_gemm_prepared(
+      x_permuted, hi, lo, offsets, y_permuted, experts, route_pairs, hidden, output,
+      as_stream(ctx->stream));
+  if (e == cudaErrorInvalidValue) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, e,
+                 "grouped_gemm_prepared needs 16-byte aligned x_permuted / y_permuted"});
+  }
+  if (e != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, e, "grouped_gemm_prepared launch failed"});
   }
   return to_c(raggedroute::success_status());
 }
@@ -1220,7 +1329,7 @@ rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
-  const rr_status impl = chain_impl(ctx, &args.gather_rows);
+  const rr_status impl = chain_impl(ctx, &args.gather_rows, &args.prepared_weights);
   if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_tokens(args, to_runtime(ctx)));
 }
@@ -1268,7 +1377,7 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
-  const rr_status impl = chain_impl(ctx, &args.gather_rows);
+  const rr_status impl = chain_impl(ctx, &args.gather_rows, &args.prepared_weights);
   if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_logits(args, to_runtime(ctx)));
 }

@@ -187,6 +187,18 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
                                    cudaStream_t stream, int weight_sets = 0,
                                    const RowScatter* scatter = nullptr,
                                    const RowGather* gather = nullptr);
+// Grouped GEMM on prepared expert weights (w_hi, w_lo: K-major [E][N][K],
+// hi = W, lo = W - trunc_tf32(W); prepare.cu). K and N multiples of 4, all
+// buffers 16-byte aligned, else cudaErrorInvalidValue; no SIMT fallback.
+cudaError_t launch_grouped_gemm_prepared(const float* x, const float* w_hi, const float* w_lo,
+                                         const int32_t* offsets, float* y, int experts, int rows,
+                                         int hidden, int output, cudaStream_t stream);
+
+// prepare.cu: bytes of one half (hi or lo) of a prepared weight buffer,
+// 256-byte aligned; the buffer is hi | lo.
+std::size_t prepared_weights_half_bytes(int experts, int hidden, int output);
+cudaError_t launch_prepare_weights(const float* w, float* hi, float* lo, int experts, int hidden,
+                                   int output, cudaStream_t stream);
 
 // misc.cu
 cudaError_t launch_cache_scrub(uint32_t* buffer, std::size_t elements, cudaStream_t stream);

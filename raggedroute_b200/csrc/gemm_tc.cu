@@ -186,13 +186,19 @@ __device__ __forceinline__ int nmajor_plain_offset(int k, int n) {
 // kGather: A rows come from x through a row map (RowGather) instead of a TMA
 // tile of a materialised x_permuted; a separate instantiation so the default
 // kernel carries none of it.
-template <bool kGather, int kMT>
+// kPrep (prepared expert weights, rr_prepare_expert_weights): B hi and B lo
+// arrive K-major from memory (tma_b: W^T, tma_b2: W^T - trunc(W^T)), so the
+// MMA takes all of B and A hi from the raw slot and the workers split only
+// A. The same shared-memory bytes are cut into 40 KB raw slots (A | B hi |
+// B lo) and 8 KB operand slots (A lo).
+template <bool kGather, int kMT, bool kPrep = false>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-    const int32_t* __restrict__ offsets, float* __restrict__ y, int experts, int rows,
-    int hidden, int output, int wsets, unsigned* err, const RowScatter scatter,
-    const RowGather gather) {
+    const __grid_constant__ CUtensorMap tma_b2, const int32_t* __restrict__ offsets,
+    float* __restrict__ y, int experts, int rows, int hidden, int output, int wsets,
+    unsigned* err, const RowScatter scatter, const RowGather gather) {
   static_assert(kMT == 1 || (kMT == 2 && !kGather), "two m-tiles only for the plain path");
+  static_assert(!kPrep || (!kGather && kMT == 1), "prepared weights: plain 128-row tiles");
   // Layout of a raw stage: A (kMT x 8 KB) | B (kTileN columns); of an operand
   // stage: A hi | A lo | B hi | B lo (A hi written only when gathering; else
   // the MMA reads A hi from the raw stage). Both total the same bytes for
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
   constexpr int kAB = kABytes * kMT;
   constexpr int kOBRaw = kAB;
   constexpr int kOAHi = 0;
-  constexpr int kOALo = kAB;
+  constexpr int kOALo = kPrep ? 0 : kAB;
   constexpr int kOBHi = 2 * kAB;
   constexpr int kOBLo = 2 * kAB + kTileN * kBK * 4;
   constexpr int kItems = (kTileN * 4 + kWorkerThreads - 1) / kWorkerThreads;
@@ -210,6 +216,19 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
+  constexpr int kPrepRaw = kABytes + 2 * kBBytes;  // A | B hi | B lo
+  constexpr int kPrepOp = kABytes;                 // A lo
+  static_assert(kRawStages * kPrepRaw + kOpStages * kPrepOp <=
+                    kRawStages * kRawBytes + kOpStages * kOpBytes,
+                "prepared-weight slots fit in the ring bytes");
+  // The raw and operand rings are the first members of Smem, back to back.
+  uint8_t* const ring = reinterpret_cast<uint8_t*>(&s);
+  auto raw_stage = [&](int i) -> uint8_t* {
+    return kPrep ? ring + i * kPrepRaw : s.raw[i];
+  };
+  auto op_stage = [&](int i) -> uint8_t* {
+    return kPrep ? ring + kRawStages * kPrepRaw + i * kPrepOp : s.op[i];
+  };
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_tiles_n = (output + kTileN - 1) / kTileN;
@@ -299,23 +318,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
     if (lane == 0) {
       tma_prefetch_desc(&tma_a);
       tma_prefetch_desc(&tma_b);
+      if (kPrep) tma_prefetch_desc(&tma_b2);
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total && !*failed; t += gridDim.x) {
         const TileGeom g = geom<kMT>(t, offsets, experts, rows, s.prefix, n_tiles_n, output);
         // A full-width B box even for a narrow last tile: columns past N
         // are zero-filled by TMA and still count toward the transaction bytes.
-        const uint32_t bytes = kAB + kTileN * kBK * 4;
+        const uint32_t bytes = kPrep ? kPrepRaw : kAB + kTileN * kBK * 4;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&s.raw_empty[stage], phase ^ 1u, err, failed)) break;
-          uint8_t* st = s.raw[stage];
+          uint8_t* st = raw_stage(stage);
           mbar_arrive_expect_tx(&s.raw_full[stage], bytes);
 #pragma unroll
           for (int m = 0; m < kMT; ++m) {
             tma_load_2d(st + m * kABytes, &tma_a, &s.raw_full[stage], kb * kBK, g.base + m * kBM);
           }
-          tma_load_3d(st + kOBRaw, &tma_b, &s.raw_full[stage], g.col0, kb * kBK,
-                      g.expert % wsets);
+          if constexpr (kPrep) {
+            // Prepared B tiles: K-major [N][K] per expert, rows past N zero.
+            tma_load_3d(st + kABytes, &tma_b, &s.raw_full[stage], kb * kBK, g.col0,
+                        g.expert % wsets);
+            tma_load_3d(st + kABytes + kBBytes, &tma_b2, &s.raw_full[stage], kb * kBK, g.col0,
+                        g.expert % wsets);
+          } else {
+            tma_load_3d(st + kOBRaw, &tma_b, &s.raw_full[stage], g.col0, kb * kBK,
+                        g.expert % wsets);
+          }
           s.issued[stage] += 1;
           if (++stage == kRawStages) {
             stage = 0;
@@ -351,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
               break;
             }
             tc_fence_after();
-            const uint32_t base = smem_u32(s.op[stage]);
-            const uint32_t rawb = smem_u32(s.raw[rstage]);
-            const uint32_t b_hi = base + kOBHi;
-            const uint32_t b_lo = base + kOBLo;
+            const uint32_t base = smem_u32(op_stage(stage));
+            const uint32_t rawb = smem_u32(raw_stage(rstage));
+            const uint32_t b_hi = kPrep ? rawb + kABytes : base + kOBHi;
+            const uint32_t b_lo = kPrep ? rawb + kABytes + kBBytes : base + kOBLo;
 #pragma unroll
             for (int ks = 0; ks < kBK / 8; ++ks) {
               // K-major, 64-byte swizzle: 8-row groups 512 B apart; the second
@@ -455,9 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
             !mbar_wait(&s.op_empty[ostage], ophase ^ 1u, err, failed)) {
           break;
         }
-        if (g.n_mma != b_for) prepare_b(g.n_mma);
-        const uint32_t raw = smem_u32(s.raw[rstage]);
-        const uint32_t op = smem_u32(s.op[ostage]);
+        if (!kPrep && g.n_mma != b_for) prepare_b(g.n_mma);
+        const uint32_t raw = smem_u32(raw_stage(rstage));
+        const uint32_t op = smem_u32(op_stage(ostage));
         // Loads first (A: one 16-byte chunk in the same K-major position in
         // and out; B: this thread's items), then split and store.
         float4 av[kMT];
@@ -467,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         const uint32_t braw = raw + kOBRaw;
 #pragma unroll
         for (int i = 0; i < kItems; ++i) {
-          if (i < b_items) {
+          if (!kPrep && i < b_items) {
             bv[i].x = lds_f32(braw + bsrc[i][0]);
             bv[i].y = lds_f32(braw + bsrc[i][1]);
             bv[i].z = lds_f32(braw + bsrc[i][2]);
@@ -486,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         }
 #pragma unroll
         for (int i = 0; i < kItems; ++i) {
-          if (i < b_items) {
+          if (!kPrep && i < b_items) {
             split4(bv[i], h, l);
             sts_v4(op + kOBHi + bdst[i], h);
             sts_v4(op + kOBLo + bdst[i], l);
@@ -641,6 +669,8 @@ bool kernel_configured() {
          cudaFuncSetAttribute(grouped_gemm_tc_kernel<false, 2>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
          cudaFuncSetAttribute(grouped_gemm_tc_kernel<true, 1>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
+         cudaFuncSetAttribute(grouped_gemm_tc_kernel<false, 1, true>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
     if (!ok) cudaGetLastError();
   });
@@ -717,17 +747,73 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
   const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
   if (gather != nullptr) {
     grouped_gemm_tc_kernel<true, 1><<<grid, kThreads, kSmemBytes, stream>>>(
-        ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
+        ma, mb, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
         *gather);
   } else if (mt == 2) {
     grouped_gemm_tc_kernel<false, 2><<<grid, kThreads, kSmemBytes, stream>>>(
-        ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
+        ma, mb, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
         RowGather{});
   } else {
     grouped_gemm_tc_kernel<false, 1><<<grid, kThreads, kSmemBytes, stream>>>(
-        ma, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
+        ma, mb, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,
         RowGather{});
   }
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_grouped_gemm_prepared(const float* x, const float* w_hi, const float* w_lo,
+                                         const int32_t* offsets, float* y, int experts, int rows,
+                                         int hidden, int output, cudaStream_t stream) {
+  if (hidden <= 0 || output <= 0 || hidden % 4 != 0 || output % 4 != 0 ||
+      !aligned_to(x, 16) || !aligned_to(w_hi, 16) || !aligned_to(w_lo, 16) ||
+      !aligned_to(y, 16)) {
+    return cudaErrorInvalidValue;
+  }
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr || !kernel_configured()) return cudaErrorNotSupported;
+  const long long a_rows = rows > 0 ? rows : (1LL << 31) - 1;
+  CUtensorMap ma{}, mh{}, ml{};
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(a_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(hidden) * 4};
+    const cuuint32_t box[2] = {kBK, kBM};
+    const cuuint32_t elem[2] = {1, 1};
+    if (encode(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box,
+               elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      return cudaErrorInvalidValue;
+    }
+  }
+  // Prepared B: [experts][output][hidden] viewed as {hidden, output, experts},
+  // one 16 x 256 box per k-block, K-major with the 64-byte swizzle (the
+  // operand layout the MMA reads), rows past N zero-filled.
+  for (int i = 0; i < 2; ++i) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(output),
+                                static_cast<cuuint64_t>(experts)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(hidden) * 4,
+                                   static_cast<cuuint64_t>(hidden) * output * 4};
+    const cuuint32_t box[3] = {kBK, kBN, 1};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    if (encode(i == 0 ? &mh : &ml, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+               const_cast<float*>(i == 0 ? w_hi : w_lo), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      return cudaErrorInvalidValue;
+    }
+  }
+  int grid = sm_count();
+  if (offsets == nullptr) {
+    const long long tiles = static_cast<long long>((rows + kBM - 1) / kBM) *
+                            ((output + kBN - 1) / kBN);
+    if (tiles <= 0) return cudaSuccess;
+    if (tiles < grid) grid = static_cast<int>(tiles);
+  }
+  grouped_gemm_tc_kernel<false, 1, true><<<grid, kThreads, kSmemBytes, stream>>>(
+      ma, mh, ml, offsets, y, experts, rows, hidden, output, experts, device_error_word(),
+      RowScatter{}, RowGather{});
   note_launch();
   return cudaGetLastError();
 }

@@ -33,13 +33,44 @@ def _ctx(ctx: Context | None, workspace: torch.Tensor | None = None) -> ctypes.P
 
 
 CHAIN_IMPL_GATHER_ROWS = 1
+CHAIN_IMPL_PREPARED_WEIGHTS = 2
 
 
-def _chain_ctx(ctx: Context | None, workspace: torch.Tensor, gather_rows: bool):
+def _chain_ctx(ctx: Context | None, workspace: torch.Tensor, gather_rows: bool,
+               prepared: bool = False):
+    if gather_rows and prepared:
+        raise ValueError("gather_rows does not combine with prepared expert weights")
     c = dataclasses.replace(ctx) if ctx is not None else Context()
     if gather_rows:
         c.implementation_id = CHAIN_IMPL_GATHER_ROWS
+    if prepared:
+        c.implementation_id = CHAIN_IMPL_PREPARED_WEIGHTS
     return _ctx(c, workspace)
+
+
+class PreparedExpertWeights:
+    """Expert weights W [E, K, N] laid out once for the grouped GEMM
+    (rr_prepare_expert_weights): K-major hi = W and lo = W - trunc_tf32(W)
+    in one device buffer twice the size of W. Pass it wherever a chain or
+    grouped_gemm_prepared takes expert weights; W itself is not kept."""
+
+    def __init__(self, expert_weights: torch.Tensor, ctx: Context | None = None):
+        _need(expert_weights, torch.float32, "expert_weights")
+        e, k, n = expert_weights.shape
+        self.shape = (e, k, n)
+        size = int(lib().rr_prepared_expert_weights_size(e, k, n))
+        if size == 0:
+            raise ValueError("expert weights must be non-empty")
+        self.buffer = torch.empty(size, dtype=torch.uint8, device=expert_weights.device)
+        check(lib().rr_prepare_expert_weights(_ptr(expert_weights), e, k, n, _ptr(self.buffer),
+                                              size, _ctx(ctx)), "prepare_expert_weights")
+
+
+def _weights(expert_weights) -> tuple[int | None, tuple[int, int, int], bool]:
+    """(pointer, (E, K, N), prepared) of raw or prepared expert weights."""
+    if isinstance(expert_weights, PreparedExpertWeights):
+        return _ptr(expert_weights.buffer), expert_weights.shape, True
+    return _ptr(expert_weights), tuple(expert_weights.shape), False
 
 
 def _need(t: torch.Tensor | None, dtype: torch.dtype, name: str) -> None:
@@ -159,6 +190,20 @@ def grouped_gemm_gather(x: torch.Tensor, sorted_route: torch.Tensor, top_k: int,
     return y_permuted
 
 
+def grouped_gemm_prepared(x_permuted: torch.Tensor, weights: PreparedExpertWeights,
+                          offsets: torch.Tensor, y_permuted: torch.Tensor, route_pairs: int,
+                          ctx: Context | None = None) -> torch.Tensor:
+    """Grouped GEMM on prepared expert weights (rr_grouped_gemm_prepared)."""
+    _need(x_permuted, torch.float32, "x_permuted")
+    _need(offsets, torch.int32, "offsets")
+    _need(y_permuted, torch.float32, "y_permuted")
+    experts, hidden, output = weights.shape
+    check(lib().rr_grouped_gemm_prepared(_ptr(x_permuted), _ptr(weights.buffer), _ptr(offsets),
+                                         _ptr(y_permuted), experts, hidden, output, route_pairs,
+                                         _ctx(ctx)), "grouped_gemm_prepared")
+    return y_permuted
+
+
 def unpermute(y_permuted: torch.Tensor, route_pos: torch.Tensor, route_weights: torch.Tensor,
               y: torch.Tensor, tokens: int, top_k: int, output: int,
               ctx: Context | None = None) -> None:
@@ -213,36 +258,37 @@ def chain_workspace_size(tokens: int, hidden: int, experts: int, output: int) ->
 
 
 def chain_from_tokens(x: torch.Tensor, router_weights: torch.Tensor,
-                      expert_weights: torch.Tensor, buf: ChainBuffers,
+                      expert_weights, buf: ChainBuffers,
                       logit_bias: torch.Tensor | None = None,
                       ctx: Context | None = None, gather_rows: bool = False) -> torch.Tensor:
     """Seven-stage chain X -> Y (benchmarks/adapters/chain_adapter.cpp:263-467).
+    expert_weights: W [E, K, N] or a PreparedExpertWeights.
     gather_rows: the grouped GEMM reads its rows from X (buf.x_permuted is
     not written); results are bit-identical."""
     tokens, hidden = x.shape
     experts = router_weights.shape[1]
-    output = expert_weights.shape[2]
+    w_ptr, (_, _, output), prepared = _weights(expert_weights)
     check(lib().rr_chain_from_tokens(
-        _ptr(x), _ptr(router_weights), _ptr(logit_bias), _ptr(expert_weights), _ptr(buf.logits),
+        _ptr(x), _ptr(router_weights), _ptr(logit_bias), w_ptr, _ptr(buf.logits),
         _ptr(buf.expert_ids), _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets),
         _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens,
-        hidden, experts, output, _chain_ctx(ctx, buf.workspace, gather_rows)),
+        hidden, experts, output, _chain_ctx(ctx, buf.workspace, gather_rows, prepared)),
         "chain_from_tokens")
     return buf.y
 
 
-def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights: torch.Tensor,
+def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights,
                       buf: ChainBuffers, ctx: Context | None = None,
                       gather_rows: bool = False) -> torch.Tensor:
-    """Six-stage chain logits -> Y."""
+    """Six-stage chain logits -> Y; expert_weights as in chain_from_tokens."""
     tokens, hidden = x.shape
     experts = logits.shape[1]
-    output = expert_weights.shape[2]
+    w_ptr, (_, _, output), prepared = _weights(expert_weights)
     check(lib().rr_chain_from_logits(
-        _ptr(logits), _ptr(x), _ptr(expert_weights), _ptr(buf.expert_ids),
+        _ptr(logits), _ptr(x), w_ptr, _ptr(buf.expert_ids),
         _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets), _ptr(buf.x_permuted),
         _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens, hidden, experts, output,
-        _chain_ctx(ctx, buf.workspace, gather_rows)), "chain_from_logits")
+        _chain_ctx(ctx, buf.workspace, gather_rows, prepared)), "chain_from_logits")
     return buf.y
 
 

@@ -118,3 +118,27 @@ def test_host_chain_flags_validation(rrlib):
     lib = rrlib.lib()
     st = lib.rr_host_chain_set_flags(None, 1)
     assert st.code == rrlib.StatusCode.INVALID_ARGUMENT
+
+
+def test_prepared_weights_size_and_validation(rrlib):
+    lib = rrlib.lib()
+    half = (3 * 40 * 36 * 4 + 255) // 256 * 256
+    assert lib.rr_prepared_expert_weights_size(3, 40, 36) == 2 * half
+    assert lib.rr_prepared_expert_weights_size(0, 40, 36) == 0
+    p = ctypes.c_void_p(256)
+    # K not a multiple of 4, a misaligned buffer, a short buffer: rejected
+    # before any device work (explicit architecture, no device query).
+    st = lib.rr_prepare_expert_weights(p, 3, 42, 36, p, 1 << 20, _ctx())
+    assert st.code == rrlib.StatusCode.INVALID_ARGUMENT
+    st = lib.rr_prepare_expert_weights(p, 3, 40, 36, ctypes.c_void_p(258), 1 << 20, _ctx())
+    assert st.code == rrlib.StatusCode.INVALID_ARGUMENT
+    st = lib.rr_prepare_expert_weights(p, 3, 40, 36, p, 16, _ctx())
+    assert st.code == rrlib.StatusCode.INSUFFICIENT_WORKSPACE
+    st = lib.rr_grouped_gemm_prepared(p, p, p, p, 3, 42, 36, 10, _ctx())
+    assert st.code == rrlib.StatusCode.INVALID_ARGUMENT
+    # Prepared weights are a token/logit chain option only.
+    from raggedroute_b200._lib import RRContext
+    ctx = ctypes.pointer(RRContext(None, None, 0, 4, 0, 2))
+    st = lib.rr_chain_from_route_ids(None, None, None, None, None, None, None, None, None, None,
+                                     None, 1, 2, 8, 4, 8, ctx)
+    assert st.code == rrlib.StatusCode.UNSUPPORTED_KERNEL_VARIANT
