@@ -16,8 +16,11 @@ metric with X in pinned host memory and Y returned to host memory every step
 token chunks with the chain; expert parallelism: ep.HostPipeline, copy in,
 EP step, copy out, with each step's copies overlapping its neighbours).
 Extra keys on one GPU: `cold_scrub` (the C5 step with 256 MiB written to
-flush L2 before every step) and `small_configs` (C1 chain_from_tokens and C2
-chain_from_logits latency, eager and replayed from a captured CUDA graph).
+flush L2 before every step), `small_configs` (C1 chain_from_tokens and C2
+chain_from_logits latency, eager and replayed from a captured CUDA graph),
+`configs` (C3 routing stages and C4 grouped GEMM, graph-timed) and
+`prepared_weights` (the chain on expert weights prepared once, an inference
+option).
 
 Multi-GPU (torchrun): expert parallelism -- every rank runs its own T=65536
 tokens (weak scaling); hot experts are replicated into virtual experts placed
@@ -437,6 +440,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         stage_bytes["token_permute"] = 12.0 * routes + 4.0 * (e + 1)
     if world == 1 and not args.no_extras:
         extras["configs"] = config_sweep(torch, rr, device, hbm, peak_3x)
+        extras["prepared_weights"] = prepared_weights_pass(
+            torch, rr, stream, inp, buf, tokens, max(3, args.steps), gemm_flops, peak_3x)
     stages = {}
     for nm in stage_names:
         ms = stage_ms[nm]
@@ -577,6 +582,58 @@ def cold_scrub_step(torch, rr, stream, step, steps: int) -> dict:
         b.synchronize()
         total += a.elapsed_time(b)
     return {"ms_per_step": round(total / steps, 3), "scrub_bytes": scrub.numel() * 4}
+
+
+def prepared_weights_pass(torch, rr, stream, inp, buf, tokens: int, steps: int,
+                          gemm_flops: float, peak_3x: float) -> dict:
+    """chain_from_tokens on expert weights prepared once (PreparedExpertWeights:
+    K-major hi/lo, so the grouped GEMM loads all of B ready for its MMAs and
+    splits only the token rows) -- an inference option next to the drop-in
+    call, which the headline value measures. Reports the one-time
+    preparation, the chain per step and the grouped GEMM alone, CUDA events on
+    the same C5 inputs. An error here is reported, not raised."""
+    try:
+        ctx = rr.Context(stream=stream.cuda_stream)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            prep = rr.PreparedExpertWeights(inp.expert_w, ctx=ctx)
+            b.record(stream)
+        b.synchronize()
+        prepare_ms = a.elapsed_time(b)
+
+        def step():
+            rr.chain_from_tokens(inp.x, inp.router_w, prep, buf, logit_bias=inp.logit_bias,
+                                 ctx=ctx)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step()
+            a.record(stream)
+            for _ in range(steps):
+                step()
+            b.record(stream)
+        b.synchronize()
+        chain_ms = a.elapsed_time(b) / steps
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for _ in range(5):
+                rr.grouped_gemm_prepared(buf.x_permuted, prep, buf.offsets, buf.y_permuted,
+                                         2 * tokens, ctx=ctx)
+            b.record(stream)
+        b.synchronize()
+        gemm_ms = a.elapsed_time(b) / 5
+        tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12
+        del prep
+        return {"prepare_ms": round(prepare_ms, 3), "ms_per_step": round(chain_ms, 3),
+                "tokens_per_s": round(tokens / (chain_ms * 1e-3), 1),
+                "grouped_gemm_ms": round(gemm_ms, 3), "grouped_gemm_TFLOP/s": round(tflops, 2),
+                "tensor_frac_3xtf32": round(tflops / peak_3x, 3),
+                "note": "expert weights prepared once (rr_prepare_expert_weights), an "
+                        "inference option; `value` is the drop-in call on raw weights"}
+    except Exception as ex:  # noqa: BLE001 - an optional extra must not cost the bench line
+        return {"error": f"{type(ex).__name__}: {ex}"[:300]}
 
 
 def _event_us(torch, rr, stream, fn, iters: int) -> float:
