@@ -399,9 +399,27 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         te = torch.tensor([s2.elapsed_time(e2)], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        # The PCIe bound of this number: one step's input copied from pinned
+        # host memory to the device alone, best of 3 (CUDA events).
+        x_dev = torch.empty_like(inp.x)
+        h2d_ms = []
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                c0 = torch.cuda.Event(enable_timing=True)
+                c1 = torch.cuda.Event(enable_timing=True)
+                c0.record(stream)
+                x_dev.copy_(x_host, non_blocking=True)
+                c1.record(stream)
+                c1.synchronize()
+                h2d_ms.append(c0.elapsed_time(c1))
+        del x_dev
+        h2d_gbs = x_host.numel() * 4 / (min(h2d_ms) * 1e-3) / 1e9
         e2e = {"value": tokens * world * args.steps / (float(te.item()) * 1e-3), "unit": UNIT,
                "h2d_bytes_per_step": x_host.numel() * 4,
                "d2h_bytes_per_step": y_host.numel() * 4,
+               "h2d_gbs_measured": round(h2d_gbs, 2),
+               "h2d_bound_tokens_per_s": round(tokens * world / (x_host.numel() * 4 / (h2d_gbs * 1e9)),
+                                               1),
                "api": ("rr_chain_from_tokens_host (input-ready plan: consecutive steps "
                        "overlap), chunk %d tokens" % args.e2e_chunk
                        if ep is None else "raggedroute_b200.ep.HostPipeline: copy in, "
@@ -422,7 +440,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     peaks = load_peaks()
     tf32 = measure_tf32_peak(torch, device)
-    peak_3x = tf32 / 3.0
+    # The 3xTF32 ceiling from the measured dense bf16 peak: TF32 runs at half
+    # the bf16 rate on this part and the split issues three MMAs per product.
+    peak_3x = float(peaks["bf16_tflops"]) / 6.0
+    peak_3x_sustained = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])) / 6.0
     gemm_flops = 2.0 * routes * k * n
     gemm_ms = stage_ms["grouped_gemm"]
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
@@ -466,7 +487,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "roofline": {"bound": "tensor", "kernel": "grouped_gemm", "achieved": round(achieved, 2),
                      "peak": round(peak_3x, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak_3x, 4),
-                     "peak_source": f"cuBLAS TF32 {tf32:.0f} TFLOP/s measured live / 3",
+                     "peak_source": ("MEASURED_PEAKS bf16_tflops %.1f (%s) / 2 (TF32 rate) / 3 "
+                                     "(MMAs per product)" % (float(peaks["bf16_tflops"]),
+                                                             peaks["source"])),
+                     "frac_of_sustained": round(achieved / peak_3x_sustained, 4),
+                     "cublas_tf32_live_tflops": round(tf32, 1),
+                     "frac_of_cublas_tf32_over_3": round(achieved / (tf32 / 3.0), 4),
                      "traffic": load_traffic("grouped_gemm")},
         "stages": stages,
         "clocks": clock_info,

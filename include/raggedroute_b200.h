@@ -129,10 +129,14 @@ size_t rr_token_permute_workspace_size(int tokens, int experts, int top_k, int h
  * exists for callers whose device memory is owned by a planner or pool with
  * nothing spare, or that reach this library through a binding without access
  * to a CUDA allocator. Calls whose rr_token_permute_workspace_size exceeds
- * 4 MiB fail with RR_INVALID_ARGUMENT. It never allocates or frees. All calls
- * share the array, so calls that overlap on the GPU race and must be
- * serialised by the caller; the first call on each device looks up the
- * array's address and should precede any stream capture. */
+ * 4 MiB fail with RR_INVALID_ARGUMENT (checked right after the shape
+ * checks; every other check is rr_token_permute's, dispatch checks first).
+ * It never allocates or frees. All calls share the array, so calls that
+ * overlap on the GPU race and must be serialised by the caller. The array's
+ * address is looked up on the first call in each CUDA context (the first
+ * call on a device, and the first after that device's context was reset or
+ * replaced) and cached under the context's id; that first call should come
+ * before any stream capture. */
 rr_status rr_token_permute_no_alloc(const float* x, const int32_t* expert_ids,
                                     const int32_t* offsets, float* x_permuted, int32_t* route_pos,
                                     int32_t* sorted_route, int tokens, int experts, int top_k,

@@ -247,6 +247,25 @@ def chain_output_f32(x, expert_w, ids, weights):
     return y
 
 
+def chain_output_f64(x, expert_w, ids, weights):
+    """The chain output in double: Y[t] = sum_k w[t,k] * (X[t] . W[ids[t,k]]),
+    the same composition as the float chain oracle
+    (benchmarks/adapters/chain_adapter.cpp:858-879) without its float
+    rounding. Routing (ids, weights) is an input, so a caller checks the
+    device's outputs against it with the device's own (exactly checked)
+    routing. Returns float64 [T, N]."""
+    x = np.asarray(x, np.float64)
+    expert_w = np.asarray(expert_w, np.float64)
+    ids = _i32(ids)
+    ids = ids.reshape(x.shape[0], -1)
+    weights = np.asarray(weights, np.float64).reshape(ids.shape)
+    y = np.zeros((x.shape[0], expert_w.shape[2]), np.float64)
+    for e in np.unique(ids):
+        rows, ranks = np.nonzero(ids == e)
+        np.add.at(y, rows, weights[rows, ranks][:, None] * (x[rows] @ expert_w[e]))
+    return y
+
+
 def route_chain_output_f32(x, expert_w, ids, weights):
     """Post-route chain output in float, rank order (postroute_chain_adapter.cpp:654-675)."""
     x = _f32(x)

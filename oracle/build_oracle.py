@@ -8,6 +8,11 @@
   is present (the build container); GPU boxes use the prebuilt file, which
   travels with the working tree. Nothing is copied out of the reference.
 
+Where the reference checkout lies: ``--reference PATH``, else the
+``RAGGEDROUTE_REFERENCE`` environment variable, else a checkout named
+``reference`` beside this repository's directory. If none of these holds the
+reference sources, only the restatement is built.
+
 Run: ``python oracle/build_oracle.py [--reference PATH]``.
 """
 from __future__ import annotations
@@ -18,7 +23,16 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REFERENCE = os.environ.get("RAGGEDROUTE_REFERENCE", "/root/reference")
+REPO = os.path.dirname(HERE)
+
+
+def reference_checkout() -> str:
+    """The reference checkout: $RAGGEDROUTE_REFERENCE, else ``reference``
+    beside the repository directory (it may not exist)."""
+    env = os.environ.get("RAGGEDROUTE_REFERENCE")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(REPO), "reference")
 
 # Reference translation units that hold the CPU oracle and its helpers.
 REFERENCE_SOURCES = [
@@ -57,8 +71,9 @@ def build_oracle(force: bool = False) -> str:
     return out
 
 
-def build_reference(reference: str = DEFAULT_REFERENCE, force: bool = False) -> str | None:
+def build_reference(reference: str | None = None, force: bool = False) -> str | None:
     """Compile the reference's CPU oracle into oracle/_ref (None if absent)."""
+    reference = reference or reference_checkout()
     out_dir = os.path.join(HERE, "_ref")
     out = os.path.join(out_dir, "librr_ref.so")
     if not os.path.isdir(os.path.join(reference, "src")):
@@ -91,7 +106,8 @@ def build_reference(reference: str = DEFAULT_REFERENCE, force: bool = False) -> 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: $RAGGEDROUTE_REFERENCE, else ../reference)")
     ap.add_argument("--force", action="store_true")
     args = ap.parse_args()
     print(build_oracle(args.force))

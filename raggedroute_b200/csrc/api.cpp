@@ -31,6 +31,12 @@ unsigned long long launch_count();
 cudaError_t consume_device_error(cudaStream_t stream, unsigned* out);
 }  // namespace rrb
 
+// Helpers shared by the wrappers below. They are not part of the reference's
+// exported API, so they stay out of the library's dynamic symbol table (a
+// caller that compiles the reference's own inline helpers of the same names
+// keeps its copies).
+#define RR_INTERNAL __attribute__((visibility("hidden")))
+
 namespace raggedroute {
 namespace detail {
 
@@ -58,7 +64,7 @@ inline OperatorSignature compute_signature(const ConstTensorView& input,
   return {input.spec, weight.spec, accumulator, output.spec};
 }
 
-Status dispatch_operator(OperatorKind kind, const OperatorSignature& signature,
+RR_INTERNAL Status dispatch_operator(OperatorKind kind, const OperatorSignature& signature,
                          KernelSelection requested, DeviceArchitecture architecture,
                          DispatchDecision* decision) noexcept {
   DeviceArchitecture resolved = DeviceArchitecture::kOther;
@@ -83,7 +89,7 @@ inline Status require_default_family(const DispatchDecision& decision) noexcept 
   return success_status();
 }
 
-bool ranges_overlap(const void* a, std::size_t a_bytes, const void* b,
+RR_INTERNAL bool ranges_overlap(const void* a, std::size_t a_bytes, const void* b,
                     std::size_t b_bytes) noexcept {
   if (a_bytes == 0 || b_bytes == 0) return false;
   const auto a0 = reinterpret_cast<std::uintptr_t>(a);
@@ -345,7 +351,7 @@ Status dense_gemm(const DenseGemmArgs& args, const RuntimeContext& context) noex
 }
 
 namespace detail {
-Status topk_gate_impl(const TopKGateArgs& args, const float* bias,
+RR_INTERNAL Status topk_gate_impl(const TopKGateArgs& args, const float* bias,
                       const RuntimeContext& context) noexcept;
 }  // namespace detail
 
@@ -739,7 +745,7 @@ Status resolve_chain_architecture(const RuntimeContext& context) noexcept {
 
 // Architecture check shared by the library's own (non-reference) entry
 // points: B200 (CC 10.0) only.
-Status detail_resolve_sm100(const RuntimeContext& context) noexcept {
+RR_INTERNAL Status detail_resolve_sm100(const RuntimeContext& context) noexcept {
   return resolve_chain_architecture(context);
 }
 

@@ -11,23 +11,33 @@
 //   * size: kNoAllocScratchBytes (4 MiB) per GPU, held by every GPU that
 //     loads the library until the process exits;
 //   * a call whose scratch need (rr_token_permute_workspace_size) exceeds it
-//     fails with RR_INVALID_ARGUMENT before any launch;
+//     fails with RR_INVALID_ARGUMENT before any launch; this size check
+//     comes right after the shape checks, the rest of the validation is
+//     rr_token_permute's own (dispatch checks first, so an empty call on an
+//     unsupported device or with an unknown kernel variant is rejected);
 //   * no cudaMalloc, cudaFree or allocating library routine is called;
 //   * the kernels overwrite every scratch word they later read, so nothing
 //     has to start at zero and no reset launch is needed;
 //   * all calls share the one array per GPU, so calls that overlap on the
 //     GPU (for example on two streams at once) race on it and must be
 //     serialised by the caller;
-//   * the array's device address is looked up on the first call on each
-//     device, with that device current (cudaGetSymbolAddress). That first
-//     call should come before any stream capture.
+//   * the array's device address belongs to a CUDA context: it is looked up
+//     (cudaGetSymbolAddress, with the device current) on the first call in
+//     each context -- the first call on a device, and again after that
+//     device's context was reset (cudaDeviceReset) or replaced -- and cached
+//     under the context's unique id, read from the call's stream. That first
+//     call in a context should come before any stream capture.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <climits>
 #include <cstdint>
 #include <limits>
 #include <mutex>
+#include <utility>
+#include <vector>
 
+#include "../../include/raggedroute/dispatch.h"
 #include "../../include/raggedroute_b200.h"
 #include "common.cuh"
 
@@ -35,34 +45,103 @@ namespace rrb {
 namespace {
 
 constexpr std::size_t kNoAllocScratchBytes = 4u << 20;
-constexpr int kMaxDevices = 64;
 
 // The scratch itself. In host code `g_no_alloc_scratch` names a host-side
 // stand-in, not device memory: only the address from cudaGetSymbolAddress
 // may be handed to a kernel.
 __device__ __align__(256) unsigned char g_no_alloc_scratch[kNoAllocScratchBytes];
 
-std::once_flag g_once[kMaxDevices];
-void* g_scratch_ptr[kMaxDevices] = {};
-cudaError_t g_lookup_error[kMaxDevices] = {};
+// Driver queries used to identify the context a call launches into. They
+// are fetched through the runtime's entry-point lookup, so the library
+// still links no driver library.
+using StreamGetCtxFn = CUresult (*)(CUstream, CUcontext*);
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-// Resolves the array's device address for the current device (once).
-cudaError_t scratch_for_current_device(void** out) {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+struct DriverQueries {
+  StreamGetCtxFn stream_get_ctx = nullptr;
+  CtxGetCurrentFn ctx_get_current = nullptr;
+  CtxGetIdFn ctx_get_id = nullptr;
+  cudaError_t error = cudaSuccess;
+};
+
+template <typename Fn>
+cudaError_t entry_point(const char* name, Fn* out) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult found = cudaDriverEntryPointSymbolNotFound;
+  const cudaError_t err = cudaGetDriverEntryPointByVersion(name, &fn, 12000, cudaEnableDefault,
+                                                           &found);
   if (err != cudaSuccess) return err;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::call_once(g_once[dev], [dev] {
-    void* p = nullptr;
-    g_lookup_error[dev] = cudaGetSymbolAddress(&p, g_no_alloc_scratch);
-    if (g_lookup_error[dev] == cudaSuccess) {
-      g_scratch_ptr[dev] = p;
-    } else {
-      cudaGetLastError();
+  if (found != cudaDriverEntryPointSuccess || fn == nullptr) return cudaErrorNotSupported;
+  *out = reinterpret_cast<Fn>(fn);
+  return cudaSuccess;
+}
+
+const DriverQueries& driver_queries() {
+  static const DriverQueries q = [] {
+    DriverQueries d;
+    d.error = entry_point("cuStreamGetCtx", &d.stream_get_ctx);
+    if (d.error == cudaSuccess) d.error = entry_point("cuCtxGetCurrent", &d.ctx_get_current);
+    if (d.error == cudaSuccess) d.error = entry_point("cuCtxGetId", &d.ctx_get_id);
+    if (d.error != cudaSuccess) cudaGetLastError();
+    return d;
+  }();
+  return q;
+}
+
+// (context id, scratch address) pairs. Context ids are never reused within
+// a process, so an entry of a destroyed context can never match again; the
+// list is bounded and drops its oldest entry when full.
+constexpr std::size_t kMaxCachedContexts = 64;
+std::mutex g_cache_mutex;
+std::vector<std::pair<unsigned long long, void*>> g_cache;
+
+bool context_id(CUcontext ctx, unsigned long long* id) {
+  return ctx != nullptr && driver_queries().ctx_get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+bool stream_context_id(cudaStream_t stream, unsigned long long* id) {
+  CUcontext ctx = nullptr;
+  if (driver_queries().stream_get_ctx(reinterpret_cast<CUstream>(stream), &ctx) != CUDA_SUCCESS) {
+    return false;
+  }
+  return context_id(ctx, id);
+}
+
+// The scratch array's address in the context that `stream` belongs to.
+cudaError_t scratch_for_stream(cudaStream_t stream, void** out) {
+  const DriverQueries& d = driver_queries();
+  if (d.error != cudaSuccess) return d.error;
+  unsigned long long id = 0;
+  if (stream_context_id(stream, &id)) {
+    std::lock_guard<std::mutex> lock(g_cache_mutex);
+    for (const auto& entry : g_cache) {
+      if (entry.first == id) {
+        *out = entry.second;
+        return cudaSuccess;
+      }
     }
-  });
-  if (g_lookup_error[dev] != cudaSuccess) return g_lookup_error[dev];
-  *out = g_scratch_ptr[dev];
+  }
+  // First call in this context: the lookup makes the current device's
+  // context current on this thread (creating it if needed) and loads the
+  // module there; the stream must belong to that same context.
+  void* p = nullptr;
+  cudaError_t err = cudaGetSymbolAddress(&p, g_no_alloc_scratch);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return err;
+  }
+  CUcontext current = nullptr;
+  unsigned long long current_id = 0;
+  if (d.ctx_get_current(&current) != CUDA_SUCCESS || !context_id(current, &current_id) ||
+      !stream_context_id(stream, &id)) {
+    return cudaErrorDeviceUninitialized;
+  }
+  if (id != current_id) return cudaErrorInvalidResourceHandle;
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  if (g_cache.size() >= kMaxCachedContexts) g_cache.erase(g_cache.begin());
+  g_cache.emplace_back(id, p);
+  *out = p;
   return cudaSuccess;
 }
 
@@ -86,7 +165,8 @@ rr_status rr_token_permute_no_alloc(const float* x, const int32_t* expert_ids,
                                     int hidden, const rr_context* ctx) {
   using rrb::make;
   if (ctx == nullptr) return make(RR_INVALID_ARGUMENT, "rr_context must not be null");
-  // Shape checks and their order follow rr_token_permute.
+  // Shape checks of rr_token_permute, so that the size query below is
+  // defined; rr_token_permute repeats them.
   if (tokens < 0 || experts <= 0 || experts > rrb::kMaxExperts || top_k <= 0 ||
       top_k > experts || hidden < 0) {
     return make(RR_INVALID_ARGUMENT,
@@ -101,34 +181,39 @@ rr_status rr_token_permute_no_alloc(const float* x, const int32_t* expert_ids,
                 "token_permute_no_alloc: scratch need exceeds the 4 MiB static array; "
                 "use rr_token_permute with a caller workspace");
   }
+  // The dispatch checks of rr_token_permute (architecture, kernel family
+  // and research id) come before the empty-call return, as they do there.
+  raggedroute::DeviceArchitecture arch = raggedroute::DeviceArchitecture::kOther;
+  raggedroute::Status status = raggedroute::resolve_device_architecture(
+      static_cast<raggedroute::DeviceArchitecture>(ctx->architecture), &arch);
+  if (status.ok()) {
+    raggedroute::DispatchRequest request;
+    request.operator_kind = raggedroute::OperatorKind::kTokenPermute;
+    request.architecture = arch;
+    request.requested_kernel.family = static_cast<raggedroute::KernelFamily>(ctx->kernel_family);
+    request.requested_kernel.implementation_id = ctx->implementation_id;
+    request.signature.input = raggedroute::TensorSpec{};
+    request.signature.output = raggedroute::TensorSpec{};
+    raggedroute::DispatchDecision decision;
+    status = raggedroute::select_kernel(request, &decision);
+  }
+  if (!status.ok()) {
+    return make(static_cast<int32_t>(status.code), status.message, status.cuda_error);
+  }
   if (tokens == 0) return make(RR_SUCCESS, "success");
-  if (expert_ids == nullptr || offsets == nullptr || route_pos == nullptr ||
-      (hidden != 0 && (x == nullptr || x_permuted == nullptr))) {
-    return make(RR_INVALID_ARGUMENT, "token_permute received a null device pointer");
-  }
-  if (!rrb::aligned_to(x, 4) || !rrb::aligned_to(x_permuted, 4)) {
-    return make(RR_INVALID_ARGUMENT, "token_permute FP32 buffers must be 4-byte aligned");
-  }
-  int32_t arch = ctx->architecture;
-  if (arch == RR_ARCH_AUTO) {
-    const rr_status q = rr_query_current_device_architecture(&arch);
-    if (q.code != RR_SUCCESS) return q;
-  }
-  if (arch != RR_ARCH_SM100) {
-    return make(RR_UNSUPPORTED_ARCHITECTURE, "libraggedroute_b200 ships sm_100a kernels only");
-  }
   void* scratch = nullptr;
-  cudaError_t err = rrb::scratch_for_current_device(&scratch);
+  const cudaError_t err = rrb::scratch_for_stream(static_cast<cudaStream_t>(ctx->stream),
+                                                  &scratch);
   if (err != cudaSuccess) {
     return make(RR_CUDA_ERROR, "token_permute_no_alloc: scratch address lookup failed", err);
   }
-  err = rrb::launch_token_permute(x, expert_ids, offsets, x_permuted, route_pos, sorted_route,
-                                  tokens, experts, top_k, hidden, scratch,
-                                  static_cast<cudaStream_t>(ctx->stream));
-  if (err != cudaSuccess) {
-    return make(RR_CUDA_ERROR, "token_permute_no_alloc kernel launch failed", err);
-  }
-  return make(RR_SUCCESS, "success");
+  // The permute itself, with rr_token_permute's remaining checks (null
+  // pointers, alignment, workspace size), on the static array.
+  rr_context with_scratch = *ctx;
+  with_scratch.workspace = scratch;
+  with_scratch.workspace_bytes = rrb::kNoAllocScratchBytes;
+  return rr_token_permute(x, expert_ids, offsets, x_permuted, route_pos, sorted_route, tokens,
+                          experts, top_k, hidden, &with_scratch);
 }
 
 }  // extern "C"

@@ -138,6 +138,44 @@ def test_grouped_tc_c4_full_size_sampled(rrlib, oracle, cuda):
     assert device_error_word(rrlib) == 0
 
 
+def test_grouped_tc_c5_shape_sampled(rrlib, oracle, cuda):
+    """The C5 grouped GEMM at its full shape (R=131072 rows, E=128, K=4096,
+    N=1408) with ragged C5-like groups (Zipf 1.0, 4 forced-empty experts, no
+    size a multiple of 16): every expert's first and last row and 300 seeded
+    rows against the FP64 oracle, elementwise within the accumulation-aware
+    bound and normwise within 1e-5."""
+    from raggedroute_b200.workloads import c4_group_sizes, offsets_from_sizes
+    r, e, k, n = 131072, 128, 4096, 1408
+    sizes = c4_group_sizes(routes=r, experts=e, empty=4, s=1.0, seed=4)
+    offsets = offsets_from_sizes(sizes)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(4)
+    x = torch.randn(r, k, generator=g, device=cuda)
+    w = torch.randn(e, k, n, generator=g, device=cuda) / 64.0
+    y = torch.full((r, n), float("nan"), device=cuda)
+    rrlib.grouped_gemm(x, w, dev(offsets, cuda), y, e, k, n, r)
+    rng = np.random.default_rng(4)
+    rows = set(rng.integers(0, r, 300).tolist())
+    for i in range(e):
+        if sizes[i] > 0:
+            rows.update({int(offsets[i]), int(offsets[i + 1] - 1)})
+    rows = np.array(sorted(rows))
+    expert_of = np.searchsorted(offsets, rows, side="right") - 1
+    xs = host(x[torch.from_numpy(rows).to(cuda)])
+    ys = host(y[torch.from_numpy(rows).to(cuda)])
+    ref = np.empty((rows.size, n), np.float64)
+    for ei in np.unique(expert_of):
+        sel = np.nonzero(expert_of == ei)[0]
+        wi = host(w[int(ei)])
+        ref[sel] = xs[sel].astype(np.float64) @ wi.astype(np.float64)
+        bound = oracle.gemm_error_bound(xs[sel], wi, k)
+        assert np.all(np.abs(ys[sel] - ref[sel]) <= bound), int(ei)
+    rel = oracle.normwise_rel_error(ys, ref)
+    assert rel <= 1e-5, rel
+    assert not torch.isnan(y).any()
+    assert device_error_word(rrlib) == 0
+
+
 @pytest.mark.parametrize("m,n,k", [(40000, 128, 256), (37999, 100, 64), (65536, 128, 128)])
 def test_dense_tc_two_tiles_per_cta(rrlib, oracle, cuda, m, n, k):
     """Router-shaped GEMMs (N <= 128, at least one wave of 256-row tiles) run

@@ -13,7 +13,10 @@ import pytest
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 FIXTURE = os.path.join(HERE, "golden", "fixture_t24_e16_top2.rrtrace")
-REF_DIR = "/root/reference/configs/workloads"
+
+from oracle.build_oracle import reference_checkout  # noqa: E402
+
+REF_DIR = os.path.join(reference_checkout(), "configs", "workloads")
 
 
 def test_read_fixture_frames(rrlib):

@@ -26,7 +26,14 @@ def _ctx():
                                     None, 0, 0, 0, 0))
 
 
-@pytest.mark.parametrize("tokens,experts,hidden", [(3000, 64, 128), (50_000, 256, 32)])
+# (tokens, experts, hidden): one CTA chunk (scratch = the E cursors only),
+# two multi-chunk cases, and the largest input whose scratch need is exactly
+# the 4 MiB limit (E=1024: 2,095,104 tokens; one more token is rejected).
+LIMIT_TOKENS = 2_095_104
+
+
+@pytest.mark.parametrize("tokens,experts,hidden", [(32, 8, 12), (3000, 64, 128),
+                                                   (50_000, 256, 32), (LIMIT_TOKENS, 1024, 4)])
 def test_no_alloc_matches_workspace_permute(rrlib, cuda, tokens, experts, hidden):
     lib = rrlib.lib()
     rng = np.random.default_rng(tokens + experts)
@@ -61,9 +68,49 @@ def test_no_alloc_matches_workspace_permute(rrlib, cuda, tokens, experts, hidden
 
 def test_no_alloc_rejects_oversize(rrlib, cuda):
     lib = rrlib.lib()
-    tokens, experts = 1 << 24, 1024  # scratch need far above 4 MiB
-    assert rrlib.token_permute_workspace_size(tokens, experts, 2, 0) > (4 << 20)
+    assert rrlib.token_permute_workspace_size(LIMIT_TOKENS, 1024, 2, 0) == 4 << 20
     p = ctypes.c_void_p(16)
-    st = lib.rr_token_permute_no_alloc(None, p, p, None, p, None, tokens, experts, 2, 0, _ctx())
-    assert st.code == rrlib.StatusCode.INVALID_ARGUMENT
-    assert b"4 MiB" in st.message
+    for tokens in (LIMIT_TOKENS + 1, 1 << 24):  # just above the limit; far above it
+        assert rrlib.token_permute_workspace_size(tokens, 1024, 2, 0) > (4 << 20)
+        st = lib.rr_token_permute_no_alloc(None, p, p, None, p, None, tokens, 1024, 2, 0,
+                                           _ctx())
+        assert st.code == rrlib.StatusCode.INVALID_ARGUMENT
+        assert b"4 MiB" in st.message
+
+
+def test_no_alloc_dispatch_checks_match(rrlib, cuda):
+    """The dispatch checks of rr_token_permute run before the empty-call
+    return: an unknown kernel variant or a non-sm_100 architecture is
+    rejected with the same code by both entry points, also for T=0."""
+    from raggedroute_b200._lib import RRContext
+    lib = rrlib.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    cases = [(rrlib.ARCH_AUTO, rrlib.FAMILY_CUDA_OPTIMIZED, 11),  # id above the accepted 1..10
+             (rrlib.ARCH_AUTO, rrlib.FAMILY_CUDA_NAIVE, 1),
+             (rrlib.ARCH_SM86, rrlib.FAMILY_AUTO, 0)]
+    p = ctypes.c_void_p(16)
+    for arch, family, impl in cases:
+        for tokens in (0, 4):
+            ctx = ctypes.pointer(RRContext(stream, None, 0, arch, family, impl))
+            a = lib.rr_token_permute(None, p, p, None, p, None, tokens, 8, 2, 0, ctx)
+            b = lib.rr_token_permute_no_alloc(None, p, p, None, p, None, tokens, 8, 2, 0, ctx)
+            assert a.code != 0 and a.code == b.code, (arch, family, impl, tokens, a.code, b.code)
+
+
+def test_no_alloc_after_device_reset():
+    """The array's address belongs to a CUDA context. A torch-free child
+    process calls both entry points, resets the device (cudaDeviceReset
+    through another CUDA runtime, which destroys the primary context), checks
+    that the new context has a new id, and calls both again on fresh
+    buffers: the no-alloc results must still equal rr_token_permute's and the
+    numpy stable permute, bit for bit."""
+    import os
+    import subprocess
+    import sys
+    worker = os.path.join(os.path.dirname(os.path.abspath(__file__)), "no_alloc_reset_worker.py")
+    env = dict(os.environ)
+    env.setdefault("CUDA_VISIBLE_DEVICES", "0")
+    res = subprocess.run([sys.executable, worker], capture_output=True, text=True, timeout=300,
+                         env=env)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "OK" in res.stdout, res.stdout
