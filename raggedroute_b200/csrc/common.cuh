@@ -182,6 +182,14 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
                                      const RowScatter* scatter = nullptr,
                                      const RowGather* gather = nullptr);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
+// CTA-pair engine (gemm_pair.cu) for the plain grouped/dense GEMM: 256 x 256
+// tiles on two SMs. cudaErrorNotSupported when no pair can be scheduled.
+bool gemm_pairs_enabled();
+int grouped_gemm_pair_units();
+cudaError_t launch_grouped_gemm_pair(const float* x, const float* w, const int32_t* offsets,
+                                     float* y, int experts, int rows, int hidden, int output,
+                                     cudaStream_t stream, int weight_sets,
+                                     const RowScatter* scatter);
 cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t* offsets,
                                    float* y, int experts, int rows, int hidden, int output,
                                    cudaStream_t stream, int weight_sets = 0,

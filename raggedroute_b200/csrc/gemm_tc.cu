@@ -72,6 +72,7 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "gemm_split.cuh"
 #include "sm100.cuh"
 #include "tile_sched.cuh"
 
@@ -121,58 +122,12 @@ struct alignas(1024) Smem {
 constexpr std::size_t kSmemBytes = sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "over the 227 KB of shared memory a CTA may use");
 
-struct TileGeom {
-  int expert, row0, row_end, base, col0, ncols, n_mma;
-};
-
 // kMT m-tiles of 128 rows share one B tile of 256 / kMT columns (kMT = 2 for
 // narrow outputs: the router's N=128 fills the same TMEM and shared memory).
 template <int kMT>
 __device__ __forceinline__ TileGeom geom(int t, const int32_t* offsets, int experts, int rows,
                                          const int* prefix, int n_tiles_n, int output) {
-  constexpr int kTileM = kBM * kMT;
-  constexpr int kTileN = kBN / kMT;
-  const TileCoord c = tile_coord(t, offsets, experts, rows, prefix, kTileM, kTileN, n_tiles_n);
-  TileGeom g;
-  g.expert = c.expert;
-  g.row0 = c.row0;
-  g.row_end = c.row_end;
-  g.base = (c.row0 + kTileM > c.row_end) ? c.row_end - kTileM : c.row0;
-  g.col0 = c.col0;
-  g.ncols = min(kTileN, output - c.col0);
-  g.n_mma = (g.ncols + 15) & ~15;
-  return g;
-}
-
-__device__ __forceinline__ void split4(const float4 v, float4& h, float4& l) {
-  h.x = tf32_rna(v.x);
-  h.y = tf32_rna(v.y);
-  h.z = tf32_rna(v.z);
-  h.w = tf32_rna(v.w);
-  l.x = tf32_rna(v.x - h.x);
-  l.y = tf32_rna(v.y - h.y);
-  l.z = tf32_rna(v.z - h.z);
-  l.w = tf32_rna(v.w - h.w);
-}
-
-// A operand split: hi = v with the low 13 mantissa bits cleared (the value
-// a kind::tf32 MMA reads from the raw FP32 bits), lo = v - hi (exact in FP32,
-// up to 13 significant bits, of which the MMA keeps the top 11).
-__device__ __forceinline__ void split_trunc4(const float4 v, float4& h, float4& l) {
-  h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-  h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-  h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-  h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-  l.x = v.x - h.x;
-  l.y = v.y - h.y;
-  l.z = v.z - h.z;
-  l.w = v.w - h.w;
-}
-
-// Byte offset of 16-byte chunk kc (k = 4*kc..4*kc+3) of row r in a K-major
-// tile of 16 fp32 per row with the 64-byte swizzle (TMA and UMMA agree on it).
-__device__ __forceinline__ int kmajor64_offset(int r, int kc) {
-  return r * 64 + ((kc ^ ((r >> 1) & 3)) << 4);
+  return tile_geom(t, offsets, experts, rows, prefix, n_tiles_n, output, kBM * kMT, kBN / kMT);
 }
 
 // Element (k, n) of the raw B tile as TMA stores it: N-major, unswizzled,
@@ -637,27 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
 
 // ---- host side ---------------------------------------------------------------------
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static std::once_flag once;
-  static EncodeTiledFn fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-    } else {
-      cudaGetLastError();
-    }
-  });
-  return fn;
-}
+EncodeTiledFn encode_fn() { return tensor_map_encoder(); }
 
 bool kernel_configured() {
   static std::once_flag once;
@@ -678,6 +613,28 @@ bool kernel_configured() {
 }
 
 }  // namespace
+
+bool gemm_pairs_enabled() {
+  const char* v = std::getenv("RAGGEDROUTE_B200_GEMM_PAIRS");
+  return v == nullptr || v[0] != '0';
+}
+
+EncodeTiledFn tensor_map_encoder() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    } else {
+      cudaGetLastError();
+    }
+  });
+  return fn;
+}
 
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output) {
   if (hidden <= 0 || output <= 0) return false;
@@ -743,6 +700,14 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
                             ((output + kBN / mt - 1) / (kBN / mt));
     if (tiles <= 0) return cudaSuccess;
     if (tiles < grid) grid = static_cast<int>(tiles);
+  }
+  // The plain path runs on CTA pairs (gemm_pair.cu) wherever the device can
+  // co-schedule them; RAGGEDROUTE_B200_GEMM_PAIRS=0 selects this one-CTA
+  // kernel instead (both compute the same results).
+  if (gather == nullptr && mt == 1 && gemm_pairs_enabled()) {
+    const cudaError_t pe = launch_grouped_gemm_pair(x, w, offsets, y, experts, rows, hidden,
+                                                    output, stream, weight_sets, scatter);
+    if (pe != cudaErrorNotSupported) return pe;
   }
   const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
   if (gather != nullptr) {

@@ -10,6 +10,18 @@
 
 #include "common.cuh"
 
+namespace rrb {
+
+// cuTensorMapEncodeTiled, fetched once through the runtime's driver
+// entry-point lookup (nullptr if unavailable).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
+
+}  // namespace rrb
+
 namespace rrb::sm100 {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -95,6 +107,64 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
       return false;
     }
   }
+}
+
+// ---- clusters (CTA pairs) ---------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster
+// (a shared::cluster address).
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier given by its shared::cluster address, which may
+// belong to the other CTA of the pair. Default semantics (release at CTA
+// scope), the form cluster pipelines use for cross-CTA hand-offs; a release
+// at cluster scope is a memory barrier per arrival (measured: it made membar
+// the dominant stall of the pair GEMM).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 32-bit store into the shared memory of a CTA of the cluster.
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+// Bounded wait of a CTA pair: like mbar_wait. It gives up when this CTA's
+// *failed is set (by itself or by the peer, which writes it through
+// peer_failed) or after limit_ns; on its own timeout it raises
+// kErrMbarTimeout and sets the failure flag of both CTAs, so the peer stops
+// waiting for work that will not come.
+__device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, unsigned* err_word,
+                                               volatile int* failed, uint32_t peer_failed,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
+    if (*failed) return false;
+    if (global_timer_ns() - start > limit_ns) {
+      raise_device_error(err_word, kErrMbarTimeout);
+      *failed = 1;
+      st_shared_cluster_u32(peer_failed, 1u);
+      return false;
+    }
+  }
+}
+
+// Every thread of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
 }
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) --------------
@@ -219,6 +289,50 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+
+// ---- tcgen05, CTA pair (cta_group::2) ---------------------------------------------
+
+// Issued by the same warp in both CTAs of the pair, with the same destination
+// offset; both CTAs then own the same TMEM columns.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Issued by one thread of the even CTA: D rows 0..M/2-1 land in this CTA's
+// TMEM and rows M/2..M-1 in the odd CTA's (same TMEM address); A rows and B
+// columns are read half from each CTA's shared memory at the same offsets.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at shared::cluster address `cluster_addr`
+// (this CTA's or the peer's) when every pair MMA issued so far by this thread
+// has completed. One commit per barrier: a stage or accumulator shared by the
+// pair is released with one commit to each CTA's barrier.
+__device__ __forceinline__ void mma_commit_pair_to(uint32_t cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_addr)
       : "memory");
 }
 
