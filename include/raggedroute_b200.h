@@ -113,7 +113,8 @@ size_t rr_histogram_exclusive_scan_workspace_size(int route_pairs, int experts);
  * route_pos[r] = offsets[ids[r]] + #{r' < r : ids[r'] == ids[r]} (stable,
  * route-ascending within each expert segment); x_permuted[route_pos[r], :] =
  * x[r / top_k, :]; sorted_route (optional, may be NULL) is the inverse map.
- * ctx->workspace must hold rr_token_permute_workspace_size(...) bytes; its
+ * ctx->workspace must hold rr_token_permute_workspace_size(...) bytes (the
+ * reference's experts * 4, whatever the number of tokens); its
  * first experts int32 entries end equal to the per-expert route counts (the
  * reference's cursor post-state). */
 rr_status rr_token_permute(const float* x, const int32_t* expert_ids, const int32_t* offsets,
@@ -124,13 +125,14 @@ size_t rr_token_permute_workspace_size(int tokens, int experts, int top_k, int h
 
 /* rr_token_permute for callers that cannot allocate device memory: same
  * arguments, results and checks, but ctx->workspace is ignored and the
- * scratch lives in a fixed 4 MiB array inside the library (held by every GPU
- * that loads it until exit). It has no counterpart in the reference; it
- * exists for callers whose device memory is owned by a planner or pool with
- * nothing spare, or that reach this library through a binding without access
- * to a CUDA allocator. Calls whose rr_token_permute_workspace_size exceeds
- * 4 MiB fail with RR_INVALID_ARGUMENT (checked right after the shape
- * checks; every other check is rr_token_permute's, dispatch checks first).
+ * scratch lives in a fixed 4 KB array inside the library (1024 int32, held
+ * by every GPU that loads it until exit). It has no counterpart in the
+ * reference; it exists for callers whose device memory is owned by a planner
+ * or pool with nothing spare, or that reach this library through a binding
+ * without access to a CUDA allocator. A call whose
+ * rr_token_permute_workspace_size exceeds the array fails with
+ * RR_INVALID_ARGUMENT (checked right after the shape checks; every other
+ * check is rr_token_permute's, dispatch checks first).
  * It never allocates or frees. All calls share the array, so calls that
  * overlap on the GPU race and must be serialised by the caller. The array's
  * address is looked up on the first call in each CUDA context (the first

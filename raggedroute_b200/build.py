@@ -3,8 +3,11 @@
 Every .cu/.cpp file under raggedroute_b200/csrc is compiled by nvcc for
 ``-gencode arch=compute_100a,code=sm_100a`` and linked into
 ``raggedroute_b200/libraggedroute_b200.so`` in the source tree, so the library
-travels with the working tree to the GPU host. The CUDA runtime is linked
-statically; NCCL (expert-parallel runtime) is linked dynamically.
+travels with the working tree to the GPU host. The CUDA runtime and NCCL
+(expert-parallel runtime) are linked dynamically: the library shares the
+calling application's CUDA runtime, so kernels it launches into the caller's
+streams and captured graphs are the caller's runtime objects (a caller can
+inspect or update their graph nodes).
 
 Usage: ``python -m raggedroute_b200.build [--force] [-j N]``.
 """
@@ -73,7 +76,7 @@ def build(force: bool = False, jobs: int = 8, verbose_ptxas: bool = False) -> st
     objs = [_obj(s) for s in srcs]
     if force or todo or not os.path.exists(LIB) or \
             os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + \
+        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "shared", "-o", LIB] + objs + \
             ["-lnccl", "-lpthread", "-Xlinker", "--version-script=" + EXPORTS]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:

@@ -7,9 +7,8 @@
 // deliberate: the executable architecture is kSm100 (the reference accepts
 // SM86 only, src/runtime/dispatch.cpp:239-242); the expert cap is 1024
 // instead of 64; every kernel family and research id the reference accepts
-// runs the same B200 kernel; token_permute may need more workspace than
-// experts*4 bytes for inputs larger than one CTA chunk (the size query says
-// how much) and produces the stable slot order.
+// runs the same B200 kernel; token_permute produces the stable slot order
+// with the reference's experts*4 bytes of workspace for every input size.
 #include <cuda_runtime.h>
 #include <nvtx3/nvToolsExt.h>
 
@@ -305,14 +304,9 @@ std::size_t get_histogram_exclusive_scan_workspace_size(
 std::size_t get_grouped_gemm_workspace_size(const GroupedGemmArgs&) noexcept { return 0; }
 std::size_t get_unpermute_workspace_size(const UnpermuteArgs&) noexcept { return 0; }
 
-// experts*4 bytes of cursors (src/permute/operator.cpp:17-19) plus, when the
-// routes span more than one CTA chunk, a [chunks][experts] int32 table.
+// experts*4 bytes of cursors (src/permute/operator.cpp:17-19), for every
+// input size.
 std::size_t get_token_permute_workspace_size(const TokenPermuteArgs& args) noexcept {
-  if (args.experts <= 0) return 0;
-  if (args.top_k <= 0 || args.tokens <= 0 ||
-      args.tokens > std::numeric_limits<int>::max() / args.top_k) {
-    return static_cast<std::size_t>(args.experts) * sizeof(std::int32_t);
-  }
   return rrb::permute_workspace_bytes(args.tokens, args.experts, args.top_k);
 }
 

@@ -13,18 +13,25 @@
 //
 // Design (no atomics on positions, so the result never depends on
 // scheduling): routes are cut into token-aligned chunks, one CTA each.
-//   1. count:  per-chunk expert histogram -> workspace [chunks][E].
+//   1. count:  per-chunk expert histogram -> the chunk's row of the chunk
+//              table (below).
 //   2. scan:   column-wise exclusive scan over chunks, seeded with offsets,
-//              giving each chunk its first slot per expert; also writes the
-//              cursor post-state.
+//              giving each chunk its first slot per expert, in place.
 //   3. place:  inside a chunk each warp owns a contiguous run of routes; the
 //              per-(warp, expert) counts are scanned in shared memory and the
 //              rank inside a warp step comes from __match_any_sync plus a
 //              popcount of the lower lanes. The CTA then copies each token row
 //              once from x (128-bit loads) to its top_k destinations.
-// A single chunk needs neither step 1 nor 2 nor any workspace beyond the
-// cursors. HBM traffic is the algorithmic minimum: x read once, x_permuted
-// written once, ids read three times (4 bytes per route each).
+// A single chunk needs neither step 1 nor 2. The only workspace is the
+// reference's E int32 cursors (src/permute/operator.cpp:17-19), for every
+// input size: every chunk but the last spans at least E routes and keeps its
+// row of the chunk table (E int32) in the first E entries of its own slice
+// of route_pos, which the place step reads before it overwrites that slice
+// with the route positions; the last chunk keeps its row in the cursors,
+// which the place step then overwrites with the per-expert counts (the
+// reference's post-state). No chunk reads or writes another's slice. HBM
+// traffic is the algorithmic minimum: x read once, x_permuted written once,
+// ids read three times (4 bytes per route each).
 #include "common.cuh"
 
 namespace rrb {
@@ -44,32 +51,37 @@ struct ChunkPlan {
   int chunks;
 };
 
-// The per-chunk expert table (chunks x experts int32) is kept to 1 MB: with
-// many experts the chunks grow instead (fewer, longer chunks).
-constexpr long long kMaxChunkTable = 1 << 18;
-
 ChunkPlan plan_chunks(int tokens, int top_k, int experts) {
   const long long routes = static_cast<long long>(tokens) * top_k;
   long long want = (routes + kTargetChunks - 1) / kTargetChunks;
   long long rc = 128;
   while (rc < want && rc < kMaxChunkRoutes) rc <<= 1;
-  while (rc < kMaxChunkRoutes && ((routes + rc - 1) / rc) * experts > kMaxChunkTable) rc <<= 1;
+  // A chunk's table row lives in its own slice of route_pos: >= E routes
+  // (E <= 1024 keeps this within kMaxChunkRoutes).
+  while (rc < experts) rc <<= 1;
   int tc = static_cast<int>(rc / top_k);
   if (tc < 1) tc = 1;
+  if (static_cast<long long>(tc) * top_k < experts) tc = ceil_div(experts, top_k);
   ChunkPlan p;
   p.tokens_per_chunk = tc;
   p.chunks = tokens <= 0 ? 0 : ceil_div(tokens, tc);
   return p;
 }
 
-std::size_t align256(std::size_t v) { return (v + 255) & ~static_cast<std::size_t>(255); }
-
 __device__ __forceinline__ int warp_leader(unsigned peers) { return __ffs(peers) - 1; }
 
-// Per-chunk histogram: chunk_hist[c][e].
+// Row c of the chunk table: the first E entries of chunk c's slice of
+// route_pos, or the cursors for the last chunk.
+__device__ __forceinline__ int32_t* chunk_row(int32_t* route_pos, int32_t* cursors, int c,
+                                              int chunks, int routes_per_chunk) {
+  return c == chunks - 1 ? cursors
+                         : route_pos + static_cast<long long>(c) * routes_per_chunk;
+}
+
+// Per-chunk histogram into the chunk's table row.
 __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
     const int32_t* __restrict__ ids, int routes, int experts, int routes_per_chunk,
-    int32_t* __restrict__ chunk_hist) {
+    int32_t* route_pos, int32_t* cursors) {
   extern __shared__ int hist[];
   for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -84,16 +96,17 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
     if (lane == warp_leader(peers) && e >= 0 && e < experts) atomicAdd(hist + e, __popc(peers));
   }
   __syncthreads();
-  int32_t* row = chunk_hist + static_cast<long long>(blockIdx.x) * experts;
+  int32_t* row = chunk_row(route_pos, cursors, blockIdx.x, gridDim.x, routes_per_chunk);
   for (int i = threadIdx.x; i < experts; i += blockDim.x) row[i] = hist[i];
 }
 
-// Column-wise exclusive scan over chunks, seeded with offsets. Each CTA owns
-// 32 experts (one per lane); its 32 warps split the chunk range.
-__global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict__ chunk_hist,
+// Column-wise exclusive scan over the chunk table, in place, seeded with
+// offsets. Each CTA owns 32 experts (one per lane); its 32 warps split the
+// chunk range.
+__global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, int32_t* cursors,
                                                             const int32_t* __restrict__ offsets,
-                                                            int32_t* __restrict__ cursors,
-                                                            int chunks, int experts) {
+                                                            int chunks, int routes_per_chunk,
+                                                            int experts) {
   __shared__ int part[32][33];
   const int lane = threadIdx.x & 31;
   const int grp = threadIdx.x >> 5;
@@ -108,7 +121,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict_
       int v[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
-        v[u] = c + u < c1 ? chunk_hist[static_cast<long long>(c + u) * experts + e] : 0;
+        v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] : 0;
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) sum += v[u];
@@ -131,16 +144,14 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* __restrict_
       int v[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
-        v[u] = c + u < c1 ? chunk_hist[static_cast<long long>(c + u) * experts + e] : 0;
+        v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] : 0;
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
-        if (c + u < c1) chunk_hist[static_cast<long long>(c + u) * experts + e] = run;
+        if (c + u < c1) chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] = run;
         run += v[u];
       }
     }
-    // The group that owns the last chunk holds the grand total.
-    if (c1 == chunks && c0 < c1) cursors[e] = run - offsets[e];
   }
 }
 
@@ -226,17 +237,17 @@ __device__ __forceinline__ void copy_row_warp_to(const float* __restrict__ src, 
   }
 }
 
-// Place + copy. chunk_base == nullptr means a single chunk seeded by offsets
-// (and this kernel then also writes the cursor post-state).
+// Place + copy. With one chunk the slots are seeded by offsets; with several,
+// by the chunk's row of the scanned chunk table. The single or last chunk
+// writes the cursor post-state (per-expert counts).
 // With kPeer the rows go to the owners' receive buffers (PeerDispatch) and
 // xp / sorted_route are unused.
 template <bool kVec, bool kPeer>
 __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ ids,
-    const int32_t* __restrict__ offsets, const int32_t* __restrict__ chunk_base,
-    float* __restrict__ xp, int32_t* __restrict__ route_pos, int32_t* __restrict__ sorted_route,
-    int32_t* __restrict__ cursors, int tokens, int experts, int top_k, int hidden,
-    int tokens_per_chunk, const PeerDispatch peer) {
+    const int32_t* __restrict__ offsets, float* __restrict__ xp, int32_t* route_pos,
+    int32_t* __restrict__ sorted_route, int32_t* cursors, int tokens, int experts, int top_k,
+    int hidden, int tokens_per_chunk, const PeerDispatch peer) {
   extern __shared__ int smem[];
   int* warp_base = smem;                            // [kPlaceWarps][experts]
   int* pos = smem + kPlaceWarps * experts;          // [routes in chunk]
@@ -280,18 +291,22 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
   }
   __syncthreads();
 
-  // Per-(warp, expert) starting slots.
+  // Per-(warp, expert) starting slots, from the chunk's table row (read
+  // here, before pass 2 overwrites this chunk's slice of route_pos).
+  const bool chunked = gridDim.x > 1;
+  const bool last = blockIdx.x == gridDim.x - 1;
+  const int32_t* row =
+      chunked ? chunk_row(route_pos, cursors, blockIdx.x, gridDim.x, tokens_per_chunk * top_k)
+              : offsets;
   for (int e = threadIdx.x; e < experts; e += blockDim.x) {
-    int run = chunk_base != nullptr ? chunk_base[static_cast<long long>(blockIdx.x) * experts + e]
-                                    : offsets[e];
-    const int first = run;
+    int run = row[e];
 #pragma unroll
     for (int w = 0; w < kPlaceWarps; ++w) {
       const int v = warp_base[w * experts + e];
       warp_base[w * experts + e] = run;
       run += v;
     }
-    if (chunk_base == nullptr) cursors[e] = run - first;
+    if (last) cursors[e] = run - offsets[e];
   }
   __syncthreads();
 
@@ -471,13 +486,8 @@ __global__ void __launch_bounds__(256) permute_copy_kernel(const float* __restri
 
 }  // namespace
 
-std::size_t permute_workspace_bytes(int tokens, int experts, int top_k) {
-  if (experts <= 0) return 0;
-  const std::size_t cursors = static_cast<std::size_t>(experts) * sizeof(int32_t);
-  if (tokens <= 0 || top_k <= 0) return cursors;
-  const ChunkPlan p = plan_chunks(tokens, top_k, experts);
-  if (p.chunks <= 1) return cursors;
-  return align256(cursors) + static_cast<std::size_t>(p.chunks) * experts * sizeof(int32_t);
+std::size_t permute_workspace_bytes(int, int experts, int) {
+  return experts <= 0 ? 0 : static_cast<std::size_t>(experts) * sizeof(int32_t);
 }
 
 namespace {
@@ -490,16 +500,13 @@ cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offs
   if (tokens <= 0) return cudaSuccess;
   const ChunkPlan p = plan_chunks(tokens, top_k, experts);
   int32_t* cursors = static_cast<int32_t*>(workspace);
-  int32_t* chunk_base = nullptr;
   const int routes_per_chunk = p.tokens_per_chunk * top_k;
   const int routes = tokens * top_k;
   if (p.chunks > 1) {
-    chunk_base = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) +
-                                            align256(static_cast<std::size_t>(experts) * 4));
     permute_count_kernel<<<p.chunks, kPlaceThreads, experts * sizeof(int), stream>>>(
-        ids, routes, experts, routes_per_chunk, chunk_base);
-    permute_scan_kernel<<<ceil_div(experts, 32), 1024, 0, stream>>>(chunk_base, offsets, cursors,
-                                                                      p.chunks, experts);
+        ids, routes, experts, routes_per_chunk, route_pos, cursors);
+    permute_scan_kernel<<<ceil_div(experts, 32), 1024, 0, stream>>>(
+        route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
     note_launch(2);
   }
   // Peer mode keeps pos[] at its full size so the int64 table that follows is
@@ -523,12 +530,12 @@ cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offs
   }
   if (vec) {
     permute_place_kernel<true, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
-        x, ids, offsets, chunk_base, x_permuted, route_pos, sorted_route, cursors, tokens,
-        experts, top_k, hidden, p.tokens_per_chunk, peer);
+        x, ids, offsets, x_permuted, route_pos, sorted_route, cursors, tokens, experts, top_k,
+        hidden, p.tokens_per_chunk, peer);
   } else {
     permute_place_kernel<false, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
-        x, ids, offsets, chunk_base, x_permuted, route_pos, sorted_route, cursors, tokens,
-        experts, top_k, hidden, p.tokens_per_chunk, peer);
+        x, ids, offsets, x_permuted, route_pos, sorted_route, cursors, tokens, experts, top_k,
+        hidden, p.tokens_per_chunk, peer);
   }
   note_launch();
   return cudaGetLastError();

@@ -8,8 +8,10 @@
 // with its scratch (the per-expert cursors and the per-chunk expert table)
 // in a fixed array that lives in this library's device image:
 //
-//   * size: kNoAllocScratchBytes (4 MiB) per GPU, held by every GPU that
-//     loads the library until the process exits;
+//   * size: kNoAllocScratchBytes (4 KB: the per-expert cursors of the
+//     largest expert count, which is all the permute needs for any number
+//     of tokens) per GPU, held by every GPU that loads the library until the
+//     process exits;
 //   * a call whose scratch need (rr_token_permute_workspace_size) exceeds it
 //     fails with RR_INVALID_ARGUMENT before any launch; this size check
 //     comes right after the shape checks, the rest of the validation is
@@ -44,7 +46,7 @@
 namespace rrb {
 namespace {
 
-constexpr std::size_t kNoAllocScratchBytes = 4u << 20;
+constexpr std::size_t kNoAllocScratchBytes = kMaxExperts * sizeof(int32_t);
 
 // The scratch itself. In host code `g_no_alloc_scratch` names a host-side
 // stand-in, not device memory: only the address from cudaGetSymbolAddress
@@ -178,7 +180,7 @@ rr_status rr_token_permute_no_alloc(const float* x, const int32_t* expert_ids,
   const std::size_t need = rrb::permute_workspace_bytes(tokens, experts, top_k);
   if (need > rrb::kNoAllocScratchBytes) {
     return make(RR_INVALID_ARGUMENT,
-                "token_permute_no_alloc: scratch need exceeds the 4 MiB static array; "
+                "token_permute_no_alloc: scratch need exceeds the 4 KB static array; "
                 "use rr_token_permute with a caller workspace");
   }
   // The dispatch checks of rr_token_permute (architecture, kernel family

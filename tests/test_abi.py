@@ -49,8 +49,19 @@ def test_cpp_api_symbols_exported(rrlib):
                "raggedroute::ops::launch_cache_scrub(", "raggedroute::chain_from_tokens(",
                "raggedroute::get_token_permute_workspace_size("]:
         assert fn in out, fn
-    # The statically linked CUDA runtime stays private.
+    # Every candidate launcher declared in include/raggedroute/candidate_ops.h.
+    text = open(os.path.join(ROOT, "include", "raggedroute", "candidate_ops.h")).read()
+    candidates = re.findall(r"cudaError_t (launch_[a-z0-9_]+)\(", text)
+    assert len(candidates) == 7
+    for fn in candidates:
+        assert f"raggedroute::ops::{fn}(" in out, fn
+    # The wrappers' internal helpers stay private, and the CUDA runtime is
+    # the caller's (linked dynamically, not exported from here).
     assert "cudaMalloc" not in out
+    assert "raggedroute::detail" not in out
+    deps = subprocess.run(["readelf", "-d", rrlib.library_path], capture_output=True, text=True,
+                          check=True).stdout
+    assert "libcudart.so.12" in deps
 
 
 def _ctx(arch=4, family=0, impl=0, ws=None, ws_bytes=0):
@@ -88,8 +99,11 @@ def test_workspace_queries(rrlib):
     lib = rrlib.lib()
     assert lib.rr_token_permute_workspace_size(1, 2, 1, 0) == 8
     assert lib.rr_token_permute_workspace_size(2, 2, 2, 2) == 8
-    big = lib.rr_token_permute_workspace_size(1 << 19, 256, 2, 128)
-    assert big > 256 * 4
+    # The reference's E*4 cursor bytes (src/permute/operator.cpp:17-19) at
+    # every size: the multi-CTA chunk table lives in route_pos.
+    for tokens in (1 << 10, 1 << 19, 1 << 24):
+        for experts in (2, 64, 256, 1024):
+            assert lib.rr_token_permute_workspace_size(tokens, experts, 2, 128) == 4 * experts
     # The chain workspace: the permute workspace at 2T routes, 256-byte
     # aligned, then sorted_route [2T] for the row-gathering variant.
     perm = lib.rr_token_permute_workspace_size(65536, 128, 2, 4096)
