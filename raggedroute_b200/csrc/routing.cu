@@ -7,10 +7,18 @@
 // (src/scan/cuda_naive/baseline.cu:12-26). Integer results are exact and
 // independent of scheduling.
 //
-// Design: ids stream through 128-bit loads; each CTA keeps a shared-memory
-// histogram and adds one warp-aggregated update per distinct expert per 32
-// ids (__match_any_sync), so an all-to-one-expert input does not serialise on
-// one shared-memory address. Three ways to merge the CTA histograms, by size:
+// Design: ids stream through 128-bit loads; each CTA keeps R shared-memory
+// copies of its histogram (R a power of two, 32 for E <= 256, fewer for more
+// experts so that the copies fit in 40 KB) and lane l adds to copy l % R with
+// a plain shared atomic. The copies are E + 1 words apart, so the same
+// expert's counters in different copies sit in different banks: an
+// all-to-one-expert input conflicts at most 32 / R ways per instruction and a
+// spread-out input touches mostly distinct banks; the copies are folded at
+// the end. (Warp aggregation
+// with __match_any_sync, measured earlier, costs in proportion to the number
+// of distinct experts in a warp: 1M uniform routes took 14.4 us over 256
+// experts against 6.2 us over one.) Three ways to merge the CTA histograms,
+// by size:
 //   * up to 32K routes: one CTA does everything (no merge, no reset);
 //   * up to 256K routes: one thread-block cluster (16 CTAs, or 8 where a
 //     16-CTA cluster cannot be placed); after a cluster barrier CTA 0 sums
@@ -19,9 +27,9 @@
 //     global atomic, and a second barrier keeps every CTA's shared memory
 //     alive until CTA 0 has read it;
 //   * beyond: CTAs merge into zeroed counts with one global atomic per
-//     non-empty bin, and the last CTA to finish (ticket taken on offsets[E],
-//     which the scan then overwrites with the total) performs the scan, so no
-//     scratch memory is needed.
+//     non-empty bin, and the fused operator then scans in a second, one-CTA
+//     launch (measured at 1M routes: a last-CTA scan behind a ticket and a
+//     fence inside the same launch was slower than the separate scan).
 #include <cooperative_groups.h>
 
 #include <mutex>
@@ -34,22 +42,48 @@ namespace {
 constexpr int kHistThreads = 512;
 // Up to this many routes the fused operator runs in a single CTA.
 constexpr int kFusedSingleCtaMaxRoutes = 1 << 15;
+// Shared memory for a CTA's histogram copies: copy r of counter e is
+// hist[r * (E + 1) + e].
+constexpr int kReplicaBytes = 40 * 1024;
 
-__device__ __forceinline__ void warp_add(int* hist, int e, int experts) {
-  const unsigned peers = __match_any_sync(0xffffffffu, e);
-  const int leader = __ffs(peers) - 1;
-  if ((threadIdx.x & 31) == leader && e >= 0 && e < experts) {
-    atomicAdd(hist + e, __popc(peers));
+// Copies for E experts: the largest power of two <= 32 that fits.
+int hist_replicas(int experts) {
+  int r = 32;
+  while (r > 1 && static_cast<long long>(r) * (experts + 1) * 4 > kReplicaBytes) r >>= 1;
+  return r;
+}
+
+std::size_t hist_smem(int experts) {
+  return static_cast<std::size_t>(hist_replicas(experts)) * (experts + 1) * sizeof(int);
+}
+
+__device__ __forceinline__ void warp_add(int* mine, int e, int experts) {
+  if (e >= 0 && e < experts) atomicAdd(mine + e, 1);
+}
+
+// Zeroes the copies. All threads of the CTA; a barrier must follow.
+__device__ __forceinline__ void zero_replicas(int* hist, int experts, int reps) {
+  for (int i = threadIdx.x; i < reps * (experts + 1); i += blockDim.x) hist[i] = 0;
+}
+
+// Folds the copies into hist[0..experts). All threads; call after a barrier
+// that follows the accumulation; a barrier must follow.
+__device__ __forceinline__ void fold_replicas(int* hist, int experts, int reps) {
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) {
+    int v = hist[i];
+    for (int r = 1; r < reps; ++r) v += hist[r * (experts + 1) + i];
+    hist[i] = v;
   }
 }
 
 // Adds the histogram of ids[begin, end) (a contiguous slice per CTA) to the
-// shared histogram. All threads of the CTA must call it.
+// shared histogram copies. All threads of the CTA must call it.
 __device__ void accumulate_slice(const int32_t* __restrict__ ids, long long begin, long long end,
-                                 int* hist, int experts, bool vec) {
+                                 int* hist, int experts, int reps, bool vec) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
+  int* mine = hist + (lane & (reps - 1)) * (experts + 1);
   if (vec) {
     // begin is a multiple of 4 and ids is 16-byte aligned.
     const long long n4 = (end - begin) >> 2;
@@ -65,22 +99,22 @@ __device__ void accumulate_slice(const int32_t* __restrict__ ids, long long begi
       }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        warp_add(hist, v[u].x, experts);
-        warp_add(hist, v[u].y, experts);
-        warp_add(hist, v[u].z, experts);
-        warp_add(hist, v[u].w, experts);
+        warp_add(mine, v[u].x, experts);
+        warp_add(mine, v[u].y, experts);
+        warp_add(mine, v[u].z, experts);
+        warp_add(mine, v[u].w, experts);
       }
     }
     for (long long base = begin + (n4 << 2) + static_cast<long long>(warp) * 32; base < end;
          base += static_cast<long long>(warps) * 32) {
       const int e = (base + lane < end) ? __ldg(ids + base + lane) : -1;
-      warp_add(hist, e, experts);
+      warp_add(mine, e, experts);
     }
   } else {
     for (long long base = begin + static_cast<long long>(warp) * 32; base < end;
          base += static_cast<long long>(warps) * 32) {
       const int e = (base + lane < end) ? __ldg(ids + base + lane) : -1;
-      warp_add(hist, e, experts);
+      warp_add(mine, e, experts);
     }
   }
 }
@@ -96,13 +130,15 @@ __device__ __forceinline__ void slice_of(long long routes, long long& begin, lon
 
 __global__ void __launch_bounds__(kHistThreads) histogram_accumulate_kernel(
     const int32_t* __restrict__ ids, int32_t* __restrict__ counts, int routes, int experts,
-    bool vec) {
+    int reps, bool vec) {
   extern __shared__ int hist[];
-  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  zero_replicas(hist, experts, reps);
   __syncthreads();
   long long begin, end;
   slice_of(routes, begin, end);
-  accumulate_slice(ids, begin, end, hist, experts, vec);
+  accumulate_slice(ids, begin, end, hist, experts, reps, vec);
+  __syncthreads();
+  fold_replicas(hist, experts, reps);
   __syncthreads();
   for (int i = threadIdx.x; i < experts; i += blockDim.x) {
     const int c = hist[i];
@@ -163,12 +199,14 @@ __global__ void __launch_bounds__(1024) hist_scan_single_kernel(const int32_t* _
                                                                 int32_t* __restrict__ counts,
                                                                 int32_t* __restrict__ offsets,
                                                                 int routes, int experts,
-                                                                bool vec) {
-  __shared__ int hist[kMaxExperts];
+                                                                int reps, bool vec) {
+  extern __shared__ int hist[];
   __shared__ int warp_sums[32];
-  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  zero_replicas(hist, experts, reps);
   __syncthreads();
-  accumulate_slice(ids, 0, routes, hist, experts, vec);
+  accumulate_slice(ids, 0, routes, hist, experts, reps, vec);
+  __syncthreads();
+  fold_replicas(hist, experts, reps);
   __syncthreads();
   const int t = threadIdx.x;
   const int v = t < experts ? hist[t] : 0;
@@ -194,17 +232,19 @@ constexpr long long kClusterMaxRoutes = 1LL << 18;
 template <bool kScan>
 __global__ void __launch_bounds__(kClusterThreads) hist_cluster_kernel(
     const int32_t* __restrict__ ids, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-    int routes, int experts, bool vec) {
+    int routes, int experts, int reps, bool vec) {
   namespace cg = cooperative_groups;
   extern __shared__ int hist[];
   __shared__ int warp_sums[32];
   cg::cluster_group cluster = cg::this_cluster();
-  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
+  zero_replicas(hist, experts, reps);
   __syncthreads();
   long long begin, end;
   slice_of(routes, begin, end);
-  accumulate_slice(ids, begin, end, hist, experts, vec);
-  cluster.sync();  // every CTA's histogram is complete and visible
+  accumulate_slice(ids, begin, end, hist, experts, reps, vec);
+  __syncthreads();
+  fold_replicas(hist, experts, reps);
+  cluster.sync();  // every CTA's folded histogram is complete and visible
   if (cluster.block_rank() == 0) {
     const int e = threadIdx.x;
     const int nblocks = static_cast<int>(cluster.num_blocks());
@@ -221,47 +261,6 @@ __global__ void __launch_bounds__(kClusterThreads) hist_cluster_kernel(
     }
   }
   cluster.sync();  // CTA 0 has read every CTA's shared memory
-}
-
-// counts and offsets[experts] are zero on entry.
-__global__ void __launch_bounds__(kHistThreads) hist_scan_multi_kernel(
-    const int32_t* __restrict__ ids, int32_t* counts, int32_t* offsets, int routes, int experts,
-    bool vec) {
-  extern __shared__ int hist[];
-  __shared__ int warp_sums[32];
-  __shared__ bool last;
-  for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  long long begin, end;
-  slice_of(routes, begin, end);
-  accumulate_slice(ids, begin, end, hist, experts, vec);
-  __syncthreads();
-  for (int i = threadIdx.x; i < experts; i += blockDim.x) {
-    const int c = hist[i];
-    if (c != 0) atomicAdd(counts + i, c);
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ticket = atomicAdd(offsets + experts, 1);
-    last = ticket == static_cast<int>(gridDim.x) - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  // Last CTA: exclusive scan of the merged counts (experts <= 1024, so the
-  // scan runs in chunks of blockDim.x with a running carry).
-  int carry = 0;
-  for (int base = 0; base < experts; base += blockDim.x) {
-    const int t = base + threadIdx.x;
-    const int v = t < experts ? __ldcg(counts + t) : 0;
-    int total = 0;
-    const int excl = block_exclusive_scan(v, warp_sums, &total);
-    if (t < experts) offsets[t] = carry + excl;
-    carry += total;
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) offsets[experts] = carry;
 }
 
 // Expert-parallel receive offsets: group q = p * local + le holds the rows
@@ -340,7 +339,7 @@ int hist_cluster_size() {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(16);
       cfg.blockDim = dim3(kClusterThreads);
-      cfg.dynamicSmemBytes = kMaxExperts * sizeof(int);
+      cfg.dynamicSmemBytes = kReplicaBytes;  // the most any launch asks for
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 16;
@@ -367,7 +366,7 @@ cudaError_t launch_hist_cluster(const int32_t* ids, int32_t* counts, int32_t* of
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(size);
   cfg.blockDim = dim3(kClusterThreads);
-  cfg.dynamicSmemBytes = static_cast<std::size_t>(experts) * sizeof(int);
+  cfg.dynamicSmemBytes = hist_smem(experts);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -378,7 +377,7 @@ cudaError_t launch_hist_cluster(const int32_t* ids, int32_t* counts, int32_t* of
   cfg.numAttrs = 1;
   const cudaError_t err =
       cudaLaunchKernelEx(&cfg, hist_cluster_kernel<kScan>, ids, counts, offsets, routes, experts,
-                         vec);
+                         hist_replicas(experts), vec);
   if (err != cudaSuccess) return err;
   note_launch();
   return cudaGetLastError();
@@ -404,8 +403,8 @@ cudaError_t launch_histogram_accumulate(const int32_t* ids, int32_t* counts, int
                                         int experts, cudaStream_t stream) {
   if (routes <= 0) return cudaSuccess;
   const bool vec = aligned_to(ids, 16);
-  histogram_accumulate_kernel<<<hist_grid(routes), kHistThreads, experts * sizeof(int),
-                                stream>>>(ids, counts, routes, experts, vec);
+  histogram_accumulate_kernel<<<hist_grid(routes), kHistThreads, hist_smem(experts), stream>>>(
+      ids, counts, routes, experts, hist_replicas(experts), vec);
   note_launch();
   return cudaGetLastError();
 }
@@ -436,7 +435,8 @@ cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
                                             cudaStream_t stream) {
   const bool vec = aligned_to(ids, 16);
   if (routes <= kFusedSingleCtaMaxRoutes) {
-    hist_scan_single_kernel<<<1, 1024, 0, stream>>>(ids, counts, offsets, routes, experts, vec);
+    hist_scan_single_kernel<<<1, 1024, hist_smem(experts), stream>>>(
+        ids, counts, offsets, routes, experts, hist_replicas(experts), vec);
     note_launch();
     return cudaGetLastError();
   }
@@ -448,12 +448,9 @@ cudaError_t launch_histogram_exclusive_scan(const int32_t* ids, int32_t* counts,
   }
   cudaError_t err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * experts, stream);
   if (err != cudaSuccess) return err;
-  err = cudaMemsetAsync(offsets + experts, 0, sizeof(int32_t), stream);
+  err = launch_histogram_accumulate(ids, counts, routes, experts, stream);
   if (err != cudaSuccess) return err;
-  hist_scan_multi_kernel<<<hist_grid(routes), kHistThreads, experts * sizeof(int), stream>>>(
-      ids, counts, offsets, routes, experts, vec);
-  note_launch();
-  return cudaGetLastError();
+  return launch_exclusive_scan(counts, offsets, experts, stream);
 }
 
 cudaError_t launch_ep_recv_offsets(const int32_t* count_all, int32_t* recv_offsets, int nranks,

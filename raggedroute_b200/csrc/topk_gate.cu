@@ -9,46 +9,49 @@
 //
 // Design: a row is owned by a group of L lanes (L = 1..32, a power of two) so
 // one warp covers 32/L rows and every lane issues 128-bit loads when the row
-// stride allows it. Candidates are packed into a 64-bit key
-//   (order-preserving bits of the value) << 32 | (~expert id)
-// so "precedes" is a plain unsigned comparison: -0 is canonicalised to +0
-// first (they compare equal in float), NaN becomes -inf, and the id half
-// breaks ties toward the lower id. Each lane keeps its local top-2 keys; the
-// group merges them with xor shuffles. The kernel is HBM-bound: 4*E bytes in
-// and 16 bytes out per row. An optional remap table rewrites each selected id
-// on output (the expert-parallel runtime's replicated "virtual" experts).
+// stride allows it. A candidate is (value, expert id) with NaN read as -inf
+// and -0 as +0; (v, e) precedes (w, f) when v > w, or v == w and e < f. A
+// lane sees its candidates in increasing id order, so inside a lane a later
+// candidate with an equal value never precedes an earlier one and one float
+// compare decides; the L partial top-2 lists of a row merge by xor shuffles
+// with the full rule. An all-NaN row therefore ranks ids 0 and 1 (both -inf,
+// lower ids first) with equal values, which is the reference's {0,1} /
+// {0.5,0.5} outcome. The grid is one resident wave; CTAs loop over row
+// groups, so no second, partly filled wave of CTAs trails the first. The
+// kernel is HBM-bound: 4*E bytes in and 16 bytes out per row. An optional
+// remap table rewrites each selected id on output (the expert-parallel
+// runtime's replicated "virtual" experts).
+#include <limits>
+
 #include "common.cuh"
 
 namespace rrb {
 namespace {
 
-__device__ __forceinline__ unsigned long long make_key(float raw, int id, bool& non_nan) {
-  const bool is_nan = raw != raw;
-  non_nan = non_nan || !is_nan;
-  float v = is_nan ? -__int_as_float(0x7f800000) : raw + 0.0f;  // -0 -> +0
-  const unsigned b = __float_as_uint(v);
-  const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return (static_cast<unsigned long long>(ord) << 32) | static_cast<unsigned>(0xffffffffu - id);
-}
+constexpr float kNegInf = -std::numeric_limits<float>::infinity();
 
-__device__ __forceinline__ float key_value(unsigned long long key) {
-  const unsigned ord = static_cast<unsigned>(key >> 32);
-  const unsigned b = (ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord;
-  return __uint_as_float(b);
-}
+__device__ __forceinline__ float canonical(float v) { return v != v ? kNegInf : v + 0.0f; }
 
-__device__ __forceinline__ int key_id(unsigned long long key) {
-  return static_cast<int>(0xffffffffu - static_cast<unsigned>(key));
-}
-
-__device__ __forceinline__ void insert(unsigned long long key, unsigned long long& k1,
-                                       unsigned long long& k2) {
-  if (key > k1) {
-    k2 = k1;
-    k1 = key;
-  } else if (key > k2) {
-    k2 = key;
+// Candidate e (larger than every id seen so far in this lane) into the
+// lane's top-2; an id of -1 marks an empty slot.
+__device__ __forceinline__ void insert_in_order(float v, int e, float& v1, int& i1, float& v2,
+                                                int& i2) {
+  if (v > v1 || i1 < 0) {
+    v2 = v1;
+    i2 = i1;
+    v1 = v;
+    i1 = e;
+  } else if (v > v2 || i2 < 0) {
+    v2 = v;
+    i2 = e;
   }
+}
+
+// (v, e) precedes (w, f): larger value, then lower id; empty slots last.
+__device__ __forceinline__ bool precedes(float v, int e, float w, int f) {
+  if (e < 0) return false;
+  if (f < 0) return true;
+  return v > w || (v == w && e < f);
 }
 
 // kPer: 128-bit loads each lane issues before it ranks them (all in flight at
@@ -63,105 +66,109 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
                                                         const int32_t* __restrict__ remap) {
   constexpr int kRowsPerWarp = 32 / L;
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
   const int group = lane / L;
   const int j = lane % L;
-  const long long row = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp) *
-                            kRowsPerWarp + group;
-  const bool active = row < tokens;
-
-  unsigned long long k1 = 0, k2 = 0;
-  bool non_nan = false;
-  if (active) {
-    const float* src = logits + row * experts;
-    if constexpr (kVec) {
-      const int nvec = experts >> 2;
-      const float4* src4 = reinterpret_cast<const float4*>(src);
-      const float4* bias4 = reinterpret_cast<const float4*>(bias);
-      // Keys order candidates totally (value, then lower id), so the order
-      // in which a lane ranks its candidates does not change the result.
-      for (int q0 = j; q0 < nvec; q0 += L * kPer) {
-        float4 v[kPer];
+  const long long warps_total = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long wrow = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) +
+                        (threadIdx.x >> 5);
+       wrow * kRowsPerWarp < tokens; wrow += warps_total) {
+    const long long row = wrow * kRowsPerWarp + group;
+    const bool active = row < tokens;
+    float v1 = kNegInf, v2 = kNegInf;
+    int i1 = -1, i2 = -1;
+    if (active) {
+      const float* src = logits + row * experts;
+      if constexpr (kVec) {
+        const int nvec = experts >> 2;
+        const float4* src4 = reinterpret_cast<const float4*>(src);
+        const float4* bias4 = reinterpret_cast<const float4*>(bias);
+        for (int q0 = j; q0 < nvec; q0 += L * kPer) {
+          float4 v[kPer];
 #pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-          const int q = q0 + u * L;
-          if (q < nvec) v[u] = __ldcs(src4 + q);
-        }
+          for (int u = 0; u < kPer; ++u) {
+            const int q = q0 + u * L;
+            if (q < nvec) v[u] = __ldcs(src4 + q);
+          }
 #pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-          const int q = q0 + u * L;
-          if (q < nvec) {
-            if (bias != nullptr) {
-              const float4 b = __ldg(bias4 + q);
-              v[u].x = v[u].x + b.x;
-              v[u].y = v[u].y + b.y;
-              v[u].z = v[u].z + b.z;
-              v[u].w = v[u].w + b.w;
+          for (int u = 0; u < kPer; ++u) {
+            const int q = q0 + u * L;
+            if (q < nvec) {
+              if (bias != nullptr) {
+                const float4 b = __ldg(bias4 + q);
+                v[u].x = v[u].x + b.x;
+                v[u].y = v[u].y + b.y;
+                v[u].z = v[u].z + b.z;
+                v[u].w = v[u].w + b.w;
+              }
+              const int e = q << 2;
+              insert_in_order(canonical(v[u].x), e, v1, i1, v2, i2);
+              insert_in_order(canonical(v[u].y), e + 1, v1, i1, v2, i2);
+              insert_in_order(canonical(v[u].z), e + 2, v1, i1, v2, i2);
+              insert_in_order(canonical(v[u].w), e + 3, v1, i1, v2, i2);
             }
-            const int e = q << 2;
-            insert(make_key(v[u].x, e, non_nan), k1, k2);
-            insert(make_key(v[u].y, e + 1, non_nan), k1, k2);
-            insert(make_key(v[u].z, e + 2, non_nan), k1, k2);
-            insert(make_key(v[u].w, e + 3, non_nan), k1, k2);
           }
         }
-      }
-    } else {
+      } else {
 #pragma unroll 4
-      for (int e = j; e < experts; e += L) {
-        float v = __ldg(src + e);
-        if (bias != nullptr) v = v + __ldg(bias + e);
-        insert(make_key(v, e, non_nan), k1, k2);
+        for (int e = j; e < experts; e += L) {
+          float v = __ldg(src + e);
+          if (bias != nullptr) v = v + __ldg(bias + e);
+          insert_in_order(canonical(v), e, v1, i1, v2, i2);
+        }
       }
     }
-  }
 
-  // Merge the L partial top-2 lists of this row's lane group.
+    // Merge the L partial top-2 lists of this row's lane group.
 #pragma unroll
-  for (int off = L / 2; off > 0; off >>= 1) {
-    const unsigned long long o1 = __shfl_xor_sync(0xffffffffu, k1, off);
-    const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, k2, off);
-    const bool o_nan = __shfl_xor_sync(0xffffffffu, non_nan ? 1 : 0, off) != 0;
-    non_nan = non_nan || o_nan;
-    if (o1 > k1) {
-      k2 = (k1 > o2) ? k1 : o2;
-      k1 = o1;
-    } else {
-      k2 = (o1 > k2) ? o1 : k2;
+    for (int off = L / 2; off > 0; off >>= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, v1, off);
+      const int p1 = __shfl_xor_sync(0xffffffffu, i1, off);
+      const float o2 = __shfl_xor_sync(0xffffffffu, v2, off);
+      const int p2 = __shfl_xor_sync(0xffffffffu, i2, off);
+      if (precedes(o1, p1, v1, i1)) {
+        // The other list's first leads; second is the better of ours and its second.
+        if (precedes(v1, i1, o2, p2)) {
+          v2 = v1;
+          i2 = i1;
+        } else {
+          v2 = o2;
+          i2 = p2;
+        }
+        v1 = o1;
+        i1 = p1;
+      } else if (precedes(o1, p1, v2, i2)) {
+        v2 = o1;
+        i2 = p1;
+      }
     }
-  }
 
-  if (!active || j != 0) return;
-  int id0 = key_id(k1);
-  int id1 = key_id(k2);
-  const float v0 = key_value(k1);
-  const float v1 = key_value(k2);
-  float w0 = 0.5f, w1 = 0.5f;
-  if (!non_nan) {
-    id0 = 0;
-    id1 = 1;
-  } else if (v0 != v1) {
-    if (v0 == __int_as_float(0x7f800000) || v1 == -__int_as_float(0x7f800000)) {
-      w0 = 1.0f;
-      w1 = 0.0f;
-    } else {
-      const float rel = expf(v1 - v0);
-      w0 = 1.0f / (1.0f + rel);
-      w1 = rel * w0;
+    if (!active || j != 0) continue;
+    int id0 = i1;
+    int id1 = i2;
+    float w0 = 0.5f, w1 = 0.5f;
+    if (v1 != v2) {
+      if (v1 == -kNegInf || v2 == kNegInf) {
+        w0 = 1.0f;
+        w1 = 0.0f;
+      } else {
+        const float rel = expf(v2 - v1);
+        w0 = 1.0f / (1.0f + rel);
+        w1 = rel * w0;
+      }
     }
-  }
-  if (remap != nullptr) {
-    id0 = __ldg(remap + id0);
-    id1 = __ldg(remap + id1);
-  }
-  if (pair_stores) {
-    reinterpret_cast<int2*>(ids)[row] = make_int2(id0, id1);
-    reinterpret_cast<float2*>(weights)[row] = make_float2(w0, w1);
-  } else {
-    ids[2 * row] = id0;
-    ids[2 * row + 1] = id1;
-    weights[2 * row] = w0;
-    weights[2 * row + 1] = w1;
+    if (remap != nullptr) {
+      id0 = __ldg(remap + id0);
+      id1 = __ldg(remap + id1);
+    }
+    if (pair_stores) {
+      reinterpret_cast<int2*>(ids)[row] = make_int2(id0, id1);
+      reinterpret_cast<float2*>(weights)[row] = make_float2(w0, w1);
+    } else {
+      ids[2 * row] = id0;
+      ids[2 * row + 1] = id1;
+      weights[2 * row] = w0;
+      weights[2 * row + 1] = w1;
+    }
   }
 }
 
@@ -171,7 +178,18 @@ cudaError_t launch_l(const float* logits, const float* bias, int32_t* ids, float
                      cudaStream_t stream) {
   constexpr int kThreads = 256;
   constexpr int kRowsPerBlock = (kThreads / 32) * (32 / L);
-  const int blocks = ceil_div(tokens, kRowsPerBlock);
+  // One resident wave (CTAs per SM from the occupancy of this instance).
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, topk_gate_kernel<L, kVec, kPer>,
+                                                      kThreads, 0) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = 1;
+    }
+    per_sm = n;
+  }
+  const int blocks = min(ceil_div(tokens, kRowsPerBlock), per_sm * sm_count());
   topk_gate_kernel<L, kVec, kPer><<<blocks, kThreads, 0, stream>>>(
       logits, bias, ids, weights, tokens, experts, pair, remap);
   note_launch();

@@ -156,7 +156,7 @@ def test_histogram_reset_kat(rrlib, cuda):
         assert host(counts).tolist() == [r // 2, r // 2]
 
 
-@pytest.mark.parametrize("experts", [1, 8, 64, 256, 1024])
+@pytest.mark.parametrize("experts", [1, 8, 33, 64, 256, 639, 640, 1024])
 @pytest.mark.parametrize("dist", ["uniform", "zipf", "one"])
 @pytest.mark.parametrize("routes", [1, 1000, 4099, 100_003, 1 << 18, 1 << 20])
 def test_histogram_scan_fused_exact(rrlib, oracle, cuda, experts, dist, routes):
