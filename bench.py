@@ -36,6 +36,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes
+import dataclasses
 import json
 
 import numpy as np
@@ -64,7 +65,12 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gather-rows", action="store_true",
-                    help="time the chain with the row-gathering grouped GEMM (no x_permuted)")
+                    help="time the chain with the row-gathering grouped GEMM (no x_permuted); "
+                         "implies --combine separate")
+    ap.add_argument("--combine", choices=["fused", "separate"], default="fused",
+                    help="fused: the unpermute runs in the grouped GEMM's epilogue "
+                         "(rr_grouped_gemm_combine, y bit-identical); separate: grouped_gemm "
+                         "then unpermute, as the reference's chain runs them")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the cold-L2 C5 pass and the C1/C2 eager-vs-graph latencies")
     ap.add_argument("--e2e-chunk", type=int, default=8192,
@@ -256,13 +262,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "expected_imbalance": round(pl.imbalance(), 4)}
     torch.cuda.synchronize()
 
-    stage_names = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
-                   "grouped_gemm", "unpermute"]
+    fused = args.combine == "fused" and not args.gather_rows
+    all_stages = ["dense_gemm", "topk_gate", "histogram_exclusive_scan", "token_permute",
+                  "grouped_gemm", "unpermute"]
+    # fused: the unpermute runs in the grouped GEMM's epilogue (y zeroed
+    # first, each output row weighted and added into its token's row).
+    stage_names = all_stages[:-1] if fused else all_stages
     # --gather-rows: the permute only ranks (route_pos, sorted_route) and the
     # grouped GEMM gathers its rows from X; x_permuted is never written.
     sorted_route = torch.empty(routes, dtype=torch.int32, device=device)
 
-    def step(events=None, only=None):
+    def step(events=None, only=None, fused=fused):
         """One chain step, stage by stage; `only` runs just that stage index."""
         calls = [
             lambda: rr.dense_gemm(inp.x, inp.router_w, buf.logits, tokens, e, k, ctx=ctx),
@@ -271,17 +281,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             lambda: rr.histogram_exclusive_scan(buf.expert_ids, buf.counts, buf.offsets, routes,
                                                 e, ctx=ctx),
             (lambda: rr.token_permute(inp.x, buf.expert_ids, buf.offsets, buf.x_permuted,
-                                      buf.route_pos, None, tokens, e, 2, k, buf.workspace,
-                                      ctx=ctx)) if not args.gather_rows else
+                                      buf.route_pos, sorted_route if fused else None, tokens, e,
+                                      2, k, buf.workspace, ctx=ctx)) if not args.gather_rows else
             (lambda: rr.token_permute(None, buf.expert_ids, buf.offsets, None, buf.route_pos,
                                       sorted_route, tokens, e, 2, 0, buf.workspace, ctx=ctx)),
+            (lambda: rr.grouped_gemm_combine(buf.x_permuted, inp.expert_w, buf.offsets,
+                                             sorted_route, buf.route_weights, buf.y, routes, 2,
+                                             ctx=ctx)) if fused else
             (lambda: rr.grouped_gemm(buf.x_permuted, inp.expert_w, buf.offsets, buf.y_permuted,
                                      e, k, n, routes, ctx=ctx)) if not args.gather_rows else
             (lambda: rr.grouped_gemm_gather(inp.x, sorted_route, 2, inp.expert_w, buf.offsets,
                                             buf.y_permuted, routes, ctx=ctx)),
             lambda: rr.unpermute(buf.y_permuted, buf.route_pos, buf.route_weights, buf.y, tokens,
                                  2, n, ctx=ctx),
-        ]
+        ][:len(all_stages) - (1 if fused else 0)]
         for i, call in enumerate(calls):
             if only is not None and i != only:
                 continue
@@ -347,6 +360,39 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         ep_info["rows_received_per_rank"] = per_rank
         ep_info["measured_imbalance"] = round(max(per_rank) / (sum(per_rank) / world), 4)
 
+    # The same step with the separate unpermute (the reference chain's
+    # order of launches), timed the same way, and its y against the fused
+    # step's bit for bit.
+    separate = None
+    if fused and world == 1 and not args.no_extras:
+        y_fused = buf.y.clone()
+        sev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)]
+               for _ in range(args.steps)]
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step(fused=False)
+        stream.synchronize()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a0.record(stream)
+            for i in range(args.steps):
+                step(sev[i], fused=False)
+            a1.record(stream)
+        a1.synchronize()
+        sep_ms = a0.elapsed_time(a1) / args.steps
+        separate = {
+            "ms_per_step": round(sep_ms, 4),
+            "tokens_per_s": round(tokens / (sep_ms * 1e-3), 1),
+            "grouped_gemm_ms": round(statistics.mean(sev[i][4].elapsed_time(sev[i][5])
+                                                     for i in range(args.steps)), 4),
+            "unpermute_ms": round(statistics.mean(sev[i][5].elapsed_time(sev[i][6])
+                                                  for i in range(args.steps)), 4),
+            "y_bit_identical_to_fused": bool(torch.equal(y_fused.view(torch.int32),
+                                                         buf.y.view(torch.int32))),
+        }
+        del y_fused
+
     # Max over ranks.
     t = torch.tensor([total_ms], device=device, dtype=torch.float64)
     if world > 1:
@@ -374,10 +420,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             from raggedroute_b200.ep import HostPipeline
             ep_host = HostPipeline(ep, ep_buf, tokens, device)
 
+        # The host chain runs the same kernels as the timed step (the fused
+        # combine through the chain's implementation bits).
+        host_ctx = dataclasses.replace(ctx, implementation_id=4 if fused else 0)
+
         def e2e_step():
             if ep is None:
                 host_chain(x_host, inp.router_w, inp.expert_w, y_host,
-                           logit_bias=inp.logit_bias, ctx=ctx)
+                           logit_bias=inp.logit_bias, ctx=host_ctx)
                 return
             ep_host(x_host, inp.router_w, local_w, y_host, logit_bias=inp.logit_bias,
                     expert_remap=remap, ctx=ctx)
@@ -430,6 +480,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if ep is not None:
         ep.close()
     extras = {}
+    if separate is not None:
+        extras["separate_unpermute"] = separate
     if world == 1 and not args.no_extras:
         cold = cold_scrub_step(torch, rr, stream, step, max(3, args.steps))
         cold["tokens_per_s"] = round(tokens / (cold["ms_per_step"] * 1e-3), 1)
@@ -459,6 +511,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if args.gather_rows:
         # ranks only: ids read, route_pos and sorted_route written
         stage_bytes["token_permute"] = 12.0 * routes + 4.0 * (e + 1)
+    if fused:
+        # permute also writes sorted_route; the GEMM writes y (not
+        # y_permuted) and reads each row's route and weight.
+        stage_bytes["token_permute"] += 4.0 * routes
+        stage_bytes["grouped_gemm"] = 4.0 * (routes * k + e * k * n + tokens * n) + 8.0 * routes
     if world == 1 and not args.no_extras:
         extras["configs"] = config_sweep(torch, rr, device, hbm, peak_3x)
         extras["prepared_weights"] = prepared_weights_pass(
@@ -499,6 +556,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "gpu_launches": int(launches),
         "e2e": e2e,
     }
+    line["path"] = ("operator calls through the C ABI on one stream: dense_gemm, "
+                    "topk_gate_biased, histogram_exclusive_scan, token_permute, " +
+                    ("grouped_gemm_combine (the unpermute fused into the grouped GEMM's epilogue; "
+                     "y bit-identical to grouped_gemm + unpermute)" if fused else
+                     "grouped_gemm, unpermute"))
     line.update(extras)
     if ep_info is not None:
         line["ep"] = ep_info

@@ -40,6 +40,13 @@ struct ChainFromTokensArgs {
   // expert_weights is a buffer filled by rr_prepare_expert_weights (new: no
   // reference counterpart), not W itself; K and N multiples of 4.
   bool prepared_weights = false;
+  // The unpermute runs inside the grouped GEMM's epilogue (new: no reference
+  // counterpart): each output row is weighted and added into its token's row
+  // of y, so buffers.y_permuted is not written and may be null. y is the
+  // same bit for bit (both paths round each product, then add with subnormal
+  // operands and results flushed to zero, and a sum of two terms does not
+  // depend on their order).
+  bool fused_combine = false;
 };
 
 struct ChainFromLogitsArgs {
@@ -53,6 +60,7 @@ struct ChainFromLogitsArgs {
   int output = 0;
   bool gather_rows = false;       // as in ChainFromTokensArgs
   bool prepared_weights = false;  // as in ChainFromTokensArgs
+  bool fused_combine = false;     // as in ChainFromTokensArgs
 };
 
 // Buffers of the post-route chain (top_k routes per token, R = T * top_k).
@@ -83,6 +91,10 @@ struct ChainFromRouteIdsArgs {
   // The grouped GEMM gathers its rows from x through buffers.sorted_route
   // (then required); buffers.x_permuted is not written and may be null.
   bool gather_rows = false;
+  // As in ChainFromTokensArgs, for top_k 1 or 2 (a larger top_k is
+  // kUnsupportedKernelVariant: the sum of three or more terms would depend on
+  // their order); buffers.sorted_route is then required.
+  bool fused_combine = false;
 };
 
 // Workspace (bytes) for either chain: the token_permute workspace at 2T

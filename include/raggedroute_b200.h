@@ -164,16 +164,26 @@ size_t rr_unpermute_workspace_size(int tokens, int top_k, int output);
 
 /* ---- L3 chains (benchmarks/adapters/chain_adapter.cpp:263-467) ----------- */
 
-/* Chains read ctx->implementation_id: 0 (default) materialises x_permuted;
+/* Chains read ctx->implementation_id as a set of bits; 0 (default) runs
+ * every stage as its own operator and leaves each intermediate buffer
+ * holding its stage's result.
  * RR_CHAIN_IMPL_GATHER_ROWS has the grouped GEMM gather its rows from x
  * through sorted_route (the permute only ranks), so x_permuted is not
  * written (may be NULL) and the permute's row copy and the GEMM's re-read
  * of it disappear; outputs are bit-identical. RR_CHAIN_IMPL_PREPARED_WEIGHTS
  * (token and logit chains) takes expert_weights as a buffer filled by
- * rr_prepare_expert_weights (below). Any other id is
- * RR_UNSUPPORTED_KERNEL_VARIANT. */
+ * rr_prepare_expert_weights (below). RR_CHAIN_IMPL_FUSED_COMBINE runs the
+ * unpermute inside the grouped GEMM's epilogue (every output row weighted
+ * and added into its token's row of y with a global float reduction; y is
+ * zeroed first), so y_permuted is not written (may be NULL) and the
+ * unpermute launch disappears; y is bit-identical (top_k <= 2 only: the
+ * route-id chain returns RR_UNSUPPORTED_KERNEL_VARIANT above 2 and then
+ * needs sorted_route). FUSED_COMBINE combines with either of the other two;
+ * GATHER_ROWS with PREPARED_WEIGHTS, and any other bit, is
+ * RR_UNSUPPORTED_KERNEL_VARIANT. None has a reference counterpart. */
 #define RR_CHAIN_IMPL_GATHER_ROWS 1u
 #define RR_CHAIN_IMPL_PREPARED_WEIGHTS 2u
+#define RR_CHAIN_IMPL_FUSED_COMBINE 4u
 
 /* ---- prepared expert weights (new: no reference counterpart) -------------
  * For expert weights that stay fixed across calls (inference), the B side
@@ -219,6 +229,36 @@ rr_status rr_grouped_gemm_gather(const float* x, const int32_t* sorted_route, in
                                  const float* expert_weights, const int32_t* offsets,
                                  float* y_permuted, int route_pairs, int hidden, int experts,
                                  int output, const rr_context* ctx);
+
+/* Grouped GEMM with the unpermute fused into its epilogue (new: no
+ * reference counterpart; the fused form of raggedroute::grouped_gemm followed
+ * by raggedroute::unpermute, src/grouped_gemm/operator.cpp and
+ * src/unpermute/operator.cpp). y [tokens, N] is zeroed, then row r of segment
+ * e (route q = sorted_route[r]) adds route_weights[q] * (x_permuted[r] .
+ * W[e]) into y[q / top_k]. sorted_route is the stable permute's [R] route
+ * order, route_weights the gate's [R] weights; R = route_pairs <= tokens *
+ * top_k. top_k 1 or 2: y then equals rr_grouped_gemm followed by
+ * rr_unpermute bit for bit (both round each product, then add with
+ * subnormal operands and results flushed to zero; two terms in either order
+ * give the same sum). */
+rr_status rr_grouped_gemm_combine(const float* x_permuted, const float* expert_weights,
+                                  const int32_t* offsets, const int32_t* sorted_route,
+                                  const float* route_weights, float* y, int experts, int hidden,
+                                  int output, int route_pairs, int tokens, int top_k,
+                                  const rr_context* ctx);
+
+/* Grouped GEMM with a row-address epilogue (new: the expert-parallel combine
+ * step). Output row r of segment e is stored at bases[b] + row * N where
+ * row_address[r] = (b << 40) | row; rows whose address is negative, whose b
+ * is not below nbases or whose row is not below row_limit are not stored.
+ * bases is a DEVICE array of nbases row-buffer pointers (this process's
+ * mappings of other GPUs' buffers included). The kernel ends with a
+ * system-scope fence so a following barrier publishes the rows. */
+rr_status rr_grouped_gemm_scatter(const float* x_permuted, const float* expert_weights,
+                                  const int32_t* offsets, const int64_t* row_address,
+                                  float* const* bases, int nbases, int64_t row_limit,
+                                  int experts, int hidden, int output, int route_pairs,
+                                  const rr_context* ctx);
 
 rr_status rr_chain_from_logits(const float* logits, const float* x, const float* expert_weights,
                                int32_t* expert_ids, float* route_weights, int32_t* counts,

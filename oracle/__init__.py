@@ -222,6 +222,34 @@ def unpermute_f64(yp, route_pos, route_weights, top_k: int = 2):
     return y
 
 
+def _ftz(v: np.ndarray) -> np.ndarray:
+    """float32 values below 2^-126 in magnitude replaced by a zero of the
+    same sign."""
+    tiny = np.abs(v) < np.float32(2.0 ** -126)
+    return np.where(tiny, np.copysign(np.float32(0.0), v), v).astype(np.float32)
+
+
+def unpermute_f32_ftz(yp, route_pos, route_weights, top_k: int = 2) -> np.ndarray:
+    """The library's unpermute arithmetic in float32, bit for bit: from 0.0f,
+    in rank order, acc = ftz(ftz(acc) + ftz(rn(w * v))) -- the rounded
+    product added with round-to-nearest and subnormal operands and result
+    flushed to zero (what a global float reduction does on the GPU, so the
+    grouped GEMM's fused combine gives the same sum). The reference's own
+    unpermute (src/unpermute/cuda_naive/baseline.cu:13-30) sums the same
+    terms in the same order with fused multiply-adds; unpermute_f64 is its
+    exact value."""
+    yp = _f32(yp)
+    route_pos = _i32(route_pos).reshape(-1)
+    w = _f32(route_weights).reshape(-1)
+    tokens = route_pos.size // top_k
+    acc = np.zeros((tokens, yp.shape[1]), np.float32)
+    for k in range(top_k):
+        pos = route_pos[k::top_k]
+        prod = _ftz((w[k::top_k][:, None] * yp[pos]).astype(np.float32))
+        acc = _ftz((_ftz(acc) + prod).astype(np.float32))
+    return acc
+
+
 def chain_logits_f32(x, router_w):
     x = _f32(x)
     router_w = _f32(router_w)

@@ -40,6 +40,8 @@ from raggedroute_b200.ops import (  # noqa: F401
     token_permute_workspace_size,
     grouped_gemm,
     grouped_gemm_gather,
+    grouped_gemm_combine,
+    grouped_gemm_scatter,
     grouped_gemm_prepared,
     PreparedExpertWeights,
     unpermute,

@@ -98,6 +98,8 @@ SIGNATURES = {
     "rr_unpermute_workspace_size": (ctypes.c_size_t, [_I, _I, _I]),
     "rr_chain_from_tokens": (RRStatus, [_P] * 13 + [_I] * 4 + [_CTX]),
     "rr_grouped_gemm_gather": (RRStatus, [_P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _CTX]),
+    "rr_grouped_gemm_combine": (RRStatus, [_P] * 6 + [_I] * 6 + [_CTX]),
+    "rr_grouped_gemm_scatter": (RRStatus, [_P] * 5 + [_I, ctypes.c_int64] + [_I] * 4 + [_CTX]),
     "rr_prepared_expert_weights_size": (ctypes.c_size_t, [_I, _I, _I]),
     "rr_prepare_expert_weights": (RRStatus, [_P, _I, _I, _I, _P, ctypes.c_size_t, _CTX]),
     "rr_grouped_gemm_prepared": (RRStatus, [_P, _P, _P, _P, _I, _I, _I, _I, _CTX]),

@@ -622,7 +622,7 @@ Status validate_chain_shape(int tokens, int hidden, int experts, int output) noe
 Status chain_after_logits(const float* logits, const float* logit_bias, const float* x,
                           const float* expert_w, const ChainBuffers& b, int tokens, int hidden,
                           int experts, int output, const RuntimeContext& context,
-                          bool gather_rows, bool prepared_weights) noexcept {
+                          bool gather_rows, bool prepared_weights, bool fused_combine) noexcept {
   cudaStream_t stream = context.stream;
   Status s = success_status();
   {
@@ -641,6 +641,36 @@ Status chain_after_logits(const float* logits, const float* logit_bias, const fl
                             "chain histogram_exclusive_scan launch failed");
   }
   if (!s.ok()) return s;
+  if (fused_combine) {
+    // The permute also records each permuted row's route (in the
+    // workspace); the grouped GEMM adds every weighted output row into its
+    // token's row of y, so neither y_permuted nor the unpermute launch exist.
+    int32_t* sorted_route = reinterpret_cast<int32_t*>(
+        static_cast<char*>(context.workspace) + chain_sorted_route_offset(tokens, experts));
+    {
+      StageRange r("raggedroute_token_permute");
+      s = detail::cuda_status(
+          rrb::launch_token_permute(x, b.expert_ids, b.offsets, gather_rows ? nullptr : b.x_permuted,
+                                    b.route_pos, sorted_route, tokens, experts, 2,
+                                    gather_rows ? 0 : hidden, context.workspace, stream),
+          "chain token_permute launch failed");
+    }
+    if (!s.ok()) return s;
+    const rrb::RowGather gather{x, sorted_route, 2};
+    const float* lo =
+        prepared_weights
+            ? reinterpret_cast<const float*>(
+                  reinterpret_cast<const char*>(expert_w) +
+                  rrb::prepared_weights_half_bytes(experts, hidden, output))
+            : nullptr;
+    StageRange r("raggedroute_grouped_gemm");
+    return detail::cuda_status(
+        rrb::launch_grouped_gemm_combine(gather_rows ? x : b.x_permuted, expert_w, lo, b.offsets,
+                                         sorted_route, b.route_weights, b.y, experts, routes,
+                                         tokens, 2, hidden, output, stream,
+                                         gather_rows ? &gather : nullptr),
+        "chain grouped_gemm (fused combine) launch failed");
+  }
   if (gather_rows) {
     // Ranks only (no row copy); the grouped GEMM gathers its rows from x
     // through sorted_route, kept in the workspace.
@@ -696,10 +726,11 @@ Status chain_after_logits(const float* logits, const float* logit_bias, const fl
 }
 
 Status validate_chain_buffers(const ChainBuffers& b, bool need_logits, int hidden,
-                              int output, bool gather_rows) noexcept {
+                              int output, bool gather_rows, bool fused_combine) noexcept {
   if ((need_logits && b.logits == nullptr) || b.expert_ids == nullptr ||
       b.route_weights == nullptr || b.counts == nullptr || b.offsets == nullptr ||
-      b.route_pos == nullptr || (output > 0 && (b.y == nullptr || b.y_permuted == nullptr)) ||
+      b.route_pos == nullptr ||
+      (output > 0 && (b.y == nullptr || (!fused_combine && b.y_permuted == nullptr))) ||
       (hidden > 0 && !gather_rows && b.x_permuted == nullptr)) {
     return detail::invalid_argument("chain received a null device buffer");
   }
@@ -708,18 +739,22 @@ Status validate_chain_buffers(const ChainBuffers& b, bool need_logits, int hidde
 
 // Prepared expert weights: the tcgen05 engine only (no FP32 fallback reads
 // that layout), so the shapes and buffers TMA needs are required up front.
-Status validate_prepared(bool prepared, bool gather_rows, const void* weights,
-                         const ChainBuffers& b, int hidden, int output) noexcept {
+Status validate_prepared(bool prepared, bool gather_rows, bool fused_combine,
+                         const void* weights, const ChainBuffers& b, int hidden,
+                         int output) noexcept {
   if (!prepared) return success_status();
   if (gather_rows) {
     return detail::make_status(StatusCode::kUnsupportedKernelVariant,
                                "prepared expert weights do not combine with row gathering");
   }
+  // The prepared engine stores into y_permuted, or adds into y when the
+  // combine is fused.
+  const float* out = fused_combine ? b.y : b.y_permuted;
   if (hidden % 4 != 0 || output % 4 != 0 || !rrb::aligned_to(weights, 256) ||
-      !rrb::aligned_to(b.x_permuted, 16) || !rrb::aligned_to(b.y_permuted, 16)) {
+      !rrb::aligned_to(b.x_permuted, 16) || !rrb::aligned_to(out, 16)) {
     return detail::invalid_argument(
         "prepared expert weights need K and N multiples of 4, a 256-byte aligned prepared "
-        "buffer and 16-byte aligned x_permuted / y_permuted");
+        "buffer and 16-byte aligned x_permuted / y_permuted (y with a fused combine)");
   }
   return success_status();
 }
@@ -756,10 +791,11 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
   if (args.expert_weights == nullptr && args.hidden > 0 && args.output > 0) {
     return detail::invalid_argument("chain expert weights are null");
   }
-  s = validate_chain_buffers(args.buffers, true, args.hidden, args.output, args.gather_rows);
+  s = validate_chain_buffers(args.buffers, true, args.hidden, args.output, args.gather_rows,
+                             args.fused_combine);
   if (!s.ok()) return s;
-  s = validate_prepared(args.prepared_weights, args.gather_rows, args.expert_weights,
-                        args.buffers, args.hidden, args.output);
+  s = validate_prepared(args.prepared_weights, args.gather_rows, args.fused_combine,
+                        args.expert_weights, args.buffers, args.hidden, args.output);
   if (!s.ok()) return s;
   const std::size_t need = get_chain_workspace_size(args.tokens, args.hidden, args.experts,
                                                     args.output);
@@ -777,7 +813,8 @@ Status chain_from_tokens(const ChainFromTokensArgs& args, const RuntimeContext& 
   if (!s.ok()) return s;
   return chain_after_logits(args.buffers.logits, args.logit_bias, args.x, args.expert_weights,
                             args.buffers, args.tokens, args.hidden, args.experts, args.output,
-                            context, args.gather_rows, args.prepared_weights);
+                            context, args.gather_rows, args.prepared_weights,
+                            args.fused_combine);
 }
 
 Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& context) noexcept {
@@ -791,10 +828,11 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
   if (args.expert_weights == nullptr && args.hidden > 0 && args.output > 0) {
     return detail::invalid_argument("chain expert weights are null");
   }
-  s = validate_chain_buffers(args.buffers, false, args.hidden, args.output, args.gather_rows);
+  s = validate_chain_buffers(args.buffers, false, args.hidden, args.output, args.gather_rows,
+                             args.fused_combine);
   if (!s.ok()) return s;
-  s = validate_prepared(args.prepared_weights, args.gather_rows, args.expert_weights,
-                        args.buffers, args.hidden, args.output);
+  s = validate_prepared(args.prepared_weights, args.gather_rows, args.fused_combine,
+                        args.expert_weights, args.buffers, args.hidden, args.output);
   if (!s.ok()) return s;
   const std::size_t need = get_chain_workspace_size(args.tokens, args.hidden, args.experts,
                                                     args.output);
@@ -804,7 +842,7 @@ Status chain_from_logits(const ChainFromLogitsArgs& args, const RuntimeContext& 
   }
   return chain_after_logits(args.logits, nullptr, args.x, args.expert_weights, args.buffers,
                             args.tokens, args.hidden, args.experts, args.output, context,
-                            args.gather_rows, args.prepared_weights);
+                            args.gather_rows, args.prepared_weights, args.fused_combine);
 }
 
 std::size_t get_route_chain_workspace_size(int tokens, int top_k, int experts) noexcept {
@@ -821,6 +859,10 @@ Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
                             const RuntimeContext& context) noexcept {
   if (args.top_k < 1 || args.top_k > 8 || args.top_k > args.experts) {
     return detail::invalid_argument("chain_from_route_ids requires 1<=top_k<=min(8,E)");
+  }
+  if (args.fused_combine && args.top_k > 2) {
+    return detail::make_status(StatusCode::kUnsupportedKernelVariant,
+                               "a fused combine needs top_k <= 2");
   }
   if (args.tokens < 0 || args.hidden < 0 || args.output < 0 || args.experts < 2 ||
       args.experts > kMaxExperts) {
@@ -843,7 +885,9 @@ Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
         (args.hidden > 0 &&
          (args.x == nullptr || (!args.gather_rows && b.x_permuted == nullptr) ||
           (args.gather_rows && b.sorted_route == nullptr))) ||
-        (args.output > 0 && (b.y == nullptr || b.y_permuted == nullptr)) ||
+        (args.output > 0 &&
+         (b.y == nullptr || (!args.fused_combine && b.y_permuted == nullptr) ||
+          (args.fused_combine && b.sorted_route == nullptr))) ||
         (args.hidden > 0 && args.output > 0 && args.expert_weights == nullptr)) {
       return detail::invalid_argument("chain received a null device buffer");
     }
@@ -866,6 +910,16 @@ Status chain_from_route_ids(const ChainFromRouteIdsArgs& args,
                                 args.top_k, gather ? 0 : args.hidden, context.workspace, stream),
       "chain token_permute launch failed");
   if (!s.ok() || args.output == 0) return s;
+  if (args.fused_combine) {
+    const rrb::RowGather g{args.x, b.sorted_route, args.top_k};
+    return detail::cuda_status(
+        rrb::launch_grouped_gemm_combine(gather ? args.x : b.x_permuted, args.expert_weights,
+                                         nullptr, b.offsets, b.sorted_route, args.route_weights,
+                                         b.y, args.experts, r, args.tokens, args.top_k,
+                                         args.hidden, args.output, stream,
+                                         gather ? &g : nullptr),
+        "chain grouped_gemm (fused combine) launch failed");
+  }
   if (gather) {
     const rrb::RowGather g{args.x, b.sorted_route, args.top_k};
     s = detail::cuda_status(rrb::launch_grouped_gemm(args.x, args.expert_weights, b.offsets,
@@ -1209,6 +1263,76 @@ rr_status rr_grouped_gemm_gather(const float* x, const int32_t* sorted_route, in
   return to_c(raggedroute::success_status());
 }
 
+rr_status rr_grouped_gemm_combine(const float* x_permuted, const float* expert_weights,
+                                  const int32_t* offsets, const int32_t* sorted_route,
+                                  const float* route_weights, float* y, int experts, int hidden,
+                                  int output, int route_pairs, int tokens, int top_k,
+                                  const rr_context* ctx) {
+  if (ctx == nullptr) return null_context();
+  if (experts <= 0 || experts > rrb::kMaxExperts || hidden < 0 || output < 0 ||
+      route_pairs < 0 || tokens < 0 || top_k < 1 ||
+      static_cast<long long>(tokens) * top_k < route_pairs) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "grouped_gemm_combine requires 1<=E<=1024, K, N, R, T >= 0 and R <= T*top_k"});
+  }
+  if (top_k > 2) {
+    return to_c({raggedroute::StatusCode::kUnsupportedKernelVariant, cudaSuccess,
+                 "a fused combine needs top_k <= 2"});
+  }
+  if (tokens == 0 || output == 0) return to_c(raggedroute::success_status());
+  if (y == nullptr || (route_pairs > 0 && (offsets == nullptr || sorted_route == nullptr ||
+                                           route_weights == nullptr ||
+                                           (hidden > 0 && (x_permuted == nullptr ||
+                                                           expert_weights == nullptr))))) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "grouped_gemm_combine received a null device buffer"});
+  }
+  const raggedroute::Status a = raggedroute::detail_resolve_sm100(to_runtime(ctx));
+  if (!a.ok()) return to_c(a);
+  const cudaError_t e = rrb::launch_grouped_gemm_combine(
+      x_permuted, expert_weights, nullptr, offsets, sorted_route, route_weights, y, experts,
+      route_pairs, tokens, top_k, hidden, output, as_stream(ctx->stream));
+  if (e != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, e, "grouped_gemm_combine launch failed"});
+  }
+  return to_c(raggedroute::success_status());
+}
+
+rr_status rr_grouped_gemm_scatter(const float* x_permuted, const float* expert_weights,
+                                  const int32_t* offsets, const int64_t* row_address,
+                                  float* const* bases, int nbases, int64_t row_limit,
+                                  int experts, int hidden, int output, int route_pairs,
+                                  const rr_context* ctx) {
+  if (ctx == nullptr) return null_context();
+  if (experts <= 0 || experts > rrb::kMaxExperts || hidden < 0 || output < 0 ||
+      route_pairs < 0 || nbases < 0 || row_limit < 0) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "grouped_gemm_scatter requires 1<=E<=1024 and K, N, R, nbases, row_limit >= 0"});
+  }
+  if (route_pairs == 0 || output == 0) return to_c(raggedroute::success_status());
+  if (offsets == nullptr || row_address == nullptr || (nbases > 0 && bases == nullptr) ||
+      (hidden > 0 && (x_permuted == nullptr || expert_weights == nullptr))) {
+    return to_c({raggedroute::StatusCode::kInvalidArgument, cudaSuccess,
+                 "grouped_gemm_scatter received a null device buffer"});
+  }
+  const raggedroute::Status a = raggedroute::detail_resolve_sm100(to_runtime(ctx));
+  if (!a.ok()) return to_c(a);
+  rrb::RowScatter sc;
+  sc.dst = row_address;
+  sc.base = bases;
+  sc.nranks = nbases;
+  sc.row_limit = row_limit;
+  // y is only the engine's alignment witness here: every stored row goes to
+  // a resolved address.
+  const cudaError_t e = rrb::launch_grouped_gemm(x_permuted, expert_weights, offsets, nullptr,
+                                                 experts, route_pairs, hidden, output,
+                                                 as_stream(ctx->stream), 0, &sc);
+  if (e != cudaSuccess) {
+    return to_c({raggedroute::StatusCode::kCudaError, e, "grouped_gemm_scatter launch failed"});
+  }
+  return to_c(raggedroute::success_status());
+}
+
 rr_status rr_unpermute(const float* y_permuted, const int32_t* route_pos,
                        const float* route_weights, float* y, int tokens, int top_k, int output,
                        const rr_context* ctx) {
@@ -1226,18 +1350,24 @@ rr_status rr_unpermute(const float* y_permuted, const int32_t* route_pos,
 }
 size_t rr_unpermute_workspace_size(int, int, int) { return 0; }
 
-// Chains read ctx->implementation_id: 0 materialises x_permuted,
-// RR_CHAIN_IMPL_GATHER_ROWS gathers the grouped GEMM's rows from x,
-// RR_CHAIN_IMPL_PREPARED_WEIGHTS (token and logit chains) takes
-// expert_weights as a buffer from rr_prepare_expert_weights.
-rr_status chain_impl(const rr_context* ctx, bool* gather_rows, bool* prepared = nullptr) {
-  *gather_rows = ctx->implementation_id == RR_CHAIN_IMPL_GATHER_ROWS;
-  const bool prep = ctx->implementation_id == RR_CHAIN_IMPL_PREPARED_WEIGHTS;
-  if (prepared != nullptr) *prepared = prep;
-  if (ctx->implementation_id != 0 && !*gather_rows && !(prep && prepared != nullptr)) {
+// Chains read ctx->implementation_id as bits: RR_CHAIN_IMPL_GATHER_ROWS
+// gathers the grouped GEMM's rows from x, RR_CHAIN_IMPL_PREPARED_WEIGHTS
+// (token and logit chains, where `prepared` is given) takes expert_weights
+// as a buffer from rr_prepare_expert_weights, RR_CHAIN_IMPL_FUSED_COMBINE
+// fuses the unpermute into the grouped GEMM. Unknown bits are rejected here;
+// gather with prepared weights by the chain's own validation.
+rr_status chain_impl(const rr_context* ctx, bool* gather_rows, bool* fused_combine,
+                     bool* prepared = nullptr) {
+  const uint32_t id = ctx->implementation_id;
+  const uint32_t known = RR_CHAIN_IMPL_GATHER_ROWS | RR_CHAIN_IMPL_FUSED_COMBINE |
+                         (prepared != nullptr ? RR_CHAIN_IMPL_PREPARED_WEIGHTS : 0u);
+  if ((id & ~known) != 0) {
     return to_c({raggedroute::StatusCode::kUnsupportedKernelVariant, cudaSuccess,
                  "unknown chain implementation id"});
   }
+  *gather_rows = (id & RR_CHAIN_IMPL_GATHER_ROWS) != 0;
+  *fused_combine = (id & RR_CHAIN_IMPL_FUSED_COMBINE) != 0;
+  if (prepared != nullptr) *prepared = (id & RR_CHAIN_IMPL_PREPARED_WEIGHTS) != 0;
   return to_c(raggedroute::success_status());
 }
 
@@ -1329,7 +1459,8 @@ rr_status rr_chain_from_tokens(const float* x, const float* router_weights,
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
-  const rr_status impl = chain_impl(ctx, &args.gather_rows, &args.prepared_weights);
+  const rr_status impl =
+      chain_impl(ctx, &args.gather_rows, &args.fused_combine, &args.prepared_weights);
   if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_tokens(args, to_runtime(ctx)));
 }
@@ -1352,7 +1483,7 @@ rr_status rr_chain_from_route_ids(const float* x, const int32_t* expert_ids,
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
-  const rr_status impl = chain_impl(ctx, &args.gather_rows);
+  const rr_status impl = chain_impl(ctx, &args.gather_rows, &args.fused_combine);
   if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_route_ids(args, to_runtime(ctx)));
 }
@@ -1377,7 +1508,8 @@ rr_status rr_chain_from_logits(const float* logits, const float* x, const float*
   args.hidden = hidden;
   args.experts = experts;
   args.output = output;
-  const rr_status impl = chain_impl(ctx, &args.gather_rows, &args.prepared_weights);
+  const rr_status impl =
+      chain_impl(ctx, &args.gather_rows, &args.fused_combine, &args.prepared_weights);
   if (impl.code != RR_SUCCESS) return impl;
   return to_c(raggedroute::chain_from_logits(args, to_runtime(ctx)));
 }

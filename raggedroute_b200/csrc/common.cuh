@@ -31,6 +31,16 @@ constexpr long long kPeerRowMask = (1LL << kPeerRankShift) - 1;
 // array of one pointer per rank (this process's mapping of every rank's
 // buffer, its own included). An address whose rank is not below nranks or
 // whose row is not below row_limit is not stored.
+//
+// Combine mode (combine != nullptr, dst == nullptr): the unpermute fused
+// into the epilogue. Output row r belongs to route q = route[r] (the stable
+// permute's sorted_route); it is multiplied by weight[q] (rounded product)
+// and added with one global float reduction into row q / top_k of combine,
+// which must hold zeros before the launch. The reduction adds with
+// round-to-nearest and flushes subnormal operands and results to zero
+// (measured on sm_100); for top_k <= 2 the result,
+// ftz(ftz(0 + a) + b) = ftz(a + b), does not depend on which of a token's
+// two rows lands first, and equals launch_unpermute's rank-order sum.
 struct RowScatter {
   const int64_t* dst = nullptr;
   float* const* base = nullptr;
@@ -39,6 +49,10 @@ struct RowScatter {
   // Abort fence (optional, host memory mapped into the device): read once at
   // kernel start; when non-zero no row is stored.
   const volatile int* abort = nullptr;
+  float* combine = nullptr;
+  const int32_t* route = nullptr;
+  const float* weight = nullptr;
+  int top_k = 1;
 };
 
 // Resolves a packed row address, or nullptr when it is out of range.
@@ -48,6 +62,34 @@ __device__ __forceinline__ float* scatter_row(const RowScatter& sc, long long ro
   const long long r = d & kPeerRowMask;
   if (d < 0 || rank >= sc.nranks || r >= sc.row_limit) return nullptr;
   return sc.base[rank] + r * output;
+}
+
+// Combine mode: the token row that output row `row` adds into, and its
+// route weight.
+__device__ __forceinline__ float* combine_row(const RowScatter& sc, long long row, int output,
+                                              float& weight) {
+  const int q = __ldg(sc.route + row);
+  weight = __ldg(sc.weight + q);
+  return sc.combine + static_cast<long long>(q / sc.top_k) * output;
+}
+
+// Global float reductions (no return value): round to nearest, subnormal
+// operands and results flushed to zero.
+__device__ __forceinline__ void red_add_f32(float* p, float a) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
+}
+__device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+// acc + v rounded to nearest with subnormal operands and result flushed to
+// zero: the arithmetic of red_add_f32, for sums that must equal it.
+__device__ __forceinline__ float add_ftz(float acc, float v) {
+  float r;
+  asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(acc), "f"(v));
+  return r;
 }
 
 // Row gather for a GEMM's A operand: row r of the problem is row
@@ -168,8 +210,9 @@ cudaError_t launch_unpermute(const float* y_permuted, const int32_t* route_pos,
 // output]; weight_sets = 0 means one weight set per group. The
 // expert-parallel runtime uses weight_sets < experts for its
 // (source rank, local expert) groups. scatter (optional) redirects every
-// stored output row (peer transport combine); y is then only an alignment
-// witness for the engine choice. gather (optional, gather->x == x) reads A
+// stored output row (peer transport combine) or, in combine mode, adds it
+// weighted into its token's row; y is then only an alignment witness for the
+// engine choice. gather (optional, gather->x == x) reads A
 // row r from x[route[r] / div] instead of x[r].
 cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* offsets,
                                 float* y, int experts, int rows, int hidden, int output,
@@ -198,9 +241,24 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
 // Grouped GEMM on prepared expert weights (w_hi, w_lo: K-major [E][N][K],
 // hi = W, lo = W - trunc_tf32(W); prepare.cu). K and N multiples of 4, all
 // buffers 16-byte aligned, else cudaErrorInvalidValue; no SIMT fallback.
+// scatter as for launch_grouped_gemm.
 cudaError_t launch_grouped_gemm_prepared(const float* x, const float* w_hi, const float* w_lo,
                                          const int32_t* offsets, float* y, int experts, int rows,
-                                         int hidden, int output, cudaStream_t stream);
+                                         int hidden, int output, cudaStream_t stream,
+                                         const RowScatter* scatter = nullptr);
+
+// The unpermute fused into the grouped GEMM (combine mode of RowScatter):
+// zeroes y[tokens, output], then runs the grouped GEMM of x (or of the rows
+// gather names) against w with every output row weighted and added into its
+// token's row of y. top_k is 1 or 2 (where the sum does not depend on the
+// order in which a token's rows land); sorted_route and route_weights are
+// the stable permute's [R] route order and the gate's [R] weights.
+// prepared_lo != nullptr: w is the hi half of prepared weights.
+cudaError_t launch_grouped_gemm_combine(const float* x, const float* w, const float* prepared_lo,
+                                        const int32_t* offsets, const int32_t* sorted_route,
+                                        const float* route_weights, float* y, int experts,
+                                        int rows, int tokens, int top_k, int hidden, int output,
+                                        cudaStream_t stream, const RowGather* gather = nullptr);
 
 // prepare.cu: bytes of one half (hi or lo) of a prepared weight buffer,
 // 256-byte aligned; the buffer is hi | lo.

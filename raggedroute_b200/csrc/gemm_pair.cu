@@ -323,11 +323,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
         const int row = pg.base + static_cast<int>(rank) * kRows + quarter * 32 + lane;
         bool store_row = pending_last && row >= pg.row0 && row < pg.row_end;
         float* out = y + static_cast<long long>(row) * output + pg.col0 + c_begin;
+        float wgt = 0.0f;
         if (scatter.dst != nullptr && store_row) {
           float* dst_row = s.no_scatter ? nullptr : scatter_row(scatter, row, output);
           store_row = dst_row != nullptr;
           out = dst_row + pg.col0 + c_begin;
+        } else if (scatter.combine != nullptr && store_row) {
+          out = combine_row(scatter, row, output, wgt) + pg.col0 + c_begin;
         }
+        // 128-bit stores where the row start allows them (caller-owned
+        // scatter bases and combine targets need not be 16-byte aligned).
+        const bool vrow = vec && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
         const int w = pg.ncols - c_begin;  // columns of this group to store
 #pragma unroll
         for (int c = 0; c < kEpiCols; c += 16) {
@@ -348,8 +354,25 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
           }
           if (!pending_last) {
             tmem_st_32x32b_x16(tmem + kColS + col + lane_addr, p);
+          } else if (store_row && scatter.combine != nullptr) {
+            if (vrow) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                if (c + j < w) {
+                  red_add_v4_f32(out + c + j, __fmul_rn(wgt, __uint_as_float(p[j])),
+                                 __fmul_rn(wgt, __uint_as_float(p[j + 1])),
+                                 __fmul_rn(wgt, __uint_as_float(p[j + 2])),
+                                 __fmul_rn(wgt, __uint_as_float(p[j + 3])));
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (c + j < w) red_add_f32(out + c + j, __fmul_rn(wgt, __uint_as_float(p[j])));
+              }
+            }
           } else if (store_row) {
-            if (vec) {
+            if (vrow) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
                 if (c + j < w) {

@@ -83,6 +83,16 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_simt_kernel(
         out = scatter_row(scatter, r, output);
         if (out == nullptr) continue;
       }
+      if (scatter.combine != nullptr) {
+        float wgt;
+        out = combine_row(scatter, r, output, wgt);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = tc.col0 + tx * 4 + j;
+          if (c < output) red_add_f32(out + c, __fmul_rn(wgt, acc[i][j]));
+        }
+        continue;
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = tc.col0 + tx * 4 + j;

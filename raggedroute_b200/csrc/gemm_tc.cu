@@ -38,7 +38,9 @@
 // instantiations, so the default kernel carries none of them: row gather
 // (kGather, A rows fetched from x through a row map by the producer warp
 // with cp.async) and, at run time, an output-row scatter to other ranks'
-// memory (expert-parallel combine, skipped once the abort fence is set).
+// memory (expert-parallel combine, skipped once the abort fence is set) or
+// the unpermute fused into the epilogue (each row weighted and added into
+// its token's row with global float reductions; RowScatter combine mode).
 // Warps are specialised:
 //   warp 0     TMA producer: A (x rows, K-major, 64-byte swizzle) and B (the
 //              expert's [K, N] weights, N-major, unswizzled) per 16-wide
@@ -504,11 +506,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         const int row = pg.base + sub * kBM + quarter * 32 + lane;
         bool store_row = pending_last && row >= pg.row0 && row < pg.row_end;
         float* out = y + static_cast<long long>(row) * output + pg.col0 + lc0;
+        float wgt = 0.0f;
         if (scatter.dst != nullptr && store_row) {
           float* dst_row = s.no_scatter ? nullptr : scatter_row(scatter, row, output);
           store_row = dst_row != nullptr;
           out = dst_row + pg.col0 + lc0;
+        } else if (scatter.combine != nullptr && store_row) {
+          out = combine_row(scatter, row, output, wgt) + pg.col0 + lc0;
         }
+        // 128-bit stores where the row start allows them (caller-owned
+        // scatter bases and combine targets need not be 16-byte aligned).
+        const bool vrow = vec && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
         const int w = pg.ncols - lc0;  // columns of this group to store
 #pragma unroll
         for (int c = 0; c < kEpiCols; c += 16) {
@@ -529,8 +537,25 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
           }
           if (!pending_last) {
             tmem_st_32x32b_x16(tmem + kColS + col + lane_addr, p);
+          } else if (store_row && scatter.combine != nullptr) {
+            if (vrow) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                if (c + j < w) {
+                  red_add_v4_f32(out + c + j, __fmul_rn(wgt, __uint_as_float(p[j])),
+                                 __fmul_rn(wgt, __uint_as_float(p[j + 1])),
+                                 __fmul_rn(wgt, __uint_as_float(p[j + 2])),
+                                 __fmul_rn(wgt, __uint_as_float(p[j + 3])));
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (c + j < w) red_add_f32(out + c + j, __fmul_rn(wgt, __uint_as_float(p[j])));
+              }
+            }
           } else if (store_row) {
-            if (vec) {
+            if (vrow) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
                 if (c + j < w) {
@@ -729,7 +754,8 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
 
 cudaError_t launch_grouped_gemm_prepared(const float* x, const float* w_hi, const float* w_lo,
                                          const int32_t* offsets, float* y, int experts, int rows,
-                                         int hidden, int output, cudaStream_t stream) {
+                                         int hidden, int output, cudaStream_t stream,
+                                         const RowScatter* scatter) {
   if (hidden <= 0 || output <= 0 || hidden % 4 != 0 || output % 4 != 0 ||
       !aligned_to(x, 16) || !aligned_to(w_hi, 16) || !aligned_to(w_lo, 16) ||
       !aligned_to(y, 16)) {
@@ -778,7 +804,7 @@ cudaError_t launch_grouped_gemm_prepared(const float* x, const float* w_hi, cons
   }
   grouped_gemm_tc_kernel<false, 1, true><<<grid, kThreads, kSmemBytes, stream>>>(
       ma, mh, ml, offsets, y, experts, rows, hidden, output, experts, device_error_word(),
-      RowScatter{}, RowGather{});
+      scatter != nullptr ? *scatter : RowScatter{}, RowGather{});
   note_launch();
   return cudaGetLastError();
 }
@@ -796,6 +822,32 @@ cudaError_t launch_grouped_gemm(const float* x, const float* w, const int32_t* o
   }
   return launch_grouped_gemm_simt(x, w, offsets, y, experts, rows, hidden, output, stream,
                                   weight_sets, scatter, gather);
+}
+
+cudaError_t launch_grouped_gemm_combine(const float* x, const float* w, const float* prepared_lo,
+                                        const int32_t* offsets, const int32_t* sorted_route,
+                                        const float* route_weights, float* y, int experts,
+                                        int rows, int tokens, int top_k, int hidden, int output,
+                                        cudaStream_t stream, const RowGather* gather) {
+  if (top_k < 1 || top_k > 2 || tokens < 0 || output < 0 || rows < 0 ||
+      static_cast<long long>(tokens) * top_k < rows) {
+    return cudaErrorInvalidValue;
+  }
+  if (tokens == 0 || output == 0) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(y, 0, static_cast<std::size_t>(tokens) * output * sizeof(float),
+                                  stream);
+  if (e != cudaSuccess || rows == 0) return e;
+  RowScatter sc;
+  sc.combine = y;
+  sc.route = sorted_route;
+  sc.weight = route_weights;
+  sc.top_k = top_k;
+  if (prepared_lo != nullptr) {
+    return launch_grouped_gemm_prepared(x, w, prepared_lo, offsets, y, experts, rows, hidden,
+                                        output, stream, &sc);
+  }
+  return launch_grouped_gemm(x, w, offsets, y, experts, rows, hidden, output, stream, 0, &sc,
+                             gather);
 }
 
 }  // namespace rrb

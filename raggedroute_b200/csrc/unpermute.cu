@@ -1,11 +1,16 @@
 // Weighted unpermute (combine) for B200.
 //
 // y[t, c] = sum_{k < top_k} w[t*top_k + k] * y_permuted[route_pos[t*top_k + k], c],
-// accumulated in rank order k = 0, 1, ... with fused multiply-adds from 0.0f
+// accumulated in rank order k = 0, 1, ... from 0.0f
 // (src/unpermute/cuda_naive/baseline.cu:13-30; the CPU reference
 // src/unpermute/cpu_reference/reference.cpp:10-37 sums the same terms in
-// double). No atomics: each output row is produced by one warp, so results
-// are bitwise reproducible.
+// double). Each term is the rounded product w * v, added with
+// round-to-nearest and subnormal operands and results flushed to zero: the
+// arithmetic of the global float reduction that the grouped GEMM's fused
+// combine uses, so the fused and the separate chains agree bit for bit
+// (products and sums below 2^-126 in magnitude become zero; the reference's
+// fused multiply-add keeps them). No atomics: each output row is produced by
+// one warp, so results are bitwise reproducible.
 //
 // Design: one warp per token; the token's route positions and weights are
 // fetched once per warp and broadcast by shuffle; each lane owns 128-bit
@@ -55,10 +60,10 @@ __global__ void __launch_bounds__(kThreads) unpermute_kernel(const float* __rest
         for (int k = 0; k < kMaxK; ++k) {
           if (k < top_k && pos[k] >= 0) {
             const float4 v = __ldg(reinterpret_cast<const float4*>(yp + pos[k] * output) + i);
-            acc.x = fmaf(w[k], v.x, acc.x);
-            acc.y = fmaf(w[k], v.y, acc.y);
-            acc.z = fmaf(w[k], v.z, acc.z);
-            acc.w = fmaf(w[k], v.w, acc.w);
+            acc.x = add_ftz(acc.x, __fmul_rn(w[k], v.x));
+            acc.y = add_ftz(acc.y, __fmul_rn(w[k], v.y));
+            acc.z = add_ftz(acc.z, __fmul_rn(w[k], v.z));
+            acc.w = add_ftz(acc.w, __fmul_rn(w[k], v.w));
           }
         }
         reinterpret_cast<float4*>(out)[i] = acc;
@@ -68,7 +73,9 @@ __global__ void __launch_bounds__(kThreads) unpermute_kernel(const float* __rest
         float acc = 0.0f;
 #pragma unroll
         for (int k = 0; k < kMaxK; ++k) {
-          if (k < top_k && pos[k] >= 0) acc = fmaf(w[k], __ldg(yp + pos[k] * output + c), acc);
+          if (k < top_k && pos[k] >= 0) {
+            acc = add_ftz(acc, __fmul_rn(w[k], __ldg(yp + pos[k] * output + c)));
+          }
         }
         out[c] = acc;
       }
@@ -90,7 +97,10 @@ __global__ void __launch_bounds__(kThreads) unpermute_wide_kernel(
       for (int k = 0; k < top_k; ++k) {
         const long long r = t * top_k + k;
         const int p = __ldg(route_pos + r);
-        if (p >= 0 && p < routes) acc = fmaf(__ldg(rw + r), __ldg(yp + static_cast<long long>(p) * output + c), acc);
+        if (p >= 0 && p < routes) {
+          acc = add_ftz(acc, __fmul_rn(__ldg(rw + r),
+                                       __ldg(yp + static_cast<long long>(p) * output + c)));
+        }
       }
       y[t * output + c] = acc;
     }

@@ -34,17 +34,19 @@ def _ctx(ctx: Context | None, workspace: torch.Tensor | None = None) -> ctypes.P
 
 CHAIN_IMPL_GATHER_ROWS = 1
 CHAIN_IMPL_PREPARED_WEIGHTS = 2
+CHAIN_IMPL_FUSED_COMBINE = 4
 
 
 def _chain_ctx(ctx: Context | None, workspace: torch.Tensor, gather_rows: bool,
-               prepared: bool = False):
+               prepared: bool = False, fused_combine: bool = False):
     if gather_rows and prepared:
         raise ValueError("gather_rows does not combine with prepared expert weights")
     c = dataclasses.replace(ctx) if ctx is not None else Context()
-    if gather_rows:
-        c.implementation_id = CHAIN_IMPL_GATHER_ROWS
-    if prepared:
-        c.implementation_id = CHAIN_IMPL_PREPARED_WEIGHTS
+    bits = ((CHAIN_IMPL_GATHER_ROWS if gather_rows else 0) |
+            (CHAIN_IMPL_PREPARED_WEIGHTS if prepared else 0) |
+            (CHAIN_IMPL_FUSED_COMBINE if fused_combine else 0))
+    if bits:
+        c.implementation_id = bits
     return _ctx(c, workspace)
 
 
@@ -190,6 +192,37 @@ def grouped_gemm_gather(x: torch.Tensor, sorted_route: torch.Tensor, top_k: int,
     return y_permuted
 
 
+def grouped_gemm_combine(x_permuted: torch.Tensor, expert_weights: torch.Tensor,
+                         offsets: torch.Tensor, sorted_route: torch.Tensor,
+                         route_weights: torch.Tensor, y: torch.Tensor, route_pairs: int,
+                         top_k: int, ctx: Context | None = None) -> torch.Tensor:
+    """Grouped GEMM with the unpermute fused into its epilogue
+    (rr_grouped_gemm_combine): y [T, N] = sum over each token's routes of
+    weight * (x_permuted row . W[e]); top_k 1 or 2."""
+    experts, hidden, output = expert_weights.shape
+    check(lib().rr_grouped_gemm_combine(_ptr(x_permuted), _ptr(expert_weights), _ptr(offsets),
+                                        _ptr(sorted_route), _ptr(route_weights), _ptr(y),
+                                        experts, hidden, output, route_pairs, y.shape[0], top_k,
+                                        _ctx(ctx)), "grouped_gemm_combine")
+    return y
+
+
+def grouped_gemm_scatter(x_permuted: torch.Tensor, expert_weights: torch.Tensor,
+                         offsets: torch.Tensor, row_address: torch.Tensor,
+                         bases: torch.Tensor, row_limit: int, route_pairs: int,
+                         ctx: Context | None = None) -> None:
+    """Grouped GEMM storing output row r at bases[a >> 40] + (a & (2**40 - 1)) * N,
+    a = row_address[r] (rr_grouped_gemm_scatter); bases is an int64 device
+    tensor of row-buffer pointers."""
+    experts, hidden, output = expert_weights.shape
+    _need(row_address, torch.int64, "row_address")
+    _need(bases, torch.int64, "bases")
+    check(lib().rr_grouped_gemm_scatter(_ptr(x_permuted), _ptr(expert_weights), _ptr(offsets),
+                                        _ptr(row_address), _ptr(bases), bases.numel(),
+                                        row_limit, experts, hidden, output, route_pairs,
+                                        _ctx(ctx)), "grouped_gemm_scatter")
+
+
 def grouped_gemm_prepared(x_permuted: torch.Tensor, weights: PreparedExpertWeights,
                           offsets: torch.Tensor, y_permuted: torch.Tensor, route_pairs: int,
                           ctx: Context | None = None) -> torch.Tensor:
@@ -260,11 +293,13 @@ def chain_workspace_size(tokens: int, hidden: int, experts: int, output: int) ->
 def chain_from_tokens(x: torch.Tensor, router_weights: torch.Tensor,
                       expert_weights, buf: ChainBuffers,
                       logit_bias: torch.Tensor | None = None,
-                      ctx: Context | None = None, gather_rows: bool = False) -> torch.Tensor:
+                      ctx: Context | None = None, gather_rows: bool = False,
+                      fused_combine: bool = False) -> torch.Tensor:
     """Seven-stage chain X -> Y (benchmarks/adapters/chain_adapter.cpp:263-467).
     expert_weights: W [E, K, N] or a PreparedExpertWeights.
     gather_rows: the grouped GEMM reads its rows from X (buf.x_permuted is
-    not written); results are bit-identical."""
+    not written); fused_combine: the unpermute runs in the grouped GEMM's
+    epilogue (buf.y_permuted is not written). Results are bit-identical."""
     tokens, hidden = x.shape
     experts = router_weights.shape[1]
     w_ptr, (_, _, output), prepared = _weights(expert_weights)
@@ -272,15 +307,16 @@ def chain_from_tokens(x: torch.Tensor, router_weights: torch.Tensor,
         _ptr(x), _ptr(router_weights), _ptr(logit_bias), w_ptr, _ptr(buf.logits),
         _ptr(buf.expert_ids), _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets),
         _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens,
-        hidden, experts, output, _chain_ctx(ctx, buf.workspace, gather_rows, prepared)),
+        hidden, experts, output,
+        _chain_ctx(ctx, buf.workspace, gather_rows, prepared, fused_combine)),
         "chain_from_tokens")
     return buf.y
 
 
 def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights,
                       buf: ChainBuffers, ctx: Context | None = None,
-                      gather_rows: bool = False) -> torch.Tensor:
-    """Six-stage chain logits -> Y; expert_weights as in chain_from_tokens."""
+                      gather_rows: bool = False, fused_combine: bool = False) -> torch.Tensor:
+    """Six-stage chain logits -> Y; options as in chain_from_tokens."""
     tokens, hidden = x.shape
     experts = logits.shape[1]
     w_ptr, (_, _, output), prepared = _weights(expert_weights)
@@ -288,7 +324,8 @@ def chain_from_logits(logits: torch.Tensor, x: torch.Tensor, expert_weights,
         _ptr(logits), _ptr(x), w_ptr, _ptr(buf.expert_ids),
         _ptr(buf.route_weights), _ptr(buf.counts), _ptr(buf.offsets), _ptr(buf.x_permuted),
         _ptr(buf.route_pos), _ptr(buf.y_permuted), _ptr(buf.y), tokens, hidden, experts, output,
-        _chain_ctx(ctx, buf.workspace, gather_rows, prepared)), "chain_from_logits")
+        _chain_ctx(ctx, buf.workspace, gather_rows, prepared, fused_combine)),
+        "chain_from_logits")
     return buf.y
 
 
@@ -326,9 +363,10 @@ class RouteChainBuffers:
 def chain_from_route_ids(x: torch.Tensor, expert_ids: torch.Tensor,
                          route_weights: torch.Tensor, expert_weights: torch.Tensor,
                          buf: RouteChainBuffers, ctx: Context | None = None,
-                         gather_rows: bool = False) -> torch.Tensor:
+                         gather_rows: bool = False, fused_combine: bool = False) -> torch.Tensor:
     """Post-route chain (benchmarks/adapters/postroute_chain_adapter.cpp:240-354):
-    expert_ids / route_weights [T, top_k] -> Y [T, N]."""
+    expert_ids / route_weights [T, top_k] -> Y [T, N]. fused_combine needs
+    top_k <= 2 and buf.sorted_route."""
     tokens, hidden = x.shape
     top_k = expert_ids.shape[1]
     experts, _, output = expert_weights.shape
@@ -336,7 +374,8 @@ def chain_from_route_ids(x: torch.Tensor, expert_ids: torch.Tensor,
         _ptr(x), _ptr(expert_ids), _ptr(route_weights), _ptr(expert_weights), _ptr(buf.counts),
         _ptr(buf.offsets), _ptr(buf.x_permuted), _ptr(buf.route_pos), _ptr(buf.sorted_route),
         _ptr(buf.y_permuted), _ptr(buf.y), tokens, top_k, hidden, experts, output,
-        _chain_ctx(ctx, buf.workspace, gather_rows)), "chain_from_route_ids")
+        _chain_ctx(ctx, buf.workspace, gather_rows, fused_combine=fused_combine)),
+        "chain_from_route_ids")
     return buf.y
 
 
