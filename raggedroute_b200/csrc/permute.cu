@@ -19,9 +19,14 @@
 //              giving each chunk its first slot per expert, in place.
 //   3. place:  inside a chunk each warp owns a contiguous run of routes; the
 //              per-(warp, expert) counts are scanned in shared memory and the
-//              rank inside a warp step comes from __match_any_sync plus a
-//              popcount of the lower lanes. The CTA then copies each token row
-//              once from x (128-bit loads) to its top_k destinations.
+//              rank inside a warp step is the popcount of the lower lanes with
+//              the same expert. The lanes with the same expert come from one
+//              ballot per bit of the expert id, a cost that does not grow with
+//              the number of distinct experts in a warp (__match_any_sync's
+//              does: measured in the histogram, 1M uniform routes took 14.4 us
+//              over 256 experts against 6.2 us over one). The CTA then copies
+//              each token row once from x (128-bit loads) to its top_k
+//              destinations.
 // A single chunk needs neither step 1 nor 2. The only workspace is the
 // reference's E int32 cursors (src/permute/operator.cpp:17-19), for every
 // input size: every chunk but the last spans at least E routes and keeps its
@@ -70,6 +75,21 @@ ChunkPlan plan_chunks(int tokens, int top_k, int experts) {
 
 __device__ __forceinline__ int warp_leader(unsigned peers) { return __ffs(peers) - 1; }
 
+// Bits of the keys 0..max_key.
+__device__ __forceinline__ int key_bits(int max_key) { return max_key <= 0 ? 0 : 32 - __clz(max_key); }
+
+// The lanes of the warp whose key equals this lane's (keys in [0, 2^nbits),
+// nbits warp-uniform; all 32 lanes call it): one ballot per key bit.
+__device__ __forceinline__ unsigned same_key_lanes(unsigned key, int nbits) {
+  unsigned m = 0xffffffffu;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (key >> b) & 1u;
+    const unsigned bal = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? bal : ~bal;
+  }
+  return m;
+}
+
 // Row c of the chunk table: the first E entries of chunk c's slice of
 // route_pos, or the cursors for the last chunk.
 __device__ __forceinline__ int32_t* chunk_row(int32_t* route_pos, int32_t* cursors, int c,
@@ -89,11 +109,14 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
   long long r1 = r0 + routes_per_chunk;
   if (r1 > routes) r1 = routes;
   const int lane = threadIdx.x & 31;
+  const int nbits = key_bits(experts);
   for (long long base = r0 + (threadIdx.x & ~31); base < r1; base += blockDim.x) {
     const long long r = base + lane;
     const int e = r < r1 ? __ldg(ids + r) : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (lane == warp_leader(peers) && e >= 0 && e < experts) atomicAdd(hist + e, __popc(peers));
+    const bool valid = e >= 0 && e < experts;
+    // Key 0 gathers every id outside the contract (never counted).
+    const unsigned peers = same_key_lanes(valid ? e + 1 : 0, nbits);
+    if (lane == warp_leader(peers) && valid) atomicAdd(hist + e, __popc(peers));
   }
   __syncthreads();
   int32_t* row = chunk_row(route_pos, cursors, blockIdx.x, gridDim.x, routes_per_chunk);
@@ -102,7 +125,13 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
 
 // Column-wise exclusive scan over the chunk table, in place, seeded with
 // offsets. Each CTA owns 32 experts (one per lane); its 32 warps split the
-// chunk range.
+// chunk range. Up to kKeep chunks per warp (chunk tables up to 1280 rows,
+// which covers every input up to 5.2M routes) the column is loaded once, all
+// loads in flight together, kept in registers and written back scanned; larger
+// tables take two batched passes.
+constexpr int kScanKeep = 40;
+
+template <bool kKeep>
 __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, int32_t* cursors,
                                                             const int32_t* __restrict__ offsets,
                                                             int chunks, int routes_per_chunk,
@@ -114,17 +143,29 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
   const int per = (chunks + 31) / 32;
   const int c0 = grp * per;
   const int c1 = min(chunks, c0 + per);
-  constexpr int kBatch = 8;  // loads in flight per lane
+  constexpr int kBatch = 8;  // loads in flight per lane on the two-pass path
+  int keep[kKeep ? kScanKeep : 1];
   int sum = 0;
   if (e < experts) {
-    for (int c = c0; c < c1; c += kBatch) {
-      int v[kBatch];
+    if constexpr (kKeep) {
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] : 0;
+      for (int u = 0; u < kScanKeep; ++u) {
+        keep[u] = c0 + u < c1 ? chunk_row(route_pos, cursors, c0 + u, chunks, routes_per_chunk)[e]
+                              : 0;
       }
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) sum += v[u];
+      for (int u = 0; u < kScanKeep; ++u) sum += keep[u];
+    } else {
+      for (int c = c0; c < c1; c += kBatch) {
+        int v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e]
+                            : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) sum += v[u];
+      }
     }
   }
   part[grp][lane] = sum;
@@ -140,16 +181,25 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
   __syncthreads();
   if (e < experts) {
     int run = offsets[e] + part[grp][lane];
-    for (int c = c0; c < c1; c += kBatch) {
-      int v[kBatch];
+    if constexpr (kKeep) {
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] : 0;
+      for (int u = 0; u < kScanKeep; ++u) {
+        if (c0 + u < c1) chunk_row(route_pos, cursors, c0 + u, chunks, routes_per_chunk)[e] = run;
+        run += keep[u];
       }
+    } else {
+      for (int c = c0; c < c1; c += kBatch) {
+        int v[kBatch];
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        if (c + u < c1) chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] = run;
-        run += v[u];
+        for (int u = 0; u < kBatch; ++u) {
+          v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e]
+                            : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (c + u < c1) chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] = run;
+          run += v[u];
+        }
       }
     }
   }
@@ -270,7 +320,9 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
   for (int i = threadIdx.x; i < kPlaceWarps * experts; i += blockDim.x) warp_base[i] = 0;
   __syncthreads();
 
-  // Pass 1: per-warp expert counts; ids stay in registers.
+  // Pass 1: per-warp expert counts; ids stay in registers. Keys: expert + 1,
+  // 0 for "no route" and "out of contract".
+  const int nbits = key_bits(experts);
   int my_ids[kMaxPerLane];
   int* my_count = warp_base + warp * experts;
 #pragma unroll
@@ -284,7 +336,7 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
         if (e < 0 || e >= experts) e = -2;  // out of contract: skipped
       }
       my_ids[s] = e;
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const unsigned peers = same_key_lanes(e >= 0 ? e + 1 : 0, nbits);
       if (lane == warp_leader(peers) && e >= 0) my_count[e] += __popc(peers);
       __syncwarp();
     }
@@ -316,7 +368,7 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
   for (int s = 0; s < kMaxPerLane; ++s) {
     if (s < steps) {
       const int e = my_ids[s];
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const unsigned peers = same_key_lanes(e >= 0 ? e + 1 : 0, nbits);
       int p = -1;
       if (e >= 0) p = my_count[e] + __popc(peers & lt);
       __syncwarp();
@@ -447,11 +499,12 @@ __global__ void __launch_bounds__(1024) permute_cursor_rank_kernel(
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     const unsigned lt = lanemask_lt();
+    const int nbits = key_bits(kMaxExperts);
     for (int base = 0; base < routes; base += 32) {
       const int r = base + lane;
       int e = r < routes ? __ldg(ids + r) : -1;
       if (e >= kMaxExperts) e = -2;
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const unsigned peers = same_key_lanes(e >= 0 ? e + 1 : 0, nbits);
       int p = -1;
       if (e >= 0) p = offsets[e] + cur[e] + __popc(peers & lt);
       __syncwarp();
@@ -505,8 +558,13 @@ cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offs
   if (p.chunks > 1) {
     permute_count_kernel<<<p.chunks, kPlaceThreads, experts * sizeof(int), stream>>>(
         ids, routes, experts, routes_per_chunk, route_pos, cursors);
-    permute_scan_kernel<<<ceil_div(experts, 32), 1024, 0, stream>>>(
-        route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
+    if (p.chunks <= 32 * kScanKeep) {
+      permute_scan_kernel<true><<<ceil_div(experts, 32), 1024, 0, stream>>>(
+          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
+    } else {
+      permute_scan_kernel<false><<<ceil_div(experts, 32), 1024, 0, stream>>>(
+          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
+    }
     note_launch(2);
   }
   // Peer mode keeps pos[] at its full size so the int64 table that follows is
