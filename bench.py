@@ -81,6 +81,11 @@ def parse_args():
     ap.add_argument("--profile-once", action="store_true",
                     help="one warm-up chain, then one validated untimed chain_from_tokens call "
                          "(NVTX range per stage: raggedroute_<stage>) for profilers")
+    ap.add_argument("--c3-permute", default=None, metavar="E:DIST[,E:DIST...]",
+                    help="run only BASELINE C3's token_permute (R=1M routes, K=128) for the "
+                         "given expert counts and id distributions, 3 calls each, and print "
+                         "their event times: a small single-operator command for Nsight "
+                         "Compute, e.g. 256:uniform,8:one")
     ap.add_argument("--only-stage", default=None,
                     choices=["dense_gemm", "topk_gate", "histogram_exclusive_scan",
                              "token_permute", "grouped_gemm", "unpermute"],
@@ -591,6 +596,44 @@ def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) 
             "ms_min": min(times)}
 
 
+def run_c3_permute(spec: str) -> dict:
+    """C3's stable token_permute (R = 1,048,576 routes, T = R/2 tokens, K = 128,
+    with sorted_route) for each E:dist in spec: histogram + scan once, then
+    three permute calls, each timed with CUDA events; nothing else runs."""
+    import torch
+
+    import raggedroute_b200 as rr
+    from raggedroute_b200.workloads import C3, route_ids
+    device = torch.device("cuda", 0)
+    routes, k = C3["routes"], C3["hidden"]
+    tokens = routes // 2
+    x = torch.rand(tokens, k, device=device) * 2 - 1
+    xp = torch.empty(routes, k, device=device)
+    pos = torch.empty(routes, dtype=torch.int32, device=device)
+    srt = torch.empty(routes, dtype=torch.int32, device=device)
+    out = {}
+    for item in spec.split(","):
+        e_s, dist = item.split(":")
+        e = int(e_s)
+        counts = torch.empty(e, dtype=torch.int32, device=device)
+        offsets = torch.empty(e + 1, dtype=torch.int32, device=device)
+        ws = torch.empty(rr.token_permute_workspace_size(tokens, e, 2, k) // 4 + 1,
+                         dtype=torch.int32, device=device)
+        ids = torch.as_tensor(route_ids(routes, e, dist, seed=C3["seed"]), device=device)
+        rr.histogram_exclusive_scan(ids, counts, offsets, routes, e)
+        times = []
+        for _ in range(3):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            rr.token_permute(x, ids, offsets, xp, pos, srt, tokens, e, 2, k, ws)
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b) * 1e3)
+        out[f"E{e}_{dist}"] = {"token_permute_us": [round(t, 2) for t in times]}
+    return {"c3_permute": out}
+
+
 def run_profile_once(torch, rr, stream, ctx, inp, buf, tokens: int, e: int) -> dict:
     """One warm-up chain, then exactly one untimed chain_from_tokens call for a
     profiler (the library brackets each stage in an NVTX range named
@@ -955,6 +998,8 @@ def _main() -> dict | None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.c3_permute is not None:
+        return run_c3_permute(args.c3_permute)
     if world > 1:
         import datetime
 
