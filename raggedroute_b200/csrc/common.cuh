@@ -53,6 +53,9 @@ struct RowScatter {
   const int32_t* route = nullptr;
   const float* weight = nullptr;
   int top_k = 1;
+  // > 0: the persistent GEMM uses at most this many SMs (CTAs), leaving the
+  // rest to a kernel that runs beside it (the expert-parallel dispatch).
+  int max_ctas = 0;
 };
 
 // Resolves a packed row address, or nullptr when it is out of range.
@@ -118,6 +121,15 @@ struct PeerDispatch {
   // Abort fence, as in RowScatter: when set at kernel start, nothing is
   // written to any rank's buffers.
   const volatile int* abort = nullptr;
+  // Only routes whose local expert index (expert % local) is in
+  // [le_lo, le_hi) are sent (a dispatch split into launches by expert range).
+  int le_lo = 0;
+  int le_hi = 1 << 30;
+  // The permute's chunk table ([chunks][experts] int32,
+  // permute_chunk_table_bytes); required when the place step runs more than
+  // once per prepared table (the default table lives in route_pos and the
+  // first placement overwrites it).
+  int32_t* chunk_table = nullptr;
 };
 
 // Counts every kernel this library launches (for the bench's launch claim).
@@ -186,10 +198,18 @@ cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32
                                  cudaStream_t stream);
 // The same permute (identical route_pos) whose copy goes to other ranks'
 // receive buffers through the peer mapping instead of to x_permuted.
+// prepare = false skips the count and scan launches and places from the
+// chunk table a previous call prepared (peer.chunk_table, kept intact);
+// max_ctas > 0 caps the place grid (a persistent loop over chunks), so a
+// placement can run beside a kernel that holds the other SMs.
 cudaError_t launch_token_permute_peer(const float* x, const int32_t* ids, const int32_t* offsets,
                                       int32_t* route_pos, int tokens, int experts, int top_k,
                                       int hidden, void* workspace, const PeerDispatch& peer,
-                                      cudaStream_t stream);
+                                      cudaStream_t stream, bool prepare = true,
+                                      int max_ctas = 0);
+// Bytes of a chunk table that serves the permute of any token count up to
+// `tokens`.
+std::size_t permute_chunk_table_bytes(int tokens, int experts, int top_k);
 // Workspace-free stable permute for the low-level launcher: the expert count
 // is unknown, cursors accumulate (caller zeroes them).
 cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,

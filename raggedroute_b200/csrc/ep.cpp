@@ -22,6 +22,13 @@
 //   5. grouped GEMM over the receive buffer; its epilogue stores each output
 //      row at its return address in the source rank's y buffer;
 //   6. barrier: all outputs have landed; local unpermute.
+// With RAGGEDROUTE_B200_EP_DISPATCH_SMS=n (n > 0) steps 3-5 overlap the
+// dispatch with the GEMM: the owners' local experts are split
+// in halves; the first half is dispatched and barriered, then its GEMM runs
+// on all SMs but a few while the second half is dispatched from those few
+// SMs on a second stream, and after a barrier the second half's GEMM runs.
+// The permute's chunk table lives in a plan buffer so that both placements
+// read it; both write the same route_pos.
 // No host synchronisation inside a step; the next call (or
 // rr_ep_last_step_rows) waits for the previous step with a deadline. The
 // barriers also order steps: a rank's next dispatch cannot start before every
@@ -53,6 +60,7 @@
 #include <atomic>
 #include <chrono>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <thread>
@@ -97,6 +105,14 @@ struct rr_ep {
   int64_t** d_ret_base = nullptr;  // [nranks] every rank's recv_ret
   float** d_y_base = nullptr;      // [nranks] every rank's y_back
   std::vector<void*> imported;     // IPC mappings to close
+  // Dispatch/GEMM overlap (peer transport): SMs left to the second half's
+  // dispatch while the first half's grouped GEMM runs (0 = no overlap), the
+  // permute's chunk table (kept intact across its two placements) and the
+  // events that order the dispatch stream (comm_stream) against the caller's.
+  int overlap_sms = 0;
+  int32_t* chunk_table = nullptr;
+  cudaEvent_t half0_ready = nullptr;
+  cudaEvent_t half1_sent = nullptr;
   // Step bookkeeping in two slots, so that a call only waits for the step
   // before the previous one and the host keeps one step queued ahead.
   unsigned* h_err = nullptr;        // pinned [2]
@@ -114,6 +130,13 @@ struct rr_ep {
 };
 
 namespace {
+
+// SMs the second half's dispatch runs on beside the first half's grouped
+// GEMM (peer transport); 0 = no overlap. Off by default: at 2 GPUs the split
+// measured slower (10.92 ms/step with 8 SMs, 11.22 with 16, against 10.52
+// without), the first half's GEMM losing more to the SMs it gives up than
+// the hidden half of the dispatch saves.
+constexpr int kDefaultOverlapSms = 0;
 
 rr_status st(int32_t code, const char* msg, int32_t cuda_err = 0) {
   rr_status s;
@@ -213,6 +236,9 @@ void free_ep(rr_ep* ep) {
   for (cudaEvent_t ev : ep->dispatched) cudaEventDestroy(ev);
   for (cudaEvent_t ev : ep->computed) cudaEventDestroy(ev);
   if (ep->local_ready != nullptr) cudaEventDestroy(ep->local_ready);
+  if (ep->half0_ready != nullptr) cudaEventDestroy(ep->half0_ready);
+  if (ep->half1_sent != nullptr) cudaEventDestroy(ep->half1_sent);
+  cudaFree(ep->chunk_table);
   if (ep->combine_done != nullptr) cudaEventDestroy(ep->combine_done);
   if (ep->comm_stream != nullptr) cudaStreamDestroy(ep->comm_stream);
   if (ep->comm != nullptr) ncclCommDestroy(ep->comm);
@@ -520,6 +546,19 @@ rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int router_e
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ep->comm_stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->local_ready, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->combine_done, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->half0_ready, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->half1_sent, cudaEventDisableTiming);
+  if (e == cudaSuccess && nranks > 1) {
+    const std::size_t tb = rrb::permute_chunk_table_bytes(max_tokens, experts, 2);
+    if (tb > 0) e = cudaMalloc(&ep->chunk_table, tb);
+  }
+  {
+    // Every rank must use the same setting (it changes the sequence of
+    // collectives): the variable is read once here.
+    const char* v = std::getenv("RAGGEDROUTE_B200_EP_DISPATCH_SMS");
+    ep->overlap_sms = v != nullptr ? std::atoi(v) : kDefaultOverlapSms;
+    if (ep->overlap_sms < 0) ep->overlap_sms = 0;
+  }
   for (int i = 0; e == cudaSuccess && i < 2; ++i) {
     e = cudaEventCreateWithFlags(&ep->step_done[i], cudaEventDisableTiming);
   }
@@ -681,22 +720,36 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     if (s.code != RR_SUCCESS) return s;
     e = rrb::launch_ep_peer_layout(ep->count_all, ep->dest_off, ep->recv_offsets, G, E, ep->rank,
                                    ep->local, ep->capacity_rows, ep->d_err, stream);
-    // 3. Dispatch fused into the permute.
+    // 3. Dispatch fused into the permute. With the overlap (every rank makes
+    // the same choice: it depends on the plan only) the owners' local
+    // experts are split in two halves: the first half's rows go out on all
+    // SMs; then, while the first half's grouped GEMM runs on all SMs but
+    // overlap_sms, the second half's rows go out from a persistent dispatch
+    // on those SMs (on comm_stream); the second half's GEMM follows once
+    // every rank's second half has landed. No kernel waits on another: the
+    // two halves meet only at NCCL barriers on the caller's stream.
+    const int L = ep->local;
+    const bool split = ep->overlap_sms > 0 && L >= 2 &&
+                       4 * ep->overlap_sms < rrb::sm_count() && ep->chunk_table != nullptr;
+    const int half = split ? L / 2 : L;
+    rrb::PeerDispatch pd;
+    pd.x_base = ep->d_x_base;
+    pd.ret_base = ep->d_ret_base;
+    pd.dest_off = ep->dest_off;
+    pd.local = L;
+    pd.me = ep->rank;
+    pd.capacity = ep->capacity_rows;
+    pd.err = ep->d_err;
+    pd.abort = ep->d_abort;
+    pd.chunk_table = ep->chunk_table;
+    pd.le_lo = 0;
+    pd.le_hi = half;
     if (e == cudaSuccess && tokens > 0) {
-      rrb::PeerDispatch pd;
-      pd.x_base = ep->d_x_base;
-      pd.ret_base = ep->d_ret_base;
-      pd.dest_off = ep->dest_off;
-      pd.local = ep->local;
-      pd.me = ep->rank;
-      pd.capacity = ep->capacity_rows;
-      pd.err = ep->d_err;
-      pd.abort = ep->d_abort;
       e = rrb::launch_token_permute_peer(x, expert_ids, offsets, route_pos, tokens, E, 2, K,
                                          ctx->workspace, pd, stream);
     }
     if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP dispatch launch failed", e);
-    // 4. Every rank's rows have landed.
+    // 4. Every rank's rows (of the first half) have landed.
     s = barrier(ep, stream);
     if (s.code != RR_SUCCESS) return s;
     // 5. Expert GEMM over the receive buffer, combine fused into its epilogue.
@@ -706,9 +759,41 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     sc.nranks = G;
     sc.row_limit = 2LL * ep->max_tokens;
     sc.abort = ep->d_abort;
-    e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets, ep->y_back,
-                                 ep->local, static_cast<int>(ep->capacity_rows), K, N, stream, 0,
-                                 &sc);
+    if (split) {
+      e = cudaEventRecord(ep->half0_ready, stream);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(ep->comm_stream, ep->half0_ready, 0);
+      if (e == cudaSuccess && tokens > 0) {
+        pd.le_lo = half;
+        pd.le_hi = L;
+        e = rrb::launch_token_permute_peer(x, expert_ids, offsets, route_pos, tokens, E, 2, K,
+                                           ctx->workspace, pd, ep->comm_stream,
+                                           /*prepare=*/false, ep->overlap_sms);
+      }
+      if (e == cudaSuccess) e = cudaEventRecord(ep->half1_sent, ep->comm_stream);
+      if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP second-half dispatch launch failed", e);
+      // The first half's GEMM walks a static tile schedule, so all of its
+      // CTA pairs must be resident together: a dispatch CTA can leave its
+      // SM's GPC with an odd number of free SMs, so every dispatch SM is
+      // counted as a lost pair (2 SMs).
+      rrb::RowScatter sc0 = sc;
+      sc0.max_ctas = rrb::sm_count() - 2 * ep->overlap_sms;
+      e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets,
+                                   ep->y_back, half, static_cast<int>(ep->capacity_rows), K, N,
+                                   stream, 0, &sc0);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ep->half1_sent, 0);
+      if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP grouped GEMM launch failed", e);
+      // Every rank's second half has landed.
+      s = barrier(ep, stream);
+      if (s.code != RR_SUCCESS) return s;
+      e = rrb::launch_grouped_gemm(ep->recv_x,
+                                   local_expert_weights + static_cast<long long>(half) * K * N,
+                                   ep->recv_offsets + half, ep->y_back, L - half,
+                                   static_cast<int>(ep->capacity_rows), K, N, stream, 0, &sc);
+    } else {
+      e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets,
+                                   ep->y_back, L, static_cast<int>(ep->capacity_rows), K, N,
+                                   stream, 0, &sc);
+    }
     if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP grouped GEMM launch failed", e);
     // 6. Every rank's outputs have landed; local unpermute.
     s = barrier(ep, stream);

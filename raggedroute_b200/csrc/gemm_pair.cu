@@ -524,6 +524,7 @@ cudaError_t launch_grouped_gemm_pair(const float* x, const float* w, const int32
     if (tiles < units) units = static_cast<int>(tiles);
   }
   const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
+  if (sc.max_ctas > 0 && units > sc.max_ctas / 2) units = sc.max_ctas / 2 > 0 ? sc.max_ctas / 2 : 1;
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pair_config(units, stream, attr);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel, ma, mb, offsets, y,

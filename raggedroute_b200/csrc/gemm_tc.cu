@@ -735,6 +735,7 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
     if (pe != cudaErrorNotSupported) return pe;
   }
   const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
+  if (sc.max_ctas > 0 && grid > sc.max_ctas) grid = sc.max_ctas;
   if (gather != nullptr) {
     grouped_gemm_tc_kernel<true, 1><<<grid, kThreads, kSmemBytes, stream>>>(
         ma, mb, mb, offsets, y, experts, rows, hidden, output, wsets, device_error_word(), sc,

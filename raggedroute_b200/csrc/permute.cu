@@ -90,10 +90,14 @@ __device__ __forceinline__ unsigned same_key_lanes(unsigned key, int nbits) {
   return m;
 }
 
-// Row c of the chunk table: the first E entries of chunk c's slice of
-// route_pos, or the cursors for the last chunk.
-__device__ __forceinline__ int32_t* chunk_row(int32_t* route_pos, int32_t* cursors, int c,
-                                              int chunks, int routes_per_chunk) {
+// Row c of the chunk table: row c of `table` when the caller provides one
+// (the expert-parallel dispatch, which places in two launches and so must
+// not lose the table to the first), else the first E entries of chunk c's
+// slice of route_pos, or the cursors for the last chunk.
+__device__ __forceinline__ int32_t* chunk_row(int32_t* table, int32_t* route_pos,
+                                              int32_t* cursors, int c, int chunks,
+                                              int routes_per_chunk, int experts) {
+  if (table != nullptr) return table + static_cast<long long>(c) * experts;
   return c == chunks - 1 ? cursors
                          : route_pos + static_cast<long long>(c) * routes_per_chunk;
 }
@@ -101,7 +105,7 @@ __device__ __forceinline__ int32_t* chunk_row(int32_t* route_pos, int32_t* curso
 // Per-chunk histogram into the chunk's table row.
 __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
     const int32_t* __restrict__ ids, int routes, int experts, int routes_per_chunk,
-    int32_t* route_pos, int32_t* cursors) {
+    int32_t* route_pos, int32_t* cursors, int32_t* table) {
   extern __shared__ int hist[];
   for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -119,7 +123,8 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
     if (lane == warp_leader(peers) && valid) atomicAdd(hist + e, __popc(peers));
   }
   __syncthreads();
-  int32_t* row = chunk_row(route_pos, cursors, blockIdx.x, gridDim.x, routes_per_chunk);
+  int32_t* row = chunk_row(table, route_pos, cursors, blockIdx.x, gridDim.x, routes_per_chunk,
+                           experts);
   for (int i = threadIdx.x; i < experts; i += blockDim.x) row[i] = hist[i];
 }
 
@@ -135,7 +140,7 @@ template <bool kKeep>
 __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, int32_t* cursors,
                                                             const int32_t* __restrict__ offsets,
                                                             int chunks, int routes_per_chunk,
-                                                            int experts) {
+                                                            int experts, int32_t* table) {
   __shared__ int part[32][33];
   const int lane = threadIdx.x & 31;
   const int grp = threadIdx.x >> 5;
@@ -144,14 +149,16 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
   const int c0 = grp * per;
   const int c1 = min(chunks, c0 + per);
   constexpr int kBatch = 8;  // loads in flight per lane on the two-pass path
+  auto row = [&](int c) {
+    return chunk_row(table, route_pos, cursors, c, chunks, routes_per_chunk, experts);
+  };
   int keep[kKeep ? kScanKeep : 1];
   int sum = 0;
   if (e < experts) {
     if constexpr (kKeep) {
 #pragma unroll
       for (int u = 0; u < kScanKeep; ++u) {
-        keep[u] = c0 + u < c1 ? chunk_row(route_pos, cursors, c0 + u, chunks, routes_per_chunk)[e]
-                              : 0;
+        keep[u] = c0 + u < c1 ? row(c0 + u)[e] : 0;
       }
 #pragma unroll
       for (int u = 0; u < kScanKeep; ++u) sum += keep[u];
@@ -160,8 +167,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
         int v[kBatch];
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-          v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e]
-                            : 0;
+          v[u] = c + u < c1 ? row(c + u)[e] : 0;
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) sum += v[u];
@@ -184,7 +190,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
     if constexpr (kKeep) {
 #pragma unroll
       for (int u = 0; u < kScanKeep; ++u) {
-        if (c0 + u < c1) chunk_row(route_pos, cursors, c0 + u, chunks, routes_per_chunk)[e] = run;
+        if (c0 + u < c1) row(c0 + u)[e] = run;
         run += keep[u];
       }
     } else {
@@ -192,12 +198,11 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
         int v[kBatch];
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-          v[u] = c + u < c1 ? chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e]
-                            : 0;
+          v[u] = c + u < c1 ? row(c + u)[e] : 0;
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-          if (c + u < c1) chunk_row(route_pos, cursors, c + u, chunks, routes_per_chunk)[e] = run;
+          if (c + u < c1) row(c + u)[e] = run;
           run += v[u];
         }
       }
@@ -287,18 +292,21 @@ __device__ __forceinline__ void copy_row_warp_to(const float* __restrict__ src, 
   }
 }
 
-// Place + copy. With one chunk the slots are seeded by offsets; with several,
-// by the chunk's row of the scanned chunk table. The single or last chunk
-// writes the cursor post-state (per-expert counts).
+// Place + copy of one chunk. With one chunk the slots are seeded by offsets;
+// with several, by the chunk's row of the scanned chunk table. The single or
+// last chunk writes the cursor post-state (per-expert counts).
 // With kPeer the rows go to the owners' receive buffers (PeerDispatch) and
-// xp / sorted_route are unused.
+// xp / sorted_route are unused; only routes whose local expert index
+// (expert % local) lies in [peer.le_lo, peer.le_hi) are sent, so a dispatch
+// can be split into launches over expert ranges (route_pos is written in
+// full by every launch, with the same values).
 template <bool kVec, bool kPeer>
-__global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
-    const float* __restrict__ x, const int32_t* __restrict__ ids,
-    const int32_t* __restrict__ offsets, float* __restrict__ xp, int32_t* route_pos,
-    int32_t* __restrict__ sorted_route, int32_t* cursors, int tokens, int experts, int top_k,
-    int hidden, int tokens_per_chunk, const PeerDispatch peer) {
-  extern __shared__ int smem[];
+__device__ __forceinline__ void place_chunk(
+    int chunk, int chunks, int* smem, const int& aborted, const float* __restrict__ x,
+    const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets, float* __restrict__ xp,
+    int32_t* route_pos, int32_t* __restrict__ sorted_route, int32_t* cursors, int tokens,
+    int experts, int top_k, int hidden, int tokens_per_chunk, int32_t* table,
+    const PeerDispatch& peer) {
   int* warp_base = smem;                            // [kPlaceWarps][experts]
   int* pos = smem + kPlaceWarps * experts;          // [routes in chunk]
   // Peer mode: packed (owner << 40 | receive row) per route, -1 = dropped.
@@ -306,7 +314,7 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
       smem + ((kPlaceWarps * experts + kMaxChunkRoutes + 1) & ~1));
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int t0 = blockIdx.x * tokens_per_chunk;
+  const int t0 = chunk * tokens_per_chunk;
   const int t1 = min(tokens, t0 + tokens_per_chunk);
   const long long r0 = static_cast<long long>(t0) * top_k;
   const int nr = (t1 - t0) * top_k;
@@ -315,8 +323,6 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
   const int w0 = warp * per_warp;
   const int steps = per_warp >> 5;  // <= kMaxPerLane
 
-  __shared__ int aborted;
-  if (threadIdx.x == 0) aborted = (kPeer && peer.abort != nullptr) ? *peer.abort : 0;
   for (int i = threadIdx.x; i < kPlaceWarps * experts; i += blockDim.x) warp_base[i] = 0;
   __syncthreads();
 
@@ -345,11 +351,11 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
 
   // Per-(warp, expert) starting slots, from the chunk's table row (read
   // here, before pass 2 overwrites this chunk's slice of route_pos).
-  const bool chunked = gridDim.x > 1;
-  const bool last = blockIdx.x == gridDim.x - 1;
-  const int32_t* row =
-      chunked ? chunk_row(route_pos, cursors, blockIdx.x, gridDim.x, tokens_per_chunk * top_k)
-              : offsets;
+  const bool chunked = chunks > 1;
+  const bool last = chunk == chunks - 1;
+  const int32_t* row = chunked ? chunk_row(table, route_pos, cursors, chunk, chunks,
+                                           tokens_per_chunk * top_k, experts)
+                               : offsets;
   for (int e = threadIdx.x; e < experts; e += blockDim.x) {
     int run = row[e];
 #pragma unroll
@@ -380,7 +386,8 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
         route_pos[r0 + local] = p;
         if constexpr (kPeer) {
           long long packed = -1;
-          if (p >= 0 && !aborted) {
+          const int le = e >= 0 ? e % peer.local : -1;
+          if (p >= 0 && !aborted && le >= peer.le_lo && le < peer.le_hi) {
             const int owner = e / peer.local;
             const long long row = static_cast<long long>(__ldg(peer.dest_off + e)) +
                                   (p - __ldg(offsets + e));
@@ -417,9 +424,6 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
         copy_row_warp_to<kVec>(x + static_cast<long long>(t) * hidden, dst, kn, hidden);
       }
     }
-    // Make this thread's stores to other ranks' memory complete before the
-    // kernel ends (the barrier that follows then publishes them).
-    __threadfence_system();
     return;
   }
   if (hidden <= 0) return;
@@ -479,6 +483,28 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
 // One CTA: finds the largest expert id, mirrors the caller's cursors into
 // shared memory, and ranks every route in order with a single warp. Slot =
 // offsets[e] + cursors[e] (running). Cursors are written back at the end.
+template <bool kVec, bool kPeer>
+__global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
+    const float* __restrict__ x, const int32_t* __restrict__ ids,
+    const int32_t* __restrict__ offsets, float* __restrict__ xp, int32_t* route_pos,
+    int32_t* __restrict__ sorted_route, int32_t* cursors, int tokens, int experts, int top_k,
+    int hidden, int tokens_per_chunk, int chunks, int32_t* table, const PeerDispatch peer) {
+  extern __shared__ int smem[];
+  __shared__ int aborted;
+  if (threadIdx.x == 0) aborted = (kPeer && peer.abort != nullptr) ? *peer.abort : 0;
+  // One chunk per CTA, or a persistent loop when the grid is capped (a
+  // dispatch that runs beside the grouped GEMM on a few SMs).
+  for (int c = blockIdx.x; c < chunks; c += gridDim.x) {
+    place_chunk<kVec, kPeer>(c, chunks, smem, aborted, x, ids, offsets, xp, route_pos,
+                             sorted_route, cursors, tokens, experts, top_k, hidden,
+                             tokens_per_chunk, table, peer);
+    __syncthreads();  // the next chunk reuses the shared memory
+  }
+  // Peer mode: complete this thread's stores to other ranks' memory before
+  // the kernel ends (the barrier that follows then publishes them).
+  if constexpr (kPeer) __threadfence_system();
+}
+
 __global__ void __launch_bounds__(1024) permute_cursor_rank_kernel(
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets, int32_t* cursors,
     int32_t* __restrict__ route_pos, int32_t* __restrict__ sorted_route, int routes) {
@@ -549,21 +575,23 @@ template <bool kPeer>
 cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offsets,
                          float* x_permuted, int32_t* route_pos, int32_t* sorted_route, int tokens,
                          int experts, int top_k, int hidden, void* workspace,
-                         const PeerDispatch& peer, cudaStream_t stream) {
+                         const PeerDispatch& peer, cudaStream_t stream, bool prepare = true,
+                         int max_ctas = 0) {
   if (tokens <= 0) return cudaSuccess;
   const ChunkPlan p = plan_chunks(tokens, top_k, experts);
   int32_t* cursors = static_cast<int32_t*>(workspace);
+  int32_t* table = kPeer ? peer.chunk_table : nullptr;
   const int routes_per_chunk = p.tokens_per_chunk * top_k;
   const int routes = tokens * top_k;
-  if (p.chunks > 1) {
+  if (p.chunks > 1 && prepare) {
     permute_count_kernel<<<p.chunks, kPlaceThreads, experts * sizeof(int), stream>>>(
-        ids, routes, experts, routes_per_chunk, route_pos, cursors);
+        ids, routes, experts, routes_per_chunk, route_pos, cursors, table);
     if (p.chunks <= 32 * kScanKeep) {
       permute_scan_kernel<true><<<ceil_div(experts, 32), 1024, 0, stream>>>(
-          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
+          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts, table);
     } else {
       permute_scan_kernel<false><<<ceil_div(experts, 32), 1024, 0, stream>>>(
-          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
+          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts, table);
     }
     note_launch(2);
   }
@@ -586,20 +614,30 @@ cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offs
     if (e1 != cudaSuccess) return e1;
     if (e2 != cudaSuccess) return e2;
   }
+  const int grid = (max_ctas > 0 && max_ctas < p.chunks) ? max_ctas : p.chunks;
   if (vec) {
-    permute_place_kernel<true, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
+    permute_place_kernel<true, kPeer><<<grid, kPlaceThreads, smem, stream>>>(
         x, ids, offsets, x_permuted, route_pos, sorted_route, cursors, tokens, experts, top_k,
-        hidden, p.tokens_per_chunk, peer);
+        hidden, p.tokens_per_chunk, p.chunks, table, peer);
   } else {
-    permute_place_kernel<false, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
+    permute_place_kernel<false, kPeer><<<grid, kPlaceThreads, smem, stream>>>(
         x, ids, offsets, x_permuted, route_pos, sorted_route, cursors, tokens, experts, top_k,
-        hidden, p.tokens_per_chunk, peer);
+        hidden, p.tokens_per_chunk, p.chunks, table, peer);
   }
   note_launch();
   return cudaGetLastError();
 }
 
 }  // namespace
+
+std::size_t permute_chunk_table_bytes(int tokens, int experts, int top_k) {
+  if (tokens <= 0 || experts <= 0) return 0;
+  // Below the 4096-route chunk cap a plan has at most kTargetChunks chunks;
+  // at the cap the count grows with the routes, so the largest input bounds it.
+  const ChunkPlan p = plan_chunks(tokens, top_k, experts);
+  const int chunks = p.chunks > kTargetChunks ? p.chunks : kTargetChunks;
+  return static_cast<std::size_t>(chunks) * experts * sizeof(int32_t);
+}
 
 cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32_t* offsets,
                                  float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
@@ -612,13 +650,14 @@ cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32
 cudaError_t launch_token_permute_peer(const float* x, const int32_t* ids, const int32_t* offsets,
                                       int32_t* route_pos, int tokens, int experts, int top_k,
                                       int hidden, void* workspace, const PeerDispatch& peer,
-                                      cudaStream_t stream) {
+                                      cudaStream_t stream, bool prepare, int max_ctas) {
   if (peer.x_base == nullptr || peer.ret_base == nullptr || peer.dest_off == nullptr ||
-      peer.local < 1) {
+      peer.local < 1 || (!prepare && peer.chunk_table == nullptr &&
+                         plan_chunks(tokens, top_k, experts).chunks > 1)) {
     return cudaErrorInvalidValue;
   }
   return permute_impl<true>(x, ids, offsets, nullptr, route_pos, nullptr, tokens, experts, top_k,
-                            hidden, workspace, peer, stream);
+                            hidden, workspace, peer, stream, prepare, max_ctas);
 }
 
 cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,

@@ -4,9 +4,10 @@
   rr_chain_from_tokens bit for bit, also through HostPipeline (host memory,
   calls overlapped).
 * Two or more GPUs: tests/ep_worker.py under torchrun, for both transports
-  (peer memory and NCCL) and with equal or ragged per-rank token counts
-  (one rank idle); every rank's EP output must equal its single-GPU chain bit
-  for bit (replicated hot experts, Zipf logit bias). Skipped, with the
+  (peer memory and NCCL), with equal or ragged per-rank token counts (one
+  rank idle), and for the peer transport with and without the dispatch/GEMM
+  overlap; every rank's EP output must equal its single-GPU chain bit for bit
+  (replicated hot experts, Zipf logit bias). Skipped, with the
   reason, when fewer than two GPUs are visible.
 """
 from __future__ import annotations
@@ -71,11 +72,16 @@ def test_ep_host_pipeline_matches_chain(rrlib, cuda):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
-@pytest.mark.parametrize("transport,ragged,port", [("peer", "0", 29531), ("peer", "1", 29532),
-                                                   ("nccl", "0", 29533), ("nccl", "1", 29534)])
-def test_ep_multi_gpu_matches_single_gpu_chain(rrlib, cuda, transport, ragged, port):
+@pytest.mark.parametrize("transport,ragged,overlap,port", [
+    ("peer", "0", "8", 29531), ("peer", "1", "8", 29532), ("peer", "1", "0", 29535),
+    ("nccl", "0", "8", 29533), ("nccl", "1", "8", 29534)])
+def test_ep_multi_gpu_matches_single_gpu_chain(rrlib, cuda, transport, ragged, overlap, port):
+    """overlap: SMs of the peer transport's second-half dispatch beside the
+    first half's grouped GEMM (RAGGEDROUTE_B200_EP_DISPATCH_SMS; 0 = one
+    dispatch, then one GEMM)."""
     world = min(torch.cuda.device_count(), 8)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TRANSPORT=transport, EP_RAGGED=ragged)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TRANSPORT=transport, EP_RAGGED=ragged,
+               RAGGEDROUTE_B200_EP_DISPATCH_SMS=overlap)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
            f"--master-port={port}", os.path.join(ROOT, "tests", "ep_worker.py")]
