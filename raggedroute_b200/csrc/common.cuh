@@ -122,14 +122,9 @@ struct PeerDispatch {
   // written to any rank's buffers.
   const volatile int* abort = nullptr;
   // Only routes whose local expert index (expert % local) is in
-  // [le_lo, le_hi) are sent (a dispatch split into launches by expert range).
+  // [le_lo, le_hi) are sent (a dispatch split by expert range).
   int le_lo = 0;
   int le_hi = 1 << 30;
-  // The permute's chunk table ([chunks][experts] int32,
-  // permute_chunk_table_bytes); required when the place step runs more than
-  // once per prepared table (the default table lives in route_pos and the
-  // first placement overwrites it).
-  int32_t* chunk_table = nullptr;
 };
 
 // Counts every kernel this library launches (for the bench's launch claim).
@@ -197,19 +192,20 @@ cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32
                                  int tokens, int experts, int top_k, int hidden, void* workspace,
                                  cudaStream_t stream);
 // The same permute (identical route_pos) whose copy goes to other ranks'
-// receive buffers through the peer mapping instead of to x_permuted.
-// prepare = false skips the count and scan launches and places from the
-// chunk table a previous call prepared (peer.chunk_table, kept intact);
-// max_ctas > 0 caps the place grid (a persistent loop over chunks), so a
-// placement can run beside a kernel that holds the other SMs.
+// receive buffers through the peer mapping instead of to x_permuted (only
+// the routes in peer's local-expert range).
 cudaError_t launch_token_permute_peer(const float* x, const int32_t* ids, const int32_t* offsets,
                                       int32_t* route_pos, int tokens, int experts, int top_k,
                                       int hidden, void* workspace, const PeerDispatch& peer,
-                                      cudaStream_t stream, bool prepare = true,
-                                      int max_ctas = 0);
-// Bytes of a chunk table that serves the permute of any token count up to
-// `tokens`.
-std::size_t permute_chunk_table_bytes(int tokens, int experts, int top_k);
+                                      cudaStream_t stream);
+// The rest of a split dispatch, after launch_token_permute_peer wrote
+// route_pos: the routes in peer's local-expert range are sent from `sms`
+// SMs (an even number; clusters of two CTAs, one CTA per SM) so that it can
+// run beside a grouped GEMM limited to the other SMs.
+cudaError_t launch_ep_dispatch_rest(const float* x, const int32_t* ids, const int32_t* offsets,
+                                    const int32_t* route_pos, int tokens, int experts, int top_k,
+                                    int hidden, const PeerDispatch& peer, int sms,
+                                    cudaStream_t stream);
 // Workspace-free stable permute for the low-level launcher: the expert count
 // is unknown, cursors accumulate (caller zeroes them).
 cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,

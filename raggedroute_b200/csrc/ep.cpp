@@ -26,9 +26,9 @@
 // dispatch with the GEMM: the owners' local experts are split
 // in halves; the first half is dispatched and barriered, then its GEMM runs
 // on all SMs but a few while the second half is dispatched from those few
-// SMs on a second stream, and after a barrier the second half's GEMM runs.
-// The permute's chunk table lives in a plan buffer so that both placements
-// read it; both write the same route_pos.
+// SMs on a second stream (a copy kernel that takes its positions from the
+// route_pos the permute wrote), and after a barrier the second half's GEMM
+// runs.
 // No host synchronisation inside a step; the next call (or
 // rr_ep_last_step_rows) waits for the previous step with a deadline. The
 // barriers also order steps: a rank's next dispatch cannot start before every
@@ -105,12 +105,11 @@ struct rr_ep {
   int64_t** d_ret_base = nullptr;  // [nranks] every rank's recv_ret
   float** d_y_base = nullptr;      // [nranks] every rank's y_back
   std::vector<void*> imported;     // IPC mappings to close
-  // Dispatch/GEMM overlap (peer transport): SMs left to the second half's
-  // dispatch while the first half's grouped GEMM runs (0 = no overlap), the
-  // permute's chunk table (kept intact across its two placements) and the
-  // events that order the dispatch stream (comm_stream) against the caller's.
+  // Dispatch/GEMM overlap (peer transport): SMs given to the second half's
+  // dispatch while the first half's grouped GEMM runs (0 = no overlap), and
+  // the events that order the dispatch stream (comm_stream) against the
+  // caller's.
   int overlap_sms = 0;
-  int32_t* chunk_table = nullptr;
   cudaEvent_t half0_ready = nullptr;
   cudaEvent_t half1_sent = nullptr;
   // Step bookkeeping in two slots, so that a call only waits for the step
@@ -238,7 +237,6 @@ void free_ep(rr_ep* ep) {
   if (ep->local_ready != nullptr) cudaEventDestroy(ep->local_ready);
   if (ep->half0_ready != nullptr) cudaEventDestroy(ep->half0_ready);
   if (ep->half1_sent != nullptr) cudaEventDestroy(ep->half1_sent);
-  cudaFree(ep->chunk_table);
   if (ep->combine_done != nullptr) cudaEventDestroy(ep->combine_done);
   if (ep->comm_stream != nullptr) cudaStreamDestroy(ep->comm_stream);
   if (ep->comm != nullptr) ncclCommDestroy(ep->comm);
@@ -548,16 +546,13 @@ rr_status rr_ep_create(const void* unique_id, int nranks, int rank, int router_e
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->combine_done, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->half0_ready, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ep->half1_sent, cudaEventDisableTiming);
-  if (e == cudaSuccess && nranks > 1) {
-    const std::size_t tb = rrb::permute_chunk_table_bytes(max_tokens, experts, 2);
-    if (tb > 0) e = cudaMalloc(&ep->chunk_table, tb);
-  }
   {
     // Every rank must use the same setting (it changes the sequence of
     // collectives): the variable is read once here.
     const char* v = std::getenv("RAGGEDROUTE_B200_EP_DISPATCH_SMS");
     ep->overlap_sms = v != nullptr ? std::atoi(v) : kDefaultOverlapSms;
     if (ep->overlap_sms < 0) ep->overlap_sms = 0;
+    ep->overlap_sms = (ep->overlap_sms + 1) & ~1;  // whole CTA pairs
   }
   for (int i = 0; e == cudaSuccess && i < 2; ++i) {
     e = cudaEventCreateWithFlags(&ep->step_done[i], cudaEventDisableTiming);
@@ -727,10 +722,10 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     // overlap_sms, the second half's rows go out from a persistent dispatch
     // on those SMs (on comm_stream); the second half's GEMM follows once
     // every rank's second half has landed. No kernel waits on another: the
-    // two halves meet only at NCCL barriers on the caller's stream.
+    // two halves meet only at NCCL barriers on the caller's stream. The
+    // permute places (and ranks) every route; it sends only the first half.
     const int L = ep->local;
-    const bool split = ep->overlap_sms > 0 && L >= 2 &&
-                       4 * ep->overlap_sms < rrb::sm_count() && ep->chunk_table != nullptr;
+    const bool split = ep->overlap_sms > 0 && L >= 2 && 4 * ep->overlap_sms < rrb::sm_count();
     const int half = split ? L / 2 : L;
     rrb::PeerDispatch pd;
     pd.x_base = ep->d_x_base;
@@ -741,7 +736,6 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
     pd.capacity = ep->capacity_rows;
     pd.err = ep->d_err;
     pd.abort = ep->d_abort;
-    pd.chunk_table = ep->chunk_table;
     pd.le_lo = 0;
     pd.le_hi = half;
     if (e == cudaSuccess && tokens > 0) {
@@ -765,18 +759,16 @@ rr_status rr_ep_chain_from_tokens(rr_ep* ep, const float* x, const float* router
       if (e == cudaSuccess && tokens > 0) {
         pd.le_lo = half;
         pd.le_hi = L;
-        e = rrb::launch_token_permute_peer(x, expert_ids, offsets, route_pos, tokens, E, 2, K,
-                                           ctx->workspace, pd, ep->comm_stream,
-                                           /*prepare=*/false, ep->overlap_sms);
+        e = rrb::launch_ep_dispatch_rest(x, expert_ids, offsets, route_pos, tokens, E, 2, K, pd,
+                                         ep->overlap_sms, ep->comm_stream);
       }
       if (e == cudaSuccess) e = cudaEventRecord(ep->half1_sent, ep->comm_stream);
       if (e != cudaSuccess) return st(RR_CUDA_ERROR, "EP second-half dispatch launch failed", e);
       // The first half's GEMM walks a static tile schedule, so all of its
-      // CTA pairs must be resident together: a dispatch CTA can leave its
-      // SM's GPC with an odd number of free SMs, so every dispatch SM is
-      // counted as a lost pair (2 SMs).
+      // CTA pairs must be resident beside the dispatch (which takes whole
+      // SM pairs, so every GPC keeps an even number of free SMs).
       rrb::RowScatter sc0 = sc;
-      sc0.max_ctas = rrb::sm_count() - 2 * ep->overlap_sms;
+      sc0.max_ctas = rrb::sm_count() - ep->overlap_sms;
       e = rrb::launch_grouped_gemm(ep->recv_x, local_expert_weights, ep->recv_offsets,
                                    ep->y_back, half, static_cast<int>(ep->capacity_rows), K, N,
                                    stream, 0, &sc0);

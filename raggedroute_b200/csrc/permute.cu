@@ -90,14 +90,10 @@ __device__ __forceinline__ unsigned same_key_lanes(unsigned key, int nbits) {
   return m;
 }
 
-// Row c of the chunk table: row c of `table` when the caller provides one
-// (the expert-parallel dispatch, which places in two launches and so must
-// not lose the table to the first), else the first E entries of chunk c's
-// slice of route_pos, or the cursors for the last chunk.
-__device__ __forceinline__ int32_t* chunk_row(int32_t* table, int32_t* route_pos,
-                                              int32_t* cursors, int c, int chunks,
-                                              int routes_per_chunk, int experts) {
-  if (table != nullptr) return table + static_cast<long long>(c) * experts;
+// Row c of the chunk table: the first E entries of chunk c's slice of
+// route_pos, or the cursors for the last chunk.
+__device__ __forceinline__ int32_t* chunk_row(int32_t* route_pos, int32_t* cursors, int c,
+                                              int chunks, int routes_per_chunk) {
   return c == chunks - 1 ? cursors
                          : route_pos + static_cast<long long>(c) * routes_per_chunk;
 }
@@ -105,7 +101,7 @@ __device__ __forceinline__ int32_t* chunk_row(int32_t* table, int32_t* route_pos
 // Per-chunk histogram into the chunk's table row.
 __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
     const int32_t* __restrict__ ids, int routes, int experts, int routes_per_chunk,
-    int32_t* route_pos, int32_t* cursors, int32_t* table) {
+    int32_t* route_pos, int32_t* cursors) {
   extern __shared__ int hist[];
   for (int i = threadIdx.x; i < experts; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -123,8 +119,7 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_count_kernel(
     if (lane == warp_leader(peers) && valid) atomicAdd(hist + e, __popc(peers));
   }
   __syncthreads();
-  int32_t* row = chunk_row(table, route_pos, cursors, blockIdx.x, gridDim.x, routes_per_chunk,
-                           experts);
+  int32_t* row = chunk_row(route_pos, cursors, blockIdx.x, gridDim.x, routes_per_chunk);
   for (int i = threadIdx.x; i < experts; i += blockDim.x) row[i] = hist[i];
 }
 
@@ -140,7 +135,7 @@ template <bool kKeep>
 __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, int32_t* cursors,
                                                             const int32_t* __restrict__ offsets,
                                                             int chunks, int routes_per_chunk,
-                                                            int experts, int32_t* table) {
+                                                            int experts) {
   __shared__ int part[32][33];
   const int lane = threadIdx.x & 31;
   const int grp = threadIdx.x >> 5;
@@ -149,9 +144,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t* route_pos, 
   const int c0 = grp * per;
   const int c1 = min(chunks, c0 + per);
   constexpr int kBatch = 8;  // loads in flight per lane on the two-pass path
-  auto row = [&](int c) {
-    return chunk_row(table, route_pos, cursors, c, chunks, routes_per_chunk, experts);
-  };
+  auto row = [&](int c) { return chunk_row(route_pos, cursors, c, chunks, routes_per_chunk); };
   int keep[kKeep ? kScanKeep : 1];
   int sum = 0;
   if (e < experts) {
@@ -305,8 +298,7 @@ __device__ __forceinline__ void place_chunk(
     int chunk, int chunks, int* smem, const int& aborted, const float* __restrict__ x,
     const int32_t* __restrict__ ids, const int32_t* __restrict__ offsets, float* __restrict__ xp,
     int32_t* route_pos, int32_t* __restrict__ sorted_route, int32_t* cursors, int tokens,
-    int experts, int top_k, int hidden, int tokens_per_chunk, int32_t* table,
-    const PeerDispatch& peer) {
+    int experts, int top_k, int hidden, int tokens_per_chunk, const PeerDispatch& peer) {
   int* warp_base = smem;                            // [kPlaceWarps][experts]
   int* pos = smem + kPlaceWarps * experts;          // [routes in chunk]
   // Peer mode: packed (owner << 40 | receive row) per route, -1 = dropped.
@@ -353,9 +345,8 @@ __device__ __forceinline__ void place_chunk(
   // here, before pass 2 overwrites this chunk's slice of route_pos).
   const bool chunked = chunks > 1;
   const bool last = chunk == chunks - 1;
-  const int32_t* row = chunked ? chunk_row(table, route_pos, cursors, chunk, chunks,
-                                           tokens_per_chunk * top_k, experts)
-                               : offsets;
+  const int32_t* row =
+      chunked ? chunk_row(route_pos, cursors, chunk, chunks, tokens_per_chunk * top_k) : offsets;
   for (int e = threadIdx.x; e < experts; e += blockDim.x) {
     int run = row[e];
 #pragma unroll
@@ -488,21 +479,72 @@ __global__ void __launch_bounds__(kPlaceThreads) permute_place_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ offsets, float* __restrict__ xp, int32_t* route_pos,
     int32_t* __restrict__ sorted_route, int32_t* cursors, int tokens, int experts, int top_k,
-    int hidden, int tokens_per_chunk, int chunks, int32_t* table, const PeerDispatch peer) {
+    int hidden, int tokens_per_chunk, int chunks, const PeerDispatch peer) {
   extern __shared__ int smem[];
   __shared__ int aborted;
   if (threadIdx.x == 0) aborted = (kPeer && peer.abort != nullptr) ? *peer.abort : 0;
-  // One chunk per CTA, or a persistent loop when the grid is capped (a
-  // dispatch that runs beside the grouped GEMM on a few SMs).
+  // One chunk per CTA (the loop covers a grid smaller than the plan).
   for (int c = blockIdx.x; c < chunks; c += gridDim.x) {
     place_chunk<kVec, kPeer>(c, chunks, smem, aborted, x, ids, offsets, xp, route_pos,
                              sorted_route, cursors, tokens, experts, top_k, hidden,
-                             tokens_per_chunk, table, peer);
+                             tokens_per_chunk, peer);
     __syncthreads();  // the next chunk reuses the shared memory
   }
   // Peer mode: complete this thread's stores to other ranks' memory before
   // the kernel ends (the barrier that follows then publishes them).
   if constexpr (kPeer) __threadfence_system();
+}
+
+// The rest of a split expert-parallel dispatch: every route whose local
+// expert index (expert % local) lies in [peer.le_lo, peer.le_hi) is sent to
+// its owner at the position the permute already wrote to route_pos (so no
+// ranking here), with its return address. One warp per token, grid-stride,
+// meant for a few CTAs beside the grouped GEMM. top_k <= 8.
+constexpr int kRestThreads = 1024;
+// Dynamic shared memory each CTA asks for (unused): more than half an SM's,
+// so no two CTAs of this kernel, and no GEMM CTA, share an SM.
+constexpr int kRestSmem = 120 * 1024;
+
+template <bool kVec>
+__global__ void __launch_bounds__(kRestThreads) ep_dispatch_rest_kernel(
+    const float* __restrict__ x, const int32_t* __restrict__ ids,
+    const int32_t* __restrict__ offsets, const int32_t* __restrict__ route_pos, int tokens,
+    int experts, int top_k, int hidden, const PeerDispatch peer) {
+  __shared__ int aborted;
+  if (threadIdx.x == 0) aborted = peer.abort != nullptr ? *peer.abort : 0;
+  __syncthreads();
+  if (aborted) return;
+  const int lane = threadIdx.x & 31;
+  const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long t = warp; t < tokens; t += nwarps) {
+    float* dst[8];
+    for (int k = 0; k < top_k; ++k) {
+      dst[k] = nullptr;
+      const long long r = t * top_k + k;
+      const int e = __ldg(ids + r);
+      if (e < 0 || e >= experts) continue;
+      const int le = e % peer.local;
+      if (le < peer.le_lo || le >= peer.le_hi) continue;
+      const int p = __ldg(route_pos + r);
+      const int owner = e / peer.local;
+      const long long row =
+          static_cast<long long>(__ldg(peer.dest_off + e)) + (p - __ldg(offsets + e));
+      if (row >= peer.capacity) {
+        if (lane == 0) raise_device_error(peer.err, kErrEpCapacity);
+        continue;
+      }
+      if (lane == 0) {
+        peer.ret_base[owner][row] =
+            (static_cast<long long>(peer.me) << kPeerRankShift) | static_cast<long long>(p);
+      }
+      dst[k] = peer.x_base[owner] + row * hidden;
+    }
+    copy_row_warp_to<kVec>(x + t * hidden, dst, top_k, hidden);
+  }
+  // Complete this thread's stores to other ranks' memory before the kernel
+  // ends (the barrier that follows then publishes them).
+  __threadfence_system();
 }
 
 __global__ void __launch_bounds__(1024) permute_cursor_rank_kernel(
@@ -575,23 +617,21 @@ template <bool kPeer>
 cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offsets,
                          float* x_permuted, int32_t* route_pos, int32_t* sorted_route, int tokens,
                          int experts, int top_k, int hidden, void* workspace,
-                         const PeerDispatch& peer, cudaStream_t stream, bool prepare = true,
-                         int max_ctas = 0) {
+                         const PeerDispatch& peer, cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
   const ChunkPlan p = plan_chunks(tokens, top_k, experts);
   int32_t* cursors = static_cast<int32_t*>(workspace);
-  int32_t* table = kPeer ? peer.chunk_table : nullptr;
   const int routes_per_chunk = p.tokens_per_chunk * top_k;
   const int routes = tokens * top_k;
-  if (p.chunks > 1 && prepare) {
+  if (p.chunks > 1) {
     permute_count_kernel<<<p.chunks, kPlaceThreads, experts * sizeof(int), stream>>>(
-        ids, routes, experts, routes_per_chunk, route_pos, cursors, table);
+        ids, routes, experts, routes_per_chunk, route_pos, cursors);
     if (p.chunks <= 32 * kScanKeep) {
       permute_scan_kernel<true><<<ceil_div(experts, 32), 1024, 0, stream>>>(
-          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts, table);
+          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
     } else {
       permute_scan_kernel<false><<<ceil_div(experts, 32), 1024, 0, stream>>>(
-          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts, table);
+          route_pos, cursors, offsets, p.chunks, routes_per_chunk, experts);
     }
     note_launch(2);
   }
@@ -614,30 +654,20 @@ cudaError_t permute_impl(const float* x, const int32_t* ids, const int32_t* offs
     if (e1 != cudaSuccess) return e1;
     if (e2 != cudaSuccess) return e2;
   }
-  const int grid = (max_ctas > 0 && max_ctas < p.chunks) ? max_ctas : p.chunks;
   if (vec) {
-    permute_place_kernel<true, kPeer><<<grid, kPlaceThreads, smem, stream>>>(
+    permute_place_kernel<true, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
         x, ids, offsets, x_permuted, route_pos, sorted_route, cursors, tokens, experts, top_k,
-        hidden, p.tokens_per_chunk, p.chunks, table, peer);
+        hidden, p.tokens_per_chunk, p.chunks, peer);
   } else {
-    permute_place_kernel<false, kPeer><<<grid, kPlaceThreads, smem, stream>>>(
+    permute_place_kernel<false, kPeer><<<p.chunks, kPlaceThreads, smem, stream>>>(
         x, ids, offsets, x_permuted, route_pos, sorted_route, cursors, tokens, experts, top_k,
-        hidden, p.tokens_per_chunk, p.chunks, table, peer);
+        hidden, p.tokens_per_chunk, p.chunks, peer);
   }
   note_launch();
   return cudaGetLastError();
 }
 
 }  // namespace
-
-std::size_t permute_chunk_table_bytes(int tokens, int experts, int top_k) {
-  if (tokens <= 0 || experts <= 0) return 0;
-  // Below the 4096-route chunk cap a plan has at most kTargetChunks chunks;
-  // at the cap the count grows with the routes, so the largest input bounds it.
-  const ChunkPlan p = plan_chunks(tokens, top_k, experts);
-  const int chunks = p.chunks > kTargetChunks ? p.chunks : kTargetChunks;
-  return static_cast<std::size_t>(chunks) * experts * sizeof(int32_t);
-}
 
 cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32_t* offsets,
                                  float* x_permuted, int32_t* route_pos, int32_t* sorted_route,
@@ -650,14 +680,51 @@ cudaError_t launch_token_permute(const float* x, const int32_t* ids, const int32
 cudaError_t launch_token_permute_peer(const float* x, const int32_t* ids, const int32_t* offsets,
                                       int32_t* route_pos, int tokens, int experts, int top_k,
                                       int hidden, void* workspace, const PeerDispatch& peer,
-                                      cudaStream_t stream, bool prepare, int max_ctas) {
+                                      cudaStream_t stream) {
   if (peer.x_base == nullptr || peer.ret_base == nullptr || peer.dest_off == nullptr ||
-      peer.local < 1 || (!prepare && peer.chunk_table == nullptr &&
-                         plan_chunks(tokens, top_k, experts).chunks > 1)) {
+      peer.local < 1) {
     return cudaErrorInvalidValue;
   }
   return permute_impl<true>(x, ids, offsets, nullptr, route_pos, nullptr, tokens, experts, top_k,
-                            hidden, workspace, peer, stream, prepare, max_ctas);
+                            hidden, workspace, peer, stream);
+}
+
+cudaError_t launch_ep_dispatch_rest(const float* x, const int32_t* ids, const int32_t* offsets,
+                                    const int32_t* route_pos, int tokens, int experts, int top_k,
+                                    int hidden, const PeerDispatch& peer, int sms,
+                                    cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  if (peer.x_base == nullptr || peer.ret_base == nullptr || peer.dest_off == nullptr ||
+      peer.local < 1 || top_k < 1 || top_k > 8 || sms < 2) {
+    return cudaErrorInvalidValue;
+  }
+  const bool vec = hidden % 4 == 0 && aligned_to(x, 16);
+  const void* fn = vec ? reinterpret_cast<const void*>(ep_dispatch_rest_kernel<true>)
+                       : reinterpret_cast<const void*>(ep_dispatch_rest_kernel<false>);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kRestSmem);
+  if (e != cudaSuccess) return e;
+  // Clusters of two CTAs: the SMs taken come in pairs inside a GPC, so every
+  // GPC keeps an even number of free SMs for the GEMM's CTA pairs.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+  cfg.blockDim = dim3(kRestThreads);
+  cfg.dynamicSmemBytes = kRestSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = vec ? cudaLaunchKernelEx(&cfg, ep_dispatch_rest_kernel<true>, x, ids, offsets, route_pos,
+                               tokens, experts, top_k, hidden, peer)
+          : cudaLaunchKernelEx(&cfg, ep_dispatch_rest_kernel<false>, x, ids, offsets, route_pos,
+                               tokens, experts, top_k, hidden, peer);
+  if (e != cudaSuccess) return e;
+  note_launch();
+  return cudaGetLastError();
 }
 
 cudaError_t launch_token_permute_cursor(const float* x, const int32_t* ids,
