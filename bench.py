@@ -484,6 +484,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if ep is not None:
         ep.close()
+    plain = None
+    if ep is not None and not args.no_extras:
+        plain = ep_plain_sharding(torch, dist, rr, args, inp, tokens, k, e, n, world, rank,
+                                  device, stream, ctx)
     extras = {}
     if separate is not None:
         extras["separate_unpermute"] = separate
@@ -569,6 +573,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     line.update(extras)
     if ep_info is not None:
         line["ep"] = ep_info
+        line["config"]["placement"] = {
+            "experts_per_gpu_plain": e // world,
+            "virtual_experts": ep_info["virtual_experts"],
+            "virtual_experts_per_gpu": ep_info["virtual_experts_per_rank"],
+            "replicas_of_hottest": ep_info["replicas_of_hottest"],
+            "rule": "hot experts replicated, copies placed by LPT (the timed value); BASELINE's "
+                    "plain sharding is timed beside it under ep_plain_sharding",
+            "transport": ep_info["transport"]}
+        if plain is not None:
+            line["ep_plain_sharding"] = plain
         line["roofline"]["note"] = ("per-GPU stage pass of the single-GPU chain on rank 0's "
                                     "tokens (same kernels), untimed region")
     if world == 1 and not args.no_cpu_baseline:
@@ -594,6 +608,51 @@ def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) 
         times.append(evs[idx].elapsed_time(evs[idx + 1]))
     return {"stage": args.only_stage, "tokens": tokens, "ms": statistics.mean(times),
             "ms_min": min(times)}
+
+
+def ep_plain_sharding(torch, dist, rr, args, inp, tokens, k, e, n, world, rank, device, stream,
+                      ctx) -> dict:
+    """BASELINE C5's plain expert sharding (experts [g*E/N, (g+1)*E/N) on GPU g,
+    no replicas), timed like the main value: warm-up, barrier, K steps
+    between CUDA events on the launching stream, max over ranks."""
+    from raggedroute_b200.ep import ExpertParallel
+    local = e // world
+    w = inp.expert_w[rank * local:(rank + 1) * local].contiguous()
+    plan = ExpertParallel(e, tokens, k, n, timeout_s=300.0, router_experts=e,
+                          transport=args.ep_transport)
+    b = rr.ChainBuffers.allocate(tokens, k, e, n, device, router_experts=e)
+
+    def one_step():
+        plan.chain_from_tokens(inp.x, inp.router_w, w, b, logit_bias=inp.logit_bias, ctx=ctx)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            one_step()
+    stream.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a0.record(stream)
+        for _ in range(args.steps):
+            one_step()
+        a1.record(stream)
+    a1.synchronize()
+    t = torch.tensor([a0.elapsed_time(a1)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    _, received = plan.last_step_rows()
+    rows = torch.tensor([received], device=device, dtype=torch.float64)
+    gathered = [torch.zeros_like(rows) for _ in range(world)]
+    dist.all_gather(gathered, rows)
+    per_rank = [int(g.item()) for g in gathered]
+    plan.close()
+    del b, w
+    return {"placement": f"experts [g*{local}, (g+1)*{local}) on GPU g, no replicas",
+            "tokens_per_s": round(tokens * world / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+            "rows_received_per_rank": per_rank,
+            "measured_imbalance": round(max(per_rank) / (sum(per_rank) / world), 4)}
 
 
 def run_c3_permute(spec: str) -> dict:
