@@ -976,8 +976,12 @@ def _run_ref_chain(ref, x, wr, bias, we, threads):
     return y
 
 
-def cpu_baseline(inp, steps: int = 1, sample_tokens: int = 32) -> dict:
-    """The reference CPU chain on a bounded token sample (rank 0, N=1)."""
+def cpu_baseline(inp, steps: int = 1, sample_tokens: int = 256) -> dict:
+    """The reference CPU chain on a bounded token sample (rank 0, N=1), timed
+    at the sample size and at half of it: every stage's work is linear in the
+    tokens (the GEMMs are per-token products, the routing stages per-route
+    passes), so equal per-token times at both sizes support extrapolating to
+    the full batch."""
     ref = _ref_lib()
     threads = os.cpu_count() or 1
     x = inp.x[:sample_tokens].contiguous().cpu()
@@ -986,15 +990,23 @@ def cpu_baseline(inp, steps: int = 1, sample_tokens: int = 32) -> dict:
     for _ in range(steps):
         _run_ref_chain(ref, x, wr, bias, we, threads)
     dt = (time.perf_counter() - t0) / steps
+    half = max(1, sample_tokens // 2)
+    th = time.perf_counter()
+    _run_ref_chain(ref, x[:half].contiguous(), wr, bias, we, threads)
+    dth = time.perf_counter() - th
     # The reference oracle as shipped is single-threaded: the same chain on
     # one host thread, on a smaller sample.
-    one = max(1, sample_tokens // 8)
+    one = max(1, sample_tokens // 16)
     t1 = time.perf_counter()
     _run_ref_chain(ref, x[:one].contiguous(), wr, bias, we, 1)
     dt1 = time.perf_counter() - t1
     return {"value": sample_tokens / dt, "unit": UNIT, "cores": threads, "kind": "reference",
             "sample": f"{sample_tokens} tokens of C5 per step through the reference's CPU "
-                      f"functions (oracle/_ref), {threads} host threads",
+                      f"functions (oracle/_ref), {threads} host threads, "
+                      f"{dt:.1f} s of CPU work; the full batch is {C5_TOKENS} tokens",
+            "linearity": {"tokens_per_s_at_sample": round(sample_tokens / dt, 2),
+                          "tokens_per_s_at_half_sample": round(half / dth, 2),
+                          "half_sample_tokens": half},
             "one_core": {"value": one / dt1, "unit": UNIT, "cores": 1,
                          "sample": f"{one} tokens of C5, 1 host thread"}}
 
@@ -1010,7 +1022,7 @@ def run_reference(args, rank: int) -> dict | None:
         return None
     ref = _ref_lib()
     threads = os.cpu_count() or 1
-    sample = int(os.environ.get("RR_REF_SAMPLE_TOKENS", "32"))
+    sample = int(os.environ.get("RR_REF_SAMPLE_TOKENS", "256"))
     x, wr, bias, we = _sample_inputs(sample)
     for _ in range(args.warmup):
         _run_ref_chain(ref, x, wr, bias, we, threads)
