@@ -107,6 +107,35 @@ def test_topk_special_modes(rrlib, oracle, cuda, mode):
     _topk_check(rrlib, oracle, cuda, x)
 
 
+@pytest.mark.parametrize("experts", [4, 8, 64, 128, 256, 1024])
+@pytest.mark.parametrize("tokens", [16384, 40001])
+@pytest.mark.parametrize("biased", [False, True])
+def test_topk_large_batches(rrlib, oracle, cuda, experts, tokens, biased):
+    """Batches of 16384 rows and more take the bulk-copy kernel (rows staged
+    in shared memory in chunks of 24 KB): ids bit-exact and weights within
+    the reference's 1e-6 against the oracle, with ties, NaN rows, infinities
+    and signed zeros spread over the chunks and a ragged last chunk."""
+    rng = np.random.default_rng(experts * 7 + tokens + biased)
+    x = rng.standard_normal((tokens, experts)).astype(np.float32)
+    x[::3] = np.round(x[::3] * 2) / 2
+    x[5::97] = NAN
+    x[7::89, experts // 2] = INF
+    x[11::83, 0] = -INF
+    x[13::79, :] = -0.0
+    x[17::71, experts - 1] = 0.0
+    bias = rng.standard_normal(experts).astype(np.float32) if biased else None
+    ids = torch.full((tokens, 2), -9, dtype=torch.int32, device=cuda)
+    w = torch.empty(tokens, 2, dtype=torch.float32, device=cuda)
+    if biased:
+        rrlib.topk_gate_biased(dev(x, cuda), dev(bias, cuda), ids, w, tokens, experts)
+    else:
+        rrlib.topk_gate(dev(x, cuda), ids, w, tokens, experts)
+    ids_ref, w_ref = oracle.top2_f32(x, bias)
+    assert np.array_equal(host(ids), ids_ref)
+    ok, err, _ = oracle.compare_floating(host(w), w_ref, 1e-6, 1e-6)
+    assert ok, err
+
+
 def test_topk_c2_logits(rrlib, oracle, cuda):
     from raggedroute_b200.workloads import c2_logits
     _topk_check(rrlib, oracle, cuda, c2_logits())
