@@ -889,6 +889,11 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float) -> dict:
     pos = torch.empty(routes, dtype=torch.int32, device=device)
     srt = torch.empty(routes, dtype=torch.int32, device=device)
     c3 = {}
+    # The floor of one launch in a graph: a one-expert scan (one tiny kernel).
+    one_c = torch.ones(1, dtype=torch.int32, device=device)
+    one_o = torch.empty(2, dtype=torch.int32, device=device)
+    floor_us = _event_us(torch, rr, stream, lambda c: rr.exclusive_scan(one_c, one_o, 1, ctx=c), 50)
+    out["launch_floor_us"] = round(floor_us, 2)
     for e in C3["experts"]:
         counts = torch.empty(e, dtype=torch.int32, device=device)
         offsets = torch.empty(e + 1, dtype=torch.int32, device=device)
@@ -909,8 +914,12 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float) -> dict:
             def frac(b, us):
                 return round(b / (us * 1e-6) / 1e9 / hbm_gbs, 3)
 
+            # Above 256K routes the histogram is a memset and one kernel, the
+            # fused operator a memset and two kernels.
             entry = {
                 "histogram_us": round(hist, 2), "histogram_hbm_frac": frac(hist_b, hist),
+                "histogram_hbm_frac_above_launch_floor":
+                    frac(hist_b, max(hist - 2 * floor_us, 1e-3)),
                 "exclusive_scan_us": round(scan, 2),
                 "histogram_exclusive_scan_us": round(fused, 2),
                 "histogram_exclusive_scan_hbm_frac": frac(fused_b, fused)}
