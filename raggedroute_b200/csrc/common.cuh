@@ -241,6 +241,13 @@ cudaError_t launch_grouped_gemm_simt(const float* x, const float* w, const int32
                                      const RowScatter* scatter = nullptr,
                                      const RowGather* gather = nullptr);
 bool tc_gemm_supported(const float* x, const float* w, const float* y, int hidden, int output);
+// Dense GEMM with N <= 128 computed transposed (gemm_narrow.cu): y[rows,
+// output] = x . w, x [rows, hidden], w [hidden, output]; hidden and output
+// multiples of 4, 16-byte aligned buffers. cudaErrorNotSupported when the
+// kernel cannot be configured. RAGGEDROUTE_B200_NARROW_DENSE=0 turns it off.
+bool dense_narrow_enabled();
+cudaError_t launch_dense_narrow(const float* x, const float* w, float* y, int rows, int hidden,
+                                int output, cudaStream_t stream);
 // CTA-pair engine (gemm_pair.cu) for the plain grouped/dense GEMM: 256 x 256
 // tiles on two SMs. cudaErrorNotSupported when no pair can be scheduled.
 bool gemm_pairs_enabled();

@@ -677,6 +677,13 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
                                    cudaStream_t stream, int weight_sets,
                                    const RowScatter* scatter, const RowGather* gather) {
   const int wsets = weight_sets > 0 ? weight_sets : experts;
+  // One group with at most 128 output columns and enough rows to fill every
+  // SM twice (the router GEMM): the transposed narrow kernel.
+  if (offsets == nullptr && gather == nullptr && scatter == nullptr && output <= kBN / 2 &&
+      rows >= 2LL * kBM * sm_count() && dense_narrow_enabled()) {
+    const cudaError_t ne = launch_dense_narrow(x, w, y, rows, hidden, output, stream);
+    if (ne != cudaErrorNotSupported) return ne;
+  }
   EncodeTiledFn encode = encode_fn();
   if (encode == nullptr) return cudaErrorNotSupported;
   if (!kernel_configured()) return cudaErrorNotSupported;

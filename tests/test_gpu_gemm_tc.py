@@ -196,6 +196,30 @@ def test_dense_tc_two_tiles_per_cta(rrlib, oracle, cuda, m, n, k):
     assert device_error_word(rrlib) == 0
 
 
+@pytest.mark.parametrize("m,n,k", [(65536, 128, 4096), (50003, 60, 512)])
+def test_dense_narrow_router_shapes(rrlib, oracle, cuda, m, n, k):
+    """Dense GEMMs with N <= 128 and rows for two waves of tiles take the
+    transposed narrow kernel (token tiles of 224 at C5's router shape,
+    65536 x 4096 x 128; a ragged row count and N = 60 with a shifted last
+    tile): 2048 sampled rows plus the first and last against the FP64
+    oracle, elementwise within the accumulation-aware bound and normwise
+    within 1e-5."""
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m + n)
+    a = torch.randn(m, k, generator=g, device=cuda)
+    b = torch.randn(k, n, generator=g, device=cuda) / math.sqrt(k)
+    c = torch.full((m, n), float("nan"), device=cuda)
+    rrlib.dense_gemm(a, b, c, m, n, k)
+    torch.cuda.synchronize()
+    assert not torch.isnan(c).any()
+    rng = np.random.default_rng(m)
+    rows = np.unique(np.concatenate([[0, m - 1], rng.choice(m, 2048, replace=False)]))
+    sel = torch.from_numpy(rows).to(cuda)
+    a_s, c_s, b_h = host(a[sel]), host(c[sel]), host(b)
+    check(oracle, c_s, a_s, b_h, oracle.dense_gemm_f64(a_s, b_h), k)
+    assert device_error_word(rrlib) == 0
+
+
 def test_integer_tf32_rounding_matches_cvt(rrlib, cuda):
     """The split rounds to TF32 with integer adds on the bit pattern; it must
     equal cvt.rna.tf32.f32 for every non-NaN input: random bit patterns over
