@@ -168,6 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
           }
           tc_fence_after();
           const int kend = min(num_kb, kc + kChunkKb);
+          // A tile's first chunk accumulates straight into S; later chunks
+          // go to P and are promoted (see the grouped engine).
+          const uint32_t dacc = tmem + (kc == 0 ? kColS : kColP);
           for (int kb = kc; kb < kend; ++kb) {
             if (!mbar_wait(&s.op_full[stage], phase, err, failed) ||
                 !mbar_wait(&s.raw_full[rstage], rphase, err, failed)) {
@@ -187,9 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
               const uint64_t xh = smem_desc(raw + ks * 32, 16, 512, Swizzle::k64B);
               const uint64_t xl = smem_desc(op + ks * 32, 16, 512, Swizzle::k64B);
               const uint32_t first = (kb == kc && ks == 0) ? 0u : 1u;
-              mma_tf32(tmem + kColP, wl, xh, idesc, first);
-              mma_tf32(tmem + kColP, wh, xl, idesc, 1u);
-              mma_tf32(tmem + kColP, wh, xh, idesc, 1u);
+              mma_tf32(dacc, wl, xh, idesc, first);
+              mma_tf32(dacc, wh, xl, idesc, 1u);
+              mma_tf32(dacc, wh, xh, idesc, 1u);
             }
             mma_commit(&s.op_empty[stage]);
             mma_commit(&s.raw_empty[rstage]);
@@ -203,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
             }
           }
           if (!ok) break;
+          if (kc == 0 && kend < num_kb) continue;  // no promotion of the first chunk
           mma_commit(&s.tmem_full);
           acc_phase ^= 1u;
         }
@@ -293,7 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
           if (c_begin + c >= tm) break;  // warp-uniform
           const uint32_t col = static_cast<uint32_t>(c_begin + c);
           uint32_t p[16];
-          tmem_ld_32x32b_x16(tmem + kColP + col + lane_addr, p);
+          // A first chunk reaches here only when it is also the last: its sum
+          // is in S.
+          tmem_ld_32x32b_x16(tmem + (pending_first ? kColS : kColP) + col + lane_addr, p);
           if (!pending_first) {
             uint32_t q[16];
             tmem_ld_32x32b_x16(tmem + kColS + col + lane_addr, q);
@@ -325,7 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
         pending = false;
       }
       if (!have_block) break;
-      if ((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) {
+      // A chunk that ends here is promoted next iteration, except a tile's
+      // first chunk when more follow (it was accumulated into S directly).
+      if (((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) &&
+          !(kb < kChunkKb && kb + 1 < num_kb)) {
         pending = true;
         pending_first = kb < kChunkKb;
         pending_last = (kb + 1 == num_kb);

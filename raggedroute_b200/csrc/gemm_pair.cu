@@ -28,8 +28,11 @@
 //   warps 2-17 workers: split A lo and this CTA's B hi/lo (B transposed to
 //              K-major, conflict-free) into the stage, then arrive on the
 //              EVEN CTA's op_full (32 arrivals: 16 warps of each CTA); promote
-//              P into the running sum S every 512 of K exactly as the one-CTA
-//              engine does, and arrive on the even CTA's tmem_empty. Arrivals
+//              P into the running sum S every 512 of K as the one-CTA engine
+//              does (except that a tile's first chunk is accumulated into S
+//              directly, which saves its copy and one MMA stall per tile;
+//              the sums are the same bit for bit), and arrive on the even
+//              CTA's tmem_empty. Arrivals
 //              on the other CTA's barriers use the default (CTA-scope release)
 //              form: a cluster-scope release is a memory barrier per arrival,
 //              which measured as the dominant stall.
@@ -206,7 +209,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + kColP;
+          // A tile's first chunk accumulates straight into S (it would only
+          // be copied there); later chunks go to P and are promoted into S.
+          // Before the second chunk the wait above passes at once: nothing
+          // was committed after the first, and P is free since the previous
+          // tile's epilogue.
+          const uint32_t d = tmem + (kc == 0 ? kColS : kColP);
           const int kend = min(num_kb, kc + kChunkKb);
           for (int kb = kc; kb < kend; ++kb) {
             if (!wait(&s.op_full[stage], phase)) {
@@ -239,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
             }
           }
           if (!ok) break;
+          if (kc == 0 && kend < num_kb) continue;  // no promotion of the first chunk
           mma_commit_pair_to(tmem_full_local);
           mma_commit_pair_to(tmem_full_peer);
           acc_phase ^= 1u;
@@ -340,7 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
           if (c_begin + c >= pg.n_mma) break;  // warp-uniform
           const uint32_t col = static_cast<uint32_t>(c_begin + c);
           uint32_t p[16];
-          tmem_ld_32x32b_x16(tmem + kColP + col + lane_addr, p);
+          // A first chunk reaches here only when it is also the last: its sum
+          // is in S.
+          tmem_ld_32x32b_x16(tmem + (pending_first ? kColS : kColP) + col + lane_addr, p);
           if (!pending_first) {
             uint32_t q[16];
             tmem_ld_32x32b_x16(tmem + kColS + col + lane_addr, q);
@@ -397,8 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
         pending = false;
       }
       if (!have_block) break;
-      // The k-block just split ends a chunk: it is promoted next iteration.
-      if ((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) {
+      // A chunk that ends here is promoted next iteration, except a tile's
+      // first chunk when more follow (it was accumulated into S directly).
+      if (((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) &&
+          !(kb < kChunkKb && kb + 1 < num_kb)) {
         pending = true;
         pending_first = kb < kChunkKb;
         pending_last = (kb + 1 == num_kb);
