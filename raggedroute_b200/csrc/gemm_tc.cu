@@ -59,8 +59,9 @@
 //              With row gathering the raw A tile is unswizzled, so A hi is
 //              written to the operand slot too and the workers release the
 //              raw slot as soon as they have read it.
-//              (b) promotion: S = P, S += P, or y = S + P for the tile's last
-//              chunk, each thread covering 64 columns of one TMEM lane.
+//              (b) promotion: S += P, or y = S + P for the tile's last chunk
+//              (a tile's first chunk is accumulated into S directly), each
+//              thread covering 64 columns of one TMEM lane.
 //              Promotion of chunk c runs after the first k-block of the next
 //              chunk has been split, so the MMA resumes at once.
 // A partial last m-tile of an expert is loaded shifted back so it ends at the
@@ -327,7 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + kColP;
+          // A tile's first chunk accumulates straight into S (it would only
+          // be copied there); later chunks go to P and are promoted. Before
+          // the second chunk the wait above passes at once (nothing was
+          // committed after the first; P is free since the last epilogue).
+          const uint32_t d = tmem + (kc == 0 ? kColS : kColP);
           const int kend = min(num_kb, kc + kChunkKb);
           for (int kb = kc; kb < kend; ++kb) {
             if (!mbar_wait(&s.op_full[stage], phase, err, failed) ||
@@ -372,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
             }
           }
           if (!ok) break;
+          if (kc == 0 && kend < num_kb) continue;  // no promotion of the first chunk
           mma_commit(&s.tmem_full);
           acc_phase ^= 1u;
         }
@@ -523,7 +529,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
           if (lc0 + c >= pg.n_mma) break;  // warp-uniform
           const uint32_t col = static_cast<uint32_t>(c_begin + c);
           uint32_t p[16];
-          tmem_ld_32x32b_x16(tmem + kColP + col + lane_addr, p);
+          // A first chunk reaches here only when it is also the last: its sum
+          // is in S.
+          tmem_ld_32x32b_x16(tmem + (pending_first ? kColS : kColP) + col + lane_addr, p);
           if (!pending_first) {
             uint32_t q[16];
             tmem_ld_32x32b_x16(tmem + kColS + col + lane_addr, q);
@@ -580,8 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_tc_kernel(
         pending = false;
       }
       if (!have_block) break;
-      // The k-block just split ends a chunk: it is promoted next iteration.
-      if ((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) {
+      // A chunk that ends here is promoted next iteration, except a tile's
+      // first chunk when more follow (it was accumulated into S directly).
+      if (((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) &&
+          !(kb < kChunkKb && kb + 1 < num_kb)) {
         pending = true;
         pending_first = kb < kChunkKb;
         pending_last = (kb + 1 == num_kb);
