@@ -41,9 +41,11 @@
 // either CTA exits, its producer waits until the pair's MMAs released every
 // stage it filled (no tensor-core read of, or commit into, an exited CTA's
 // shared memory), and both CTAs meet at a cluster barrier before freeing TMEM.
-// A 256-row tile pads a ragged expert's last tile further than a 128-row one;
-// tiles are scheduled on the device from offsets (tile_sched.cuh), with the
-// last m-tile of an expert shifted back to end at the segment end.
+// A 256-row tile pads a ragged expert's last tile further than a 128-row one,
+// so a last m-tile that stores at most 128 rows is issued as M = 128 (64 rows
+// per CTA, half the tensor-core time); tiles are scheduled on the device from
+// offsets (tile_sched.cuh), with the last m-tile of an expert shifted back to
+// end at the segment end.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
     return mbar_wait_pair(bar, parity, err, failed, peer_failed);
   };
   auto geom = [&](int t) {
-    return tile_geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output, kTileM, kTileN);
+    return tile_geom(t, offsets, experts, rows, s.prefix, n_tiles_n, output, kTileM, kTileN, true);
   };
 
   if (warp == 0) {
@@ -162,7 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
       uint32_t phase = 0;
       for (int t = unit; t < total && !*failed; t += units) {
         const TileGeom g = geom(t);
-        const int arow = g.base + static_cast<int>(rank) * kRows;
+        // CTA r holds rows [r*m/2, (r+1)*m/2) of the tile (m = 256, or 128
+        // for a half tail tile, of whose 128-row box the MMA reads the first
+        // 64 rows).
+        const int arow = g.base + static_cast<int>(rank) * (g.m_mma >> 1);
         const int bcol = g.col0 + static_cast<int>(rank) * (g.n_mma >> 1);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!wait(&s.empty[stage], phase ^ 1u)) break;
@@ -202,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
       const uint32_t tmem_full_peer = mapa_shared(tmem_full_local, 1u);
       for (int t = unit; t < total && ok && !*failed; t += units) {
         const TileGeom g = geom(t);
-        const uint32_t idesc = idesc_tf32(kTileM, g.n_mma, false, false);
+        const uint32_t idesc = idesc_tf32(g.m_mma, g.n_mma, false, false);
         for (int kc = 0; kc < num_kb && ok; kc += kChunkKb) {
           if (!wait(&s.tmem_empty, acc_phase ^ 1u)) {
             ok = false;
@@ -328,25 +333,35 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
         // Promotion of the finished chunk in P (this CTA's 128 rows).
         if (!wait(&s.tmem_full, acc_phase)) break;
         tc_fence_after();
-        const int c_begin = cgroup * kEpiCols;
-        const int row = pg.base + static_cast<int>(rank) * kRows + quarter * 32 + lane;
+        // A full tile holds this CTA's 128 rows x n_mma columns in TMEM lanes
+        // 0-127. A half tile (M = 128: 64 rows per CTA) is folded: lanes 0-63
+        // hold columns [0, n_mma/2) of the 64 rows, lanes 64-127 columns
+        // [n_mma/2, n_mma), in TMEM columns [0, n_mma/2).
+        const bool half = pg.m_mma < kTileM;
+        const int width = half ? (pg.n_mma >> 1) : pg.n_mma;  // TMEM columns in use
+        const int epi = half ? kEpiCols / 2 : kEpiCols;
+        const int c_begin = cgroup * epi;
+        const int col_base = half ? (quarter >> 1) * width : 0;
+        const int row = pg.base + static_cast<int>(rank) * (pg.m_mma >> 1) +
+                        (half ? (quarter & 1) * 32 : quarter * 32) + lane;
         bool store_row = pending_last && row >= pg.row0 && row < pg.row_end;
-        float* out = y + static_cast<long long>(row) * output + pg.col0 + c_begin;
+        float* out = y + static_cast<long long>(row) * output + pg.col0 + col_base + c_begin;
         float wgt = 0.0f;
         if (scatter.dst != nullptr && store_row) {
           float* dst_row = s.no_scatter ? nullptr : scatter_row(scatter, row, output);
           store_row = dst_row != nullptr;
-          out = dst_row + pg.col0 + c_begin;
+          out = dst_row + pg.col0 + col_base + c_begin;
         } else if (scatter.combine != nullptr && store_row) {
-          out = combine_row(scatter, row, output, wgt) + pg.col0 + c_begin;
+          out = combine_row(scatter, row, output, wgt) + pg.col0 + col_base + c_begin;
         }
         // 128-bit stores where the row start allows them (caller-owned
         // scatter bases and combine targets need not be 16-byte aligned).
         const bool vrow = vec && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-        const int w = pg.ncols - c_begin;  // columns of this group to store
+        // Columns of this group to store.
+        const int w = min(width, pg.ncols - col_base) - c_begin;
 #pragma unroll
         for (int c = 0; c < kEpiCols; c += 16) {
-          if (c_begin + c >= pg.n_mma) break;  // warp-uniform
+          if (c >= epi || c_begin + c >= width) break;  // warp-uniform
           const uint32_t col = static_cast<uint32_t>(c_begin + c);
           uint32_t p[16];
           // A first chunk reaches here only when it is also the last: its sum
@@ -499,7 +514,9 @@ cudaError_t launch_grouped_gemm_pair(const float* x, const float* w, const int32
   int units = grouped_gemm_pair_units();
   if (encode == nullptr || units <= 0) return cudaErrorNotSupported;
   // A: x [rows, hidden] row-major, one CTA's 128 rows per box. Shifted last
-  // tiles never read at or past the last segment end.
+  // tiles read no row of a full tile at or past the last segment end; the
+  // odd CTA's box of a half tile may reach past `rows` (zero-filled, and
+  // beyond the 64 rows its MMA reads).
   const long long a_rows = rows > 0 ? rows : (1LL << 31) - 1;
   CUtensorMap ma{}, mb{};
   {

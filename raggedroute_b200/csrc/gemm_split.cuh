@@ -9,22 +9,26 @@
 namespace rrb {
 
 struct TileGeom {
-  int expert, row0, row_end, base, col0, ncols, n_mma;
+  int expert, row0, row_end, base, col0, ncols, n_mma, m_mma;
 };
 
 // Geometry of tile t of a schedule with tile_m x tile_n tiles. A partial last
 // m-tile of an expert is shifted back to end at the segment end (base), so
 // TMA never reads a row at or beyond offsets[E]; rows before row0 are
 // computed but not stored. n_mma is the tile's width rounded up to 16.
+// m_mma is the tile's height: tile_m, or tile_m / 2 for a last m-tile that
+// stores at most tile_m / 2 rows when half_tail is set (the CTA-pair engine's
+// M = 128 instruction).
 __device__ __forceinline__ TileGeom tile_geom(int t, const int32_t* offsets, int experts, int rows,
                                               const int* prefix, int n_tiles_n, int output,
-                                              int tile_m, int tile_n) {
+                                              int tile_m, int tile_n, bool half_tail = false) {
   const TileCoord c = tile_coord(t, offsets, experts, rows, prefix, tile_m, tile_n, n_tiles_n);
   TileGeom g;
   g.expert = c.expert;
   g.row0 = c.row0;
   g.row_end = c.row_end;
-  g.base = (c.row0 + tile_m > c.row_end) ? c.row_end - tile_m : c.row0;
+  g.m_mma = (half_tail && c.row_end - c.row0 <= tile_m / 2) ? tile_m / 2 : tile_m;
+  g.base = (c.row0 + g.m_mma > c.row_end) ? c.row_end - g.m_mma : c.row0;
   g.col0 = c.col0;
   g.ncols = min(tile_n, output - c.col0);
   g.n_mma = (g.ncols + 15) & ~15;

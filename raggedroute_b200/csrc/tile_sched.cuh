@@ -92,7 +92,14 @@ __device__ __forceinline__ TileCoord tile_coord(int t, const int32_t* __restrict
   }
   const int local = t - prefix[e];
   const int mt = local / n_tiles_n;
-  const int ntile = local - mt * n_tiles_n;
+  // The n-tiles of one row block are visited in an order rotated by the
+  // block's global index t / n_tiles_n (prefix[e] is a multiple of
+  // n_tiles_n, so this permutes tiles within a row block only). A persistent
+  // CTA that takes every units-th tile would otherwise see only the n-tiles
+  // congruent to its own index modulo gcd(units, n_tiles_n): with 74 CTA
+  // pairs and 6 n-tiles (N = 1408), the narrower last n-tile would fall to
+  // the odd pairs only, and the even pairs would carry ~10% more work.
+  const int ntile = (local - mt * n_tiles_n + t / n_tiles_n) % n_tiles_n;
   TileCoord c;
   c.expert = e;
   const int base = offsets != nullptr ? __ldg(offsets + e) : 0;

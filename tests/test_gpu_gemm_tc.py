@@ -89,6 +89,36 @@ def test_grouped_tc(rrlib, oracle, cuda, sizes, k, n):
     assert device_error_word(rrlib) == 0
 
 
+@pytest.mark.parametrize("n", [8, 20, 40, 264, 1408])
+def test_grouped_tc_half_tail_tiles(rrlib, oracle, cuda, n):
+    """A last m-tile of an expert that stores at most 128 rows runs as an
+    M = 128 pair MMA whose accumulator is folded across the TMEM lanes (64
+    rows per CTA, columns [0, n/2) in lanes 0-63 and [n/2, n) in lanes
+    64-127). Remainders 1, 64, 127, 128 of a 256-row tile take it, 129 and
+    255 do not; every width, including half widths that are not a multiple
+    of 16 (n = 40: 24 columns per half) and a 8-column last n-tile."""
+    sizes = np.array([1, 64, 127, 128, 129, 255, 257, 384, 385, 612, 0, 3], np.int32)
+    k = 64
+    rng = np.random.default_rng(n)
+    e = sizes.size
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
+    r = int(offsets[-1])
+    x = rng.uniform(-1, 1, (r, k)).astype(np.float32)
+    w = rng.normal(0, 1 / math.sqrt(k), (e, k, n)).astype(np.float32)
+    dx, dw = dev(x, cuda), dev(w, cuda)
+    y = torch.full((r + 8, n), float("nan"), device=cuda)
+    rrlib.grouped_gemm(dx, dw, dev(offsets, cuda), y, e, k, n, r)
+    got = host(y)
+    ref = oracle.grouped_gemm_f64(x, w, offsets)
+    for i in range(e):
+        s = slice(offsets[i], offsets[i + 1])
+        if offsets[i + 1] > offsets[i]:
+            check(oracle, got[s], x[s], w[i], ref[s], k)
+    assert not np.isnan(got[:r]).any()
+    assert np.isnan(got[r:]).all()
+    assert device_error_word(rrlib) == 0
+
+
 def test_grouped_tc_rows_outside_segments_untouched(rrlib, cuda):
     """Rows past offsets[E] keep their previous contents."""
     k, n = 32, 64
