@@ -251,6 +251,9 @@ cudaError_t launch_dense_narrow(const float* x, const float* w, float* y, int ro
 // CTA-pair engine (gemm_pair.cu) for the plain grouped/dense GEMM: 256 x 256
 // tiles on two SMs. cudaErrorNotSupported when no pair can be scheduled.
 bool gemm_pairs_enabled();
+// Whether the pair engine runs the mixed split (TF32 hi.hi plus bfloat16
+// corrections) for this K; RAGGEDROUTE_B200_GEMM_MIXED=0 keeps 3xTF32.
+bool gemm_mixed_split(int hidden);
 int grouped_gemm_pair_units();
 cudaError_t launch_grouped_gemm_pair(const float* x, const float* w, const int32_t* offsets,
                                      float* y, int experts, int rows, int hidden, int output,

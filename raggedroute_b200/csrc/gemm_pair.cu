@@ -1,7 +1,24 @@
 // Ragged grouped GEMM on CTA pairs (tcgen05.mma.cta_group::2, sm_100a), with
-// the same 3xTF32 split and FP32 contract as the one-CTA engine (gemm_tc.cu):
+// the FP32 contract of the one-CTA engine (gemm_tc.cu):
 // y[r, :] = x[r, :] . W[e] for r in [offsets[e], offsets[e+1]), rows outside
 // every segment untouched; offsets == nullptr is one group of `rows` rows.
+//
+// Two operand splits, one instantiation each:
+// * 3xTF32 (kMixed = false; K < 128, or RAGGEDROUTE_B200_GEMM_MIXED=0): the
+//   one-CTA engine's split, lo.hi + hi.lo + hi.hi in TF32, bit-identical to
+//   it.
+// * mixed (kMixed = true, the default from K = 128 up): hi.hi in TF32 (A hi =
+//   trunc_tf32(a), read by the MMA from the raw tile; B hi = rna_tf32(b)),
+//   plus two correction products in bfloat16, lo(A).B and hi(A).lo(B), with
+//   lo(A) = a - hi(A) and lo(B) = b - hi(B) exact in FP32 and every
+//   bfloat16 operand rounded to nearest. A kind::f16 MMA runs at twice the
+//   kind::tf32 rate, so the three products cost two TF32 steps of tensor time
+//   instead of three (measured at C5: 7.39 -> 6.72 ms per launch). The
+//   three products sum every part of a.b; the bfloat16 rounding of the
+//   corrections leaves at most about 2^-18 of |a||b| per product (typically
+//   far less, with random sign), within the accumulation-aware bound
+//   4*K*2^-24 of sums of 128 terms and more, and the chain holds 1e-5
+//   normwise against FP64 at C5.
 //
 // Why pairs. The one-CTA engine moves, per SM and 16-wide k-block of a
 // 128 x 256 tile, 24 KB in by TMA, 24 KB through the split's reads, 40 KB of
@@ -20,7 +37,8 @@
 //              and B columns [col0 + rank*n/2, +n/2) of the tile (N-major,
 //              unswizzled) per k-block into the stage; no multicast.
 //   warp 1     even CTA: MMA issuer, 3 x tcgen05.mma.cta_group::2 (M=256,
-//              N=tile width, K=8) per k-step into P; A hi is the raw A tile
+//              N=tile width, K=8) per k-step into P (mixed split: 2 TF32
+//              K=8 and 2 bfloat16 K=16 per k-block); A hi is the raw A tile
 //              itself (the MMA reads FP32 bits as TF32 by truncation). One
 //              commit to each CTA's `empty` barrier releases a stage in both,
 //              one to each CTA's `tmem_full` hands P to both CTAs' workers.
@@ -86,6 +104,22 @@ constexpr int kOffBHi = 3 * kABytes;
 constexpr int kOffBLo = kOffBHi + kBBytes;
 constexpr int kStageBytes = kOffBLo + kBBytes;
 
+// Mixed split (kMixed): the same 40 KB re-cut as raw A | raw B half | B hi
+// half (TF32) | A lo | A | B half | B lo half (bfloat16, 4 KB each).
+constexpr int kA16Bytes = kRows * kBK * 2;
+constexpr int kB16Bytes = kHalfN * kBK * 2;
+constexpr int kOffMBHi = 2 * kABytes;
+constexpr int kOffMALo = kOffMBHi + kBBytes;
+constexpr int kOffMA = kOffMALo + kA16Bytes;
+constexpr int kOffMB = kOffMA + kA16Bytes;
+constexpr int kOffMBLo = kOffMB + kB16Bytes;
+static_assert(kOffMBLo + kB16Bytes == kStageBytes, "the mixed split fills the same stage");
+// Below this K the mixed split's per-product error (about 2^-18 of |a||b|
+// at worst, from the bfloat16 rounding of the correction operands) could
+// exceed the accumulation-aware bound 4*K*2^-24 of short sums; the 3xTF32
+// split runs there.
+constexpr int kMixedMinK = 128;
+
 struct alignas(1024) PairSmem {
   uint8_t stage[kStages][kStageBytes];
   uint64_t raw_full[kStages];  // this CTA's TMA bytes of the stage landed
@@ -105,6 +139,7 @@ constexpr std::size_t kPairSmemBytes = sizeof(PairSmem) + 1024;
 static_assert(kPairSmemBytes <= 227 * 1024, "over the 227 KB of shared memory a CTA may use");
 static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KB alignment of the swizzled tiles");
 
+template <bool kMixed>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
     const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
     const int32_t* __restrict__ offsets, float* __restrict__ y, int experts, int rows,
@@ -208,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
       for (int t = unit; t < total && ok && !*failed; t += units) {
         const TileGeom g = geom(t);
         const uint32_t idesc = idesc_tf32(g.m_mma, g.n_mma, false, false);
+        const uint32_t idesc16 = idesc_bf16(g.m_mma, g.n_mma);
         for (int kc = 0; kc < num_kb && ok; kc += kChunkKb) {
           if (!wait(&s.tmem_empty, acc_phase ^ 1u)) {
             ok = false;
@@ -228,6 +264,24 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
             }
             tc_fence_after();
             const uint32_t base = smem_u32(s.stage[stage]);
+            if constexpr (kMixed) {
+              // hi.hi in TF32 (two K=8 steps), then the corrections lo(A).B
+              // and A.lo(B) in bfloat16 (one K=16 step each, at twice the
+              // TF32 rate): two TF32 steps' worth of tensor time, not three.
+#pragma unroll
+              for (int ks = 0; ks < kBK / 8; ++ks) {
+                const uint64_t ah =
+                    smem_desc(base + kOffARaw + ks * 32, 16, 512, Swizzle::k64B);
+                const uint64_t bh =
+                    smem_desc(base + kOffMBHi + ks * 32, 16, 512, Swizzle::k64B);
+                mma_tf32_pair(d, ah, bh, idesc, (kb == kc && ks == 0) ? 0u : 1u);
+              }
+              // 32-byte rows, 8-row groups 256 B apart.
+              mma_bf16_pair(d, smem_desc(base + kOffMALo, 16, 256, Swizzle::k32B),
+                            smem_desc(base + kOffMB, 16, 256, Swizzle::k32B), idesc16, 1u);
+              mma_bf16_pair(d, smem_desc(base + kOffMA, 16, 256, Swizzle::k32B),
+                            smem_desc(base + kOffMBLo, 16, 256, Swizzle::k32B), idesc16, 1u);
+            } else {
 #pragma unroll
             for (int ks = 0; ks < kBK / 8; ++ks) {
               // K-major, 64-byte swizzle: 8-row groups 512 B apart; the
@@ -242,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
               mma_tf32_pair(d, al, bh, idesc, first);
               mma_tf32_pair(d, ah, bl, idesc, 1u);
               mma_tf32_pair(d, ah, bh, idesc, 1u);
+            }
             }
             const uint32_t e = smem_u32(&s.empty[stage]);
             mma_commit_pair_to(e);
@@ -283,6 +338,24 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
 #pragma unroll
     for (int j = 0; j < 4; ++j) bsrc[j] = static_cast<uint32_t>((4 * bkc + j) * (kHalfN * 4) + bn * 4);
     const uint32_t bdst = static_cast<uint32_t>(kmajor64_offset(bn, bkc));
+    // Mixed split: worker warps 0-7 take B (column mbn of this CTA's half, k
+    // rows 8*mkh..+7: eight 128-byte row reads per warp, 16-byte bfloat16
+    // chunks that fill all 32 banks), warps 8-15 take A (the 16-byte chunks
+    // ca and ca + 256 of the raw tile, each written as two 8-byte bfloat16
+    // halves at the same row and k of the 32-byte-swizzled tiles).
+    const int mbn = (tid & 31) + ((ew >> 1) << 5);
+    const int mkh = ew & 1;
+    const uint32_t mb_src = static_cast<uint32_t>(8 * mkh * (kHalfN * 4) + mbn * 4);
+    const uint32_t mb_hi0 = static_cast<uint32_t>(kmajor64_offset(mbn, 2 * mkh));
+    const uint32_t mb_hi1 = static_cast<uint32_t>(kmajor64_offset(mbn, 2 * mkh + 1));
+    const uint32_t mb_16 = static_cast<uint32_t>(kmajor32_offset(mbn, mkh));
+    const int ca = tid & 255;
+    auto a16_offset = [](int c) {
+      const int r = c >> 2;
+      const int kc = (c & 3) ^ ((r >> 1) & 3);  // logical 4-float chunk of the raw row
+      return static_cast<uint32_t>(kmajor32_offset(r, kc >> 1) + ((kc & 1) << 3));
+    };
+    const uint32_t ma_16[2] = {a16_offset(ca), a16_offset(ca + 256)};
     int stage = 0;
     uint32_t phase = 0, acc_phase = 0;
     bool pending = false, pending_first = false, pending_last = false;
@@ -299,6 +372,49 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
       if (have_block) {
         if (!wait(&s.raw_full[stage], phase)) break;
         const uint32_t st = smem_u32(s.stage[stage]);
+        if constexpr (kMixed) {
+          if (ew < 8) {
+            // B: hi = rna_tf32(v) for the TF32 product; v and lo = v - hi
+            // (exact) rounded to bfloat16 for the correction products.
+            if (mbn < (((g.n_mma >> 1) + 31) & ~31)) {  // warp-uniform
+              float v[8], hi[8];
+              uint32_t p16[4], l16[4];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                v[j] = lds_f32(st + kOffBRaw + mb_src + j * (kHalfN * 4));
+                hi[j] = tf32_rna(v[j]);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                p16[j] = bf16x2_rn(v[2 * j], v[2 * j + 1]);
+                l16[j] = bf16x2_rn(v[2 * j] - hi[2 * j], v[2 * j + 1] - hi[2 * j + 1]);
+              }
+              sts_v4(st + kOffMBHi + mb_hi0, make_float4(hi[0], hi[1], hi[2], hi[3]));
+              sts_v4(st + kOffMBHi + mb_hi1, make_float4(hi[4], hi[5], hi[6], hi[7]));
+              sts_v4_u32(st + kOffMB + mb_16, p16[0], p16[1], p16[2], p16[3]);
+              sts_v4_u32(st + kOffMBLo + mb_16, l16[0], l16[1], l16[2], l16[3]);
+            }
+          } else {
+            // A: the MMA reads hi = trunc_tf32(v) from the raw tile; lo = v -
+            // hi (exact) and hi itself go to the bfloat16 tiles, so that
+            // hi.hi + lo(A).B + hi(A).lo(B) sums every part of the product.
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const float4 av = lds_v4(st + kOffARaw + (ca + 256 * i) * 16);
+              float4 h, l;
+              split_trunc4(av, h, l);
+              sts_v2_u32(st + kOffMALo + ma_16[i], bf16x2_rn(l.x, l.y), bf16x2_rn(l.z, l.w));
+              sts_v2_u32(st + kOffMA + ma_16[i], bf16x2_rn(h.x, h.y), bf16x2_rn(h.z, h.w));
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(op_full_leader + stage * 8);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        } else {
         // Columns of this CTA's half that the MMA reads (warp-uniform test).
         const bool b_used = bn < (((g.n_mma >> 1) + 31) & ~31);
         const float4 av = lds_v4(st + kOffARaw + tid * 16);
@@ -327,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
+        }
         }
       }
       if (pending) {
@@ -464,7 +581,11 @@ bool pair_kernel_configured() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [] {
-    ok = cudaFuncSetAttribute(grouped_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ok = cudaFuncSetAttribute(grouped_gemm_pair_kernel<false>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kPairSmemBytes)) == cudaSuccess &&
+         cudaFuncSetAttribute(grouped_gemm_pair_kernel<true>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kPairSmemBytes)) == cudaSuccess;
     if (!ok) cudaGetLastError();
   });
@@ -488,6 +609,14 @@ cudaLaunchConfig_t pair_config(int units, cudaStream_t stream, cudaLaunchAttribu
 
 }  // namespace
 
+bool gemm_mixed_split(int hidden) {
+  static const bool enabled = [] {
+    const char* v = std::getenv("RAGGEDROUTE_B200_GEMM_MIXED");
+    return v == nullptr || v[0] != '0';
+  }();
+  return enabled && hidden >= kMixedMinK;
+}
+
 int grouped_gemm_pair_units() {
   static std::once_flag once;
   static int units = 0;
@@ -496,7 +625,8 @@ int grouped_gemm_pair_units() {
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = pair_config(sm_count(), nullptr, attr);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_pair_kernel, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_pair_kernel<false>, &cfg) !=
+        cudaSuccess) {
       cudaGetLastError();
       n = 0;
     }
@@ -557,9 +687,12 @@ cudaError_t launch_grouped_gemm_pair(const float* x, const float* w, const int32
   if (sc.max_ctas > 0 && units > sc.max_ctas / 2) units = sc.max_ctas / 2 > 0 ? sc.max_ctas / 2 : 1;
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pair_config(units, stream, attr);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel, ma, mb, offsets, y,
-                                           experts, rows, hidden, output, wsets,
-                                           device_error_word(), sc);
+  const cudaError_t e =
+      gemm_mixed_split(hidden)
+          ? cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<true>, ma, mb, offsets, y, experts,
+                               rows, hidden, output, wsets, device_error_word(), sc)
+          : cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<false>, ma, mb, offsets, y,
+                               experts, rows, hidden, output, wsets, device_error_word(), sc);
   if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();

@@ -67,4 +67,12 @@ __device__ __forceinline__ int kmajor64_offset(int r, int kc) {
   return r * 64 + ((kc ^ ((r >> 1) & 3)) << 4);
 }
 
+// Byte offset of 16-byte chunk c (k = 8*c..8*c+7) of row r in a K-major tile
+// of 16 bfloat16 per row (32 bytes) with the 32-byte swizzle: address bit 4
+// is flipped by bit 7 (row bit 2), the layout the tcgen05 descriptor's
+// 32-byte swizzle mode reads.
+__device__ __forceinline__ int kmajor32_offset(int r, int c) {
+  return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
+}
+
 }  // namespace rrb

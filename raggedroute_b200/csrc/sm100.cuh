@@ -189,6 +189,25 @@ __device__ __forceinline__ void sts_v4(uint32_t addr, float4 v) {
                : "memory");
 }
 
+__device__ __forceinline__ void sts_v2_u32(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+__device__ __forceinline__ void sts_v4_u32(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                           uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// Two floats rounded to bfloat16 (to nearest, ties to even) and packed: `lo`
+// in the low half (the lower address in memory), `hi` in the high half.
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // ---- TMA (cp.async.bulk.tensor, no multicast) -------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -325,6 +344,18 @@ __device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, 
       : "memory");
 }
 
+// The same for kind::f16 operands (both bfloat16 per the instruction
+// descriptor), FP32 accumulation into the same TMEM layout as kind::tf32.
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on the mbarrier at shared::cluster address `cluster_addr`
 // (this CTA's or the peer's) when every pair MMA issued so far by this thread
 // has completed. One commit per barrier: a stage or accumulator shared by the
@@ -417,6 +448,16 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn_major,
          | (static_cast<uint32_t>(b_mn_major) << 16)  // B major
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+}
+
+// Instruction descriptor for kind::f16 with bfloat16 A and B (both K-major)
+// and FP32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4)                                // D format: F32
+         | (1u << 7)                              // A format: BF16
+         | (1u << 10)                             // B format: BF16
+         | (static_cast<uint32_t>(n >> 3) << 17)  // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24); // M / 16
 }
 
 // ---- TF32 split --------------------------------------------------------------------
