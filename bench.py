@@ -170,6 +170,12 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def gemm_mixed_split(hidden: int) -> bool:
+    """Whether the CTA-pair grouped GEMM runs the mixed split at this K (the
+    library's rule: K >= 128 unless RAGGEDROUTE_B200_GEMM_MIXED=0)."""
+    return hidden >= 128 and os.environ.get("RAGGEDROUTE_B200_GEMM_MIXED", "1")[:1] != "0"
+
+
 def measure_tf32_peak(torch, device) -> float:
     """cuBLAS TF32 GEMM throughput (TFLOP/s) on this GPU, 8192^3, best of 10.
     The 3xTF32 roofline is this figure / 3."""
@@ -501,10 +507,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     peaks = load_peaks()
     tf32 = measure_tf32_peak(torch, device)
-    # The 3xTF32 ceiling from the measured dense bf16 peak: TF32 runs at half
-    # the bf16 rate on this part and the split issues three MMAs per product.
+    # Ceilings from the measured dense bf16 peak, in bf16-MMA units per
+    # product (TF32 runs at half the bf16 rate on this part): the mixed split
+    # the grouped GEMM runs (hi.hi in TF32 = 2 units, two bfloat16 corrections
+    # = 2 units) is bf16 / 4; the 3xTF32 split (3 TF32 products = 6 units),
+    # kept for reference and for the one-CTA engine, is bf16 / 6.
+    mixed = gemm_mixed_split(k)
+    div = 4.0 if mixed else 6.0
     peak_3x = float(peaks["bf16_tflops"]) / 6.0
-    peak_3x_sustained = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])) / 6.0
+    peak_split = float(peaks["bf16_tflops"]) / div
+    peak_split_sustained = float(peaks.get("bf16_tflops_sustained",
+                                           peaks["bf16_tflops"])) / div
     gemm_flops = 2.0 * routes * k * n
     gemm_ms = stage_ms["grouped_gemm"]
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
@@ -526,7 +539,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         stage_bytes["token_permute"] += 4.0 * routes
         stage_bytes["grouped_gemm"] = 4.0 * (routes * k + e * k * n + tokens * n) + 8.0 * routes
     if world == 1 and not args.no_extras:
-        extras["configs"] = config_sweep(torch, rr, device, hbm, peak_3x)
+        extras["configs"] = config_sweep(torch, rr, device, hbm, peak_3x,
+                                         float(peaks["bf16_tflops"]))
         extras["prepared_weights"] = prepared_weights_pass(
             torch, rr, stream, inp, buf, tokens, max(3, args.steps), gemm_flops, peak_3x)
     stages = {}
@@ -536,7 +550,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         entry = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3)}
         if nm == "grouped_gemm":
             entry["TFLOP/s"] = round(achieved, 2)
-            entry["tensor_frac_3xtf32"] = round(achieved / peak_3x, 3)
+            entry["tensor_frac"] = round(achieved / peak_split, 3)
+            entry["split"] = "mixed (TF32 hi.hi + bf16 corrections)" if mixed else "3xTF32"
         if nm == "dense_gemm":
             df = 2.0 * tokens * k * e / (ms * 1e-3) / 1e12
             entry["TFLOP/s"] = round(df, 2)
@@ -547,18 +562,24 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 GEMMs)",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": ("f32 (grouped GEMM: TF32 hi.hi + bf16 corrections; router GEMM: 3xTF32)"
+                  if mixed else "f32 (3xTF32 GEMMs)"),
         "data": "synthetic (seeded; BASELINE C5 shapes and distributions)",
         "config": workload_config(tokens, world),
         "roofline": {"bound": "tensor", "kernel": "grouped_gemm", "achieved": round(achieved, 2),
-                     "peak": round(peak_3x, 2), "unit": "TFLOP/s",
-                     "frac": round(achieved / peak_3x, 4),
-                     "peak_source": ("MEASURED_PEAKS bf16_tflops %.1f (%s) / 2 (TF32 rate) / 3 "
-                                     "(MMAs per product)" % (float(peaks["bf16_tflops"]),
-                                                             peaks["source"])),
-                     "frac_of_sustained": round(achieved / peak_3x_sustained, 4),
+                     "peak": round(peak_split, 2), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak_split, 4),
+                     "peak_source": (
+                         ("MEASURED_PEAKS bf16_tflops %.1f (%s) / 4 (mixed split: one TF32 "
+                          "product at half the bf16 rate + two bf16 products)"
+                          if mixed else
+                          "MEASURED_PEAKS bf16_tflops %.1f (%s) / 2 (TF32 rate) / 3 "
+                          "(MMAs per product)") % (float(peaks["bf16_tflops"]), peaks["source"])),
+                     "frac_of_sustained": round(achieved / peak_split_sustained, 4),
+                     "frac_of_3xtf32_ceiling": round(achieved / peak_3x, 4),
                      "cublas_tf32_live_tflops": round(tf32, 1),
-                     "frac_of_cublas_tf32_over_3": round(achieved / (tf32 / 3.0), 4),
+                     "frac_of_cublas_tf32_ceiling": round(achieved / (tf32 / (div / 2.0)), 4),
                      "traffic": load_traffic("grouped_gemm")},
         "stages": stages,
         "clocks": clock_info,
@@ -849,7 +870,7 @@ def _event_us(torch, rr, stream, fn, iters: int) -> float:
     return a.elapsed_time(b) * 1e3 / iters
 
 
-def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float) -> dict:
+def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float, bf16_tflops: float) -> dict:
     """The BASELINE parity configs C3 and C4 timed on their own (warm L2 as in
     the reference's protocol; device time per call from a captured graph of
     back-to-back calls, see _event_us).
@@ -942,8 +963,10 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float) -> dict:
     gemm = _event_us(torch, rr, stream,
                      lambda c: rr.grouped_gemm(a, w, offsets, y, e, k, n, r, ctx=c), 20)
     tflops = 2.0 * r * k * n / (gemm * 1e-6) / 1e12
+    c4_mixed = gemm_mixed_split(k)
     out["C4"] = {"grouped_gemm_us": round(gemm, 2), "TFLOP/s": round(tflops, 2),
-                 "tensor_frac_3xtf32": round(tflops / peak_3x, 3),
+                 "tensor_frac": round(tflops / (bf16_tflops / (4.0 if c4_mixed else 6.0)), 3),
+                 "split": "mixed" if c4_mixed else "3xTF32",
                  "note": "W (256 MiB) and Xp (128 MiB) partly L2-resident between calls"}
     return out
 
