@@ -316,7 +316,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 events[i + 1].record(stream)
 
     if args.only_stage is not None:
-        return run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n)
+        return run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n, buf)
     if args.profile_once:
         return run_profile_once(torch, rr, stream, ctx, inp, buf, tokens, e)
 
@@ -611,7 +611,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     return line
 
 
-def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) -> dict:
+def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n, buf) -> dict:
     """Runs the whole chain once (untimed setup), then `steps` launches of one
     stage through the same C ABI call the chain uses; reports its mean time.
     Meant as a small, single-kernel command for Nsight Compute."""
@@ -627,8 +627,17 @@ def run_only_stage(args, torch, rr, stream, step, stage_names, tokens, e, k, n) 
             step(evs, only=idx)
         stream.synchronize()
         times.append(evs[idx].elapsed_time(evs[idx + 1]))
+    counts = buf.counts.cpu()
+    nonempty = int((counts > 0).sum())
+    rows = int(counts.sum())
+    # Algorithmic DRAM bytes of the fused grouped GEMM at this size: x_permuted
+    # rows and the weights of the experts that have rows read once, y written
+    # once, route and weight read per row (so a capture's traffic can be set
+    # against its own size).
+    gemm_bytes = 4.0 * (rows * k + nonempty * k * n + tokens * n) + 8.0 * rows
     return {"stage": args.only_stage, "tokens": tokens, "ms": statistics.mean(times),
-            "ms_min": min(times)}
+            "ms_min": min(times), "rows": rows, "nonempty_experts": nonempty,
+            "grouped_gemm_algorithmic_bytes": gemm_bytes}
 
 
 def ep_plain_sharding(torch, dist, rr, args, inp, tokens, k, e, n, world, rank, device, stream,
