@@ -250,12 +250,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
             break;
           }
           tc_fence_after();
-          // A tile's first chunk accumulates straight into S (it would only
-          // be copied there); later chunks go to P and are promoted into S.
-          // Before the second chunk the wait above passes at once: nothing
-          // was committed after the first, and P is free since the previous
-          // tile's epilogue.
-          const uint32_t d = tmem + (kc == 0 ? kColS : kColP);
+          // Every chunk accumulates into P and is promoted into S (a tile's
+          // first chunk by a copy). P is free once the previous chunk's
+          // promotion has read it; the previous tile's stores from S then
+          // run beside this chunk's MMAs.
+          const uint32_t d = tmem + kColP;
           const int kend = min(num_kb, kc + kChunkKb);
           for (int kb = kc; kb < kend; ++kb) {
             if (!wait(&s.op_full[stage], phase)) {
@@ -307,7 +306,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
             }
           }
           if (!ok) break;
-          if (kc == 0 && kend < num_kb) continue;  // no promotion of the first chunk
           mma_commit_pair_to(tmem_full_local);
           mma_commit_pair_to(tmem_full_peer);
           acc_phase ^= 1u;
@@ -359,6 +357,56 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
     int stage = 0;
     uint32_t phase = 0, acc_phase = 0;
     bool pending = false, pending_first = false, pending_last = false;
+    // Stores of a finished tile's y from S still to do: the next column
+    // offset within this thread's 64 columns, or -1.
+    int epi_c = -1, epi_cb = 0, epi_width = 0, epi_w = 0;
+    bool epi_store = false, epi_vrow = false;
+    float* epi_out = nullptr;
+    float epi_wgt = 0.0f;
+    auto epi_step = [&]() {
+      const int c = epi_c;
+      uint32_t p[16];
+      tmem_ld_32x32b_x16(tmem + kColS + static_cast<uint32_t>(epi_cb + c) + lane_addr, p);
+      tmem_ld_wait();
+      float* const out = epi_out;
+      const int w = epi_w;
+      if (epi_store && scatter.combine != nullptr) {
+        if (epi_vrow) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            if (c + j < w) {
+              red_add_v4_f32(out + c + j, __fmul_rn(epi_wgt, __uint_as_float(p[j])),
+                             __fmul_rn(epi_wgt, __uint_as_float(p[j + 1])),
+                             __fmul_rn(epi_wgt, __uint_as_float(p[j + 2])),
+                             __fmul_rn(epi_wgt, __uint_as_float(p[j + 3])));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (c + j < w) red_add_f32(out + c + j, __fmul_rn(epi_wgt, __uint_as_float(p[j])));
+          }
+        }
+      } else if (epi_store) {
+        if (epi_vrow) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            if (c + j < w) {
+              *reinterpret_cast<float4*>(out + c + j) =
+                  make_float4(__uint_as_float(p[j]), __uint_as_float(p[j + 1]),
+                              __uint_as_float(p[j + 2]), __uint_as_float(p[j + 3]));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (c + j < w) out[c + j] = __uint_as_float(p[j]);
+          }
+        }
+      }
+      epi_c = c + 16;
+      if (epi_c >= kEpiCols || epi_cb + epi_c >= epi_width) epi_c = -1;  // warp-uniform
+    };
     TileGeom pg{};
     int t = unit;
     int kb = 0;
@@ -447,43 +495,29 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
         }
       }
       if (pending) {
-        // Promotion of the finished chunk in P (this CTA's 128 rows).
+        // Promotion of the finished chunk in P (this CTA's 128 rows): S = P
+        // for a tile's first chunk, else S += P, in TMEM only; then P is
+        // released to the MMA. For a tile's last chunk the stores of y from
+        // S follow, one 16-column group per later iteration (epi_step).
+        while (epi_c >= 0) epi_step();  // this thread's reads of S come first
         if (!wait(&s.tmem_full, acc_phase)) break;
         tc_fence_after();
         // A full tile holds this CTA's 128 rows x n_mma columns in TMEM lanes
         // 0-127. A half tile (M = 128: 64 rows per CTA) is folded: lanes 0-63
         // hold columns [0, n_mma/2) of the 64 rows, lanes 64-127 columns
-        // [n_mma/2, n_mma), in TMEM columns [0, n_mma/2).
+        // [n_mma/2, n_mma), in TMEM columns [0, n_mma/2). Either way thread
+        // (quarter, cgroup) owns TMEM lanes quarter*32.. and columns
+        // cgroup*64..+63, so every TMEM word of P and S is read and written
+        // by one thread only, in program order.
         const bool half = pg.m_mma < kTileM;
         const int width = half ? (pg.n_mma >> 1) : pg.n_mma;  // TMEM columns in use
-        const int epi = half ? kEpiCols / 2 : kEpiCols;
-        const int c_begin = cgroup * epi;
-        const int col_base = half ? (quarter >> 1) * width : 0;
-        const int row = pg.base + static_cast<int>(rank) * (pg.m_mma >> 1) +
-                        (half ? (quarter & 1) * 32 : quarter * 32) + lane;
-        bool store_row = pending_last && row >= pg.row0 && row < pg.row_end;
-        float* out = y + static_cast<long long>(row) * output + pg.col0 + col_base + c_begin;
-        float wgt = 0.0f;
-        if (scatter.dst != nullptr && store_row) {
-          float* dst_row = s.no_scatter ? nullptr : scatter_row(scatter, row, output);
-          store_row = dst_row != nullptr;
-          out = dst_row + pg.col0 + col_base + c_begin;
-        } else if (scatter.combine != nullptr && store_row) {
-          out = combine_row(scatter, row, output, wgt) + pg.col0 + col_base + c_begin;
-        }
-        // 128-bit stores where the row start allows them (caller-owned
-        // scatter bases and combine targets need not be 16-byte aligned).
-        const bool vrow = vec && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-        // Columns of this group to store.
-        const int w = min(width, pg.ncols - col_base) - c_begin;
+        const int c_begin = cgroup * kEpiCols;
 #pragma unroll
         for (int c = 0; c < kEpiCols; c += 16) {
-          if (c >= epi || c_begin + c >= width) break;  // warp-uniform
+          if (c_begin + c >= width) break;  // warp-uniform
           const uint32_t col = static_cast<uint32_t>(c_begin + c);
           uint32_t p[16];
-          // A first chunk reaches here only when it is also the last: its sum
-          // is in S.
-          tmem_ld_32x32b_x16(tmem + (pending_first ? kColS : kColP) + col + lane_addr, p);
+          tmem_ld_32x32b_x16(tmem + kColP + col + lane_addr, p);
           if (!pending_first) {
             uint32_t q[16];
             tmem_ld_32x32b_x16(tmem + kColS + col + lane_addr, q);
@@ -495,55 +529,49 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_pair_kernel(
           } else {
             tmem_ld_wait();
           }
-          if (!pending_last) {
-            tmem_st_32x32b_x16(tmem + kColS + col + lane_addr, p);
-          } else if (store_row && scatter.combine != nullptr) {
-            if (vrow) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                if (c + j < w) {
-                  red_add_v4_f32(out + c + j, __fmul_rn(wgt, __uint_as_float(p[j])),
-                                 __fmul_rn(wgt, __uint_as_float(p[j + 1])),
-                                 __fmul_rn(wgt, __uint_as_float(p[j + 2])),
-                                 __fmul_rn(wgt, __uint_as_float(p[j + 3])));
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (c + j < w) red_add_f32(out + c + j, __fmul_rn(wgt, __uint_as_float(p[j])));
-              }
-            }
-          } else if (store_row) {
-            if (vrow) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                if (c + j < w) {
-                  *reinterpret_cast<float4*>(out + c + j) =
-                      make_float4(__uint_as_float(p[j]), __uint_as_float(p[j + 1]),
-                                  __uint_as_float(p[j + 2]), __uint_as_float(p[j + 3]));
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (c + j < w) out[c + j] = __uint_as_float(p[j]);
-              }
-            }
-          }
+          tmem_st_32x32b_x16(tmem + kColS + col + lane_addr, p);
         }
-        if (!pending_last) tmem_st_wait();
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(tmem_empty_leader);
         acc_phase ^= 1u;
+        if (pending_last && c_begin < width) {
+          const int col_base = half ? (quarter >> 1) * width : 0;
+          const int row = pg.base + static_cast<int>(rank) * (pg.m_mma >> 1) +
+                          (half ? (quarter & 1) * 32 : quarter * 32) + lane;
+          bool store_row = row >= pg.row0 && row < pg.row_end;
+          float* out = y + static_cast<long long>(row) * output + pg.col0 + col_base + c_begin;
+          float wgt = 0.0f;
+          if (scatter.dst != nullptr && store_row) {
+            float* dst_row = s.no_scatter ? nullptr : scatter_row(scatter, row, output);
+            store_row = dst_row != nullptr;
+            out = dst_row + pg.col0 + col_base + c_begin;
+          } else if (scatter.combine != nullptr && store_row) {
+            out = combine_row(scatter, row, output, wgt) + pg.col0 + col_base + c_begin;
+          }
+          epi_c = 0;
+          epi_cb = c_begin;
+          epi_width = width;
+          epi_store = store_row;
+          epi_out = out;
+          epi_wgt = wgt;
+          // 128-bit stores where the row start allows them (caller-owned
+          // scatter bases and combine targets need not be 16-byte aligned).
+          epi_vrow = vec && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+          // Columns of this group to store.
+          epi_w = min(width, pg.ncols - col_base) - c_begin;
+        }
         pending = false;
+      } else if (epi_c >= 0) {
+        epi_step();
       }
-      if (!have_block) break;
-      // A chunk that ends here is promoted next iteration, except a tile's
-      // first chunk when more follow (it was accumulated into S directly).
-      if (((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) &&
-          !(kb < kChunkKb && kb + 1 < num_kb)) {
+      if (!have_block) {
+        while (epi_c >= 0) epi_step();
+        break;
+      }
+      // A chunk that ends here is promoted next iteration.
+      if ((kb + 1) % kChunkKb == 0 || kb + 1 == num_kb) {
         pending = true;
         pending_first = kb < kChunkKb;
         pending_last = (kb + 1 == num_kb);
