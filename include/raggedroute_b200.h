@@ -455,7 +455,10 @@ uint64_t rr_kernel_launch_count(void);
 /* Reads and clears the device-side error word set by bounded waits in the
  * library's kernels (0 = no error). Synchronizes the given stream. */
 rr_status rr_consume_device_error(void* stream, uint32_t* error_word);
-/* Which grouped-GEMM engine a shape takes: 1 = tcgen05 3xTF32, 2 = FP32 SIMT. */
+/* Which grouped-GEMM engine a shape takes (plain grouped GEMM, no row
+ * gathering or prepared weights): 1 = tcgen05 with the 3xTF32 split, 2 = FP32
+ * SIMT, 3 = tcgen05 CTA pairs with the mixed split (TF32 hi.hi plus bfloat16
+ * corrections; K >= 128 unless RAGGEDROUTE_B200_GEMM_MIXED=0). */
 int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
                            float* y_permuted, int hidden, int output);
 const char* rr_version(void);

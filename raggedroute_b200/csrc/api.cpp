@@ -1591,7 +1591,11 @@ rr_status rr_consume_device_error(void* stream, uint32_t* error_word) {
 
 int rr_grouped_gemm_engine(const float* x_permuted, const float* expert_weights,
                            float* y_permuted, int hidden, int output) {
-  return rrb::tc_gemm_supported(x_permuted, expert_weights, y_permuted, hidden, output) ? 1 : 2;
+  if (!rrb::tc_gemm_supported(x_permuted, expert_weights, y_permuted, hidden, output)) return 2;
+  return (rrb::gemm_pairs_enabled() && rrb::grouped_gemm_pair_units() > 0 &&
+          rrb::gemm_mixed_split(hidden))
+             ? 3
+             : 1;
 }
 
 rr_status rr_bounded_wait_selftest(uint64_t limit_ns, unsigned long long* elapsed_ns,

@@ -202,9 +202,12 @@ __device__ __forceinline__ void sts_v4_u32(uint32_t addr, uint32_t a, uint32_t b
 
 // Two floats rounded to bfloat16 (to nearest, ties to even) and packed: `lo`
 // in the low half (the lower address in memory), `hi` in the high half.
+// Saturating: a finite float beyond the largest finite bfloat16 (3.39e38)
+// becomes that value, not infinity, so a correction product of a value near
+// FLT_MAX with a zero lo part stays 0 instead of inf * 0 = NaN; NaN stays NaN.
 __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
   uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  asm("cvt.rn.satfinite.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
 

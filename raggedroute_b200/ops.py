@@ -485,4 +485,4 @@ def grouped_gemm_engine(x_permuted: torch.Tensor, expert_weights: torch.Tensor,
                         y_permuted: torch.Tensor, hidden: int, output: int) -> str:
     e = lib().rr_grouped_gemm_engine(_ptr(x_permuted), _ptr(expert_weights), _ptr(y_permuted),
                                      hidden, output)
-    return {1: "tcgen05_3xtf32", 2: "fp32_simt"}[e]
+    return {1: "tcgen05_3xtf32", 2: "fp32_simt", 3: "tcgen05_mixed"}[e]

@@ -1,4 +1,5 @@
-"""tcgen05 3xTF32 GEMM engine: accuracy against the FP64 oracle.
+"""tcgen05 GEMM engines (3xTF32 split; mixed TF32 + bfloat16 split of the
+CTA-pair grouped GEMM from K = 128 up): accuracy against the FP64 oracle.
 
 Tolerance: the reference's accumulation-aware FP32 bound
 4*gamma_K*sum|a||b| + 1e-7 (src/correctness/reference_validation.cpp:70-115)
@@ -54,7 +55,8 @@ def test_dense_tc(rrlib, oracle, cuda, m, n, k):
     b = rng.normal(0, 1 / math.sqrt(k), (k, n)).astype(np.float32)
     da, db = dev(a, cuda), dev(b, cuda)
     c = torch.full((m, n), float("nan"), device=cuda)
-    assert rrlib.grouped_gemm_engine(da, db, c, k, n) == "tcgen05_3xtf32"
+    assert rrlib.grouped_gemm_engine(da, db, c, k, n) == \
+        ("tcgen05_mixed" if k >= 128 else "tcgen05_3xtf32")
     rrlib.dense_gemm(da, db, c, m, n, k)
     check(oracle, host(c), a, b, oracle.dense_gemm_f64(a, b), k)
     assert device_error_word(rrlib) == 0
@@ -77,7 +79,8 @@ def test_grouped_tc(rrlib, oracle, cuda, sizes, k, n):
     w = rng.normal(0, 1 / math.sqrt(k), (e, k, n)).astype(np.float32)
     dx, dw = dev(x, cuda), dev(w, cuda)
     y = torch.full((r, n), float("nan"), device=cuda)
-    assert rrlib.grouped_gemm_engine(dx, dw, y, k, n) == "tcgen05_3xtf32"
+    assert rrlib.grouped_gemm_engine(dx, dw, y, k, n) == \
+        ("tcgen05_mixed" if k >= 128 else "tcgen05_3xtf32")
     rrlib.grouped_gemm(dx, dw, dev(offsets, cuda), y, e, k, n, r)
     got = host(y)
     ref = oracle.grouped_gemm_f64(x, w, offsets)
@@ -86,6 +89,52 @@ def test_grouped_tc(rrlib, oracle, cuda, sizes, k, n):
         if offsets[i + 1] > offsets[i]:
             check(oracle, got[s], x[s], w[i], ref[s], k)
     assert not np.isnan(got).any()
+    assert device_error_word(rrlib) == 0
+
+
+@pytest.mark.parametrize("k", [64, 256])
+def test_grouped_tc_extreme_magnitudes(rrlib, oracle, cuda, k):
+    """Operands across the FP32 range through both splits (K = 64: 3xTF32;
+    K = 256: the mixed split with bfloat16 corrections): rows holding values
+    up to 3.4e38 (beyond the largest finite bfloat16, 3.39e38) against
+    weights that are exact in TF32 (their lo part is 0, so an unsaturated
+    bfloat16 rounding of the large value would give inf * 0 = NaN in a
+    correction product), rows of subnormals, of 1e-30 and of zeros, mixed
+    with ordinary rows in the same tiles. Every output whose FP64 value is
+    finite in FP32 must be finite and within the accumulation-aware bound."""
+    rng = np.random.default_rng(k)
+    sizes = np.asarray([150, 0, 90], np.int32)
+    e, n = sizes.size, 40
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
+    r = int(offsets[-1])
+    x = rng.uniform(-1, 1, (r, k)).astype(np.float32)
+    # Weights exact in TF32: multiples of 2^-8 in [-1, 1).
+    w = (rng.integers(-256, 256, (e, k, n)) / 256.0).astype(np.float32)
+    big = np.float32(3.4e38)
+    x[3, :] = 0.0
+    x[3, 5] = big                       # one huge term per output
+    x[4, :] = 0.0
+    x[4, 0], x[4, 1] = big, -big        # huge terms that cancel exactly... or not
+    x[7, :] = rng.uniform(-1, 1, k).astype(np.float32) * np.float32(1e-40)  # subnormals
+    x[8, :] = rng.uniform(-1, 1, k).astype(np.float32) * np.float32(1e-30)
+    x[9, :] = 0.0
+    x[160, :] = 0.0
+    x[160, 7] = np.float32(-3.39e38)
+    w[0, 5, :] = 0.25                   # finite products 8.5e37 for row 3
+    dx, dw = dev(x, cuda), dev(w, cuda)
+    y = torch.full((r, n), float("nan"), device=cuda)
+    rrlib.grouped_gemm(dx, dw, dev(offsets, cuda), y, e, k, n, r)
+    got = host(y)
+    ref = oracle.grouped_gemm_f64(x, w, offsets)
+    finite = np.abs(ref) < np.float64(np.finfo(np.float32).max)
+    assert np.isfinite(got[finite]).all(), np.argwhere(~np.isfinite(got) & finite)[:8]
+    for i in range(e):
+        lo, hi = offsets[i], offsets[i + 1]
+        if hi > lo:
+            bound = oracle.gemm_error_bound(x[lo:hi], w[i], k)
+            err = np.abs(got[lo:hi].astype(np.float64) - ref[lo:hi])
+            ok = ~finite[lo:hi] | (err <= bound)
+            assert ok.all(), np.argwhere(~ok)[:8]
     assert device_error_word(rrlib) == 0
 
 
