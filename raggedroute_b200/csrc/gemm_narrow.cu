@@ -2,10 +2,12 @@
 // tcgen05 tensor cores, computed transposed: Y^T = W^T X^T.
 //
 // Contract: the dense_gemm of src/dense_gemm/cuda_naive/baseline.cu:16-58 of
-// the reference, y[m, n] = x[m, :] . w[:, n], with the 3xTF32 split and the
-// promotion every 512 of K of the grouped engine (gemm_tc.cu), so the
-// results hold the same FP32 contract (not bit-identical to that engine: the
-// tensor core sums a product's terms in its own order per M x N shape).
+// the reference, y[m, n] = x[m, :] . w[:, n], with the operand splits of the
+// CTA-pair grouped engine (gemm_pair.cu: the mixed split, TF32 hi.hi plus
+// bfloat16 corrections, from K = 128 up unless RAGGEDROUTE_B200_GEMM_MIXED=0;
+// 3xTF32 below) and the promotion every 512 of K, so the results hold the
+// same FP32 contract (not bit-identical to that engine: the tensor core sums
+// a product's terms in its own order per M x N shape).
 //
 // Why transposed: with the expert dimension (128) as the MMA's M, the token
 // dimension becomes the MMA's N, which may be any multiple of 16 up to 256.
@@ -49,6 +51,14 @@ constexpr int kXBytes = kMaxTM * kBK * 4;           // 16 KB (64 B rows)
 constexpr int kWBytes = kNW * kBK * 4;              // 8 KB
 constexpr int kRawBytes = kXBytes + kWBytes;        // X raw | W raw (N-major)
 constexpr int kOpBytes = kXBytes + 2 * kWBytes;     // X lo | W^T hi | W^T lo
+// Mixed split: the operand slot re-cut as W^T hi (TF32) | W^T | W^T lo |
+// X | X lo (bfloat16, K-major with the 32-byte swizzle).
+constexpr int kOffMWHi = 0;
+constexpr int kOffMW = kWBytes;
+constexpr int kOffMWLo = kOffMW + kWBytes / 2;
+constexpr int kOffMX = 2 * kWBytes;
+constexpr int kOffMXLo = kOffMX + kXBytes / 2;
+static_assert(kOffMXLo + kXBytes / 2 == kOpBytes, "the mixed split fills the operand slot");
 constexpr int kChunkKb = 32;                        // k-blocks per promoted chunk (K = 512)
 constexpr uint32_t kColP = 0;
 constexpr uint32_t kColS = 256;
@@ -90,6 +100,7 @@ __device__ __forceinline__ NarrowTile narrow_tile(int t, int rows, int tm) {
   return g;
 }
 
+template <bool kMixed>
 __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
     const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
     float* __restrict__ y, int rows, int hidden, int output, int tm, unsigned* err) {
@@ -160,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
       uint32_t phase = 0, rphase = 0, acc_phase = 0;
       bool ok = true;
       const uint32_t idesc = idesc_tf32(kNW, tm, false, false);
+      const uint32_t idesc16 = idesc_bf16(kNW, tm);
       for (int t = blockIdx.x; t < total && ok && !*failed; t += gridDim.x) {
         for (int kc = 0; kc < num_kb && ok; kc += kChunkKb) {
           if (!mbar_wait(&s.tmem_empty, acc_phase ^ 1u, err, failed)) {
@@ -180,6 +192,19 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
             tc_fence_after();
             const uint32_t op = smem_u32(s.op[stage]);
             const uint32_t raw = smem_u32(s.raw[rstage]);
+            if constexpr (kMixed) {
+              // hi(W).hi(X) in TF32, then W.lo(X) and lo(W).hi(X) in bfloat16.
+#pragma unroll
+              for (int ks = 0; ks < kBK / 8; ++ks) {
+                const uint64_t wh = smem_desc(op + kOffMWHi + ks * 32, 16, 512, Swizzle::k64B);
+                const uint64_t xh = smem_desc(raw + ks * 32, 16, 512, Swizzle::k64B);
+                mma_tf32(dacc, wh, xh, idesc, (kb == kc && ks == 0) ? 0u : 1u);
+              }
+              mma_bf16(dacc, smem_desc(op + kOffMW, 16, 256, Swizzle::k32B),
+                       smem_desc(op + kOffMXLo, 16, 256, Swizzle::k32B), idesc16, 1u);
+              mma_bf16(dacc, smem_desc(op + kOffMWLo, 16, 256, Swizzle::k32B),
+                       smem_desc(op + kOffMX, 16, 256, Swizzle::k32B), idesc16, 1u);
+            } else {
 #pragma unroll
             for (int ks = 0; ks < kBK / 8; ++ks) {
               // K-major, 64-byte swizzle: 8-row groups 512 B apart; the second
@@ -193,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
               mma_tf32(dacc, wl, xh, idesc, first);
               mma_tf32(dacc, wh, xl, idesc, 1u);
               mma_tf32(dacc, wh, xh, idesc, 1u);
+            }
             }
             mma_commit(&s.op_empty[stage]);
             mma_commit(&s.raw_empty[rstage]);
@@ -231,6 +257,15 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
 #pragma unroll
     for (int j = 0; j < 4; ++j) wsrc[j] = static_cast<uint32_t>((4 * wkc + j) * (kNW * 4) + wn * 4);
     const uint32_t wdst = static_cast<uint32_t>(kmajor64_offset(wn, wkc));
+    // Mixed split: the same W item as four bfloat16 (8 bytes) in row wn of
+    // the 32-byte rows; an X chunk c (row c / 4) likewise.
+    const uint32_t wdst16 = static_cast<uint32_t>(kmajor32_offset(wn, wkc >> 1) + ((wkc & 1) << 3));
+    auto x16_offset = [](int c) {
+      const int r = c >> 2;
+      const int kc = (c & 3) ^ ((r >> 1) & 3);  // logical 4-float chunk of the raw row
+      return static_cast<uint32_t>(kmajor32_offset(r, kc >> 1) + ((kc & 1) << 3));
+    };
+    const uint32_t xdst16[2] = {x16_offset(tid), x16_offset(tid + kWorkerThreads)};
     // X chunks of this thread: 16 bytes at tid * 16 and (tid + 512) * 16 of
     // the raw tile, written to the same (swizzled) position of X lo.
     const int xchunks = tm * 4;
@@ -261,17 +296,41 @@ __global__ void __launch_bounds__(kThreads, 1) dense_narrow_kernel(
         wv.z = lds_f32(raw + kXBytes + wsrc[2]);
         wv.w = lds_f32(raw + kXBytes + wsrc[3]);
         float4 h, l;
-        if (tid < xchunks) {
-          split_trunc4(x0, h, l);
-          sts_v4(op + tid * 16, l);
+        if constexpr (kMixed) {
+          // X: hi = trunc_tf32(x) is read by the MMA from the raw tile; hi
+          // and lo = x - hi (exact) go to the bfloat16 tiles. W: hi =
+          // rna_tf32(w) (TF32 tile), w and lo = w - hi (exact) in bfloat16.
+          if (tid < xchunks) {
+            split_trunc4(x0, h, l);
+            sts_v2_u32(op + kOffMX + xdst16[0], bf16x2_rn(h.x, h.y), bf16x2_rn(h.z, h.w));
+            sts_v2_u32(op + kOffMXLo + xdst16[0], bf16x2_rn(l.x, l.y), bf16x2_rn(l.z, l.w));
+          }
+          if (second) {
+            split_trunc4(x1, h, l);
+            sts_v2_u32(op + kOffMX + xdst16[1], bf16x2_rn(h.x, h.y), bf16x2_rn(h.z, h.w));
+            sts_v2_u32(op + kOffMXLo + xdst16[1], bf16x2_rn(l.x, l.y), bf16x2_rn(l.z, l.w));
+          }
+          h.x = tf32_rna(wv.x);
+          h.y = tf32_rna(wv.y);
+          h.z = tf32_rna(wv.z);
+          h.w = tf32_rna(wv.w);
+          sts_v4(op + kOffMWHi + wdst, h);
+          sts_v2_u32(op + kOffMW + wdst16, bf16x2_rn(wv.x, wv.y), bf16x2_rn(wv.z, wv.w));
+          sts_v2_u32(op + kOffMWLo + wdst16, bf16x2_rn(wv.x - h.x, wv.y - h.y),
+                     bf16x2_rn(wv.z - h.z, wv.w - h.w));
+        } else {
+          if (tid < xchunks) {
+            split_trunc4(x0, h, l);
+            sts_v4(op + tid * 16, l);
+          }
+          if (second) {
+            split_trunc4(x1, h, l);
+            sts_v4(op + (tid + kWorkerThreads) * 16, l);
+          }
+          split4(wv, h, l);
+          sts_v4(op + kXBytes + wdst, h);
+          sts_v4(op + kXBytes + kWBytes + wdst, l);
         }
-        if (second) {
-          split_trunc4(x1, h, l);
-          sts_v4(op + (tid + kWorkerThreads) * 16, l);
-        }
-        split4(wv, h, l);
-        sts_v4(op + kXBytes + wdst, h);
-        sts_v4(op + kXBytes + kWBytes + wdst, l);
         // Order this thread's generic reads and writes before the async
         // proxy (next TMA into raw, MMA reads of op).
         fence_proxy_async_smem();
@@ -369,7 +428,11 @@ bool narrow_configured() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [] {
-    ok = cudaFuncSetAttribute(dense_narrow_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ok = cudaFuncSetAttribute(dense_narrow_kernel<false>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kNarrowSmemBytes)) == cudaSuccess &&
+         cudaFuncSetAttribute(dense_narrow_kernel<true>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kNarrowSmemBytes)) == cudaSuccess;
     if (!ok) cudaGetLastError();
   });
@@ -427,9 +490,13 @@ cudaError_t launch_dense_narrow(const float* x, const float* w, float* y, int ro
   }
   const int tiles = (rows + tm - 1) / tm;
   const int grid = tiles < sms ? tiles : sms;
-  dense_narrow_kernel<<<grid, kThreads, kNarrowSmemBytes, stream>>>(mx, mw, y, rows, hidden,
-                                                                    output, tm,
-                                                                    device_error_word());
+  if (gemm_mixed_split(hidden)) {
+    dense_narrow_kernel<true><<<grid, kThreads, kNarrowSmemBytes, stream>>>(
+        mx, mw, y, rows, hidden, output, tm, device_error_word());
+  } else {
+    dense_narrow_kernel<false><<<grid, kThreads, kNarrowSmemBytes, stream>>>(
+        mx, mw, y, rows, hidden, output, tm, device_error_word());
+  }
   note_launch();
   return cudaGetLastError();
 }
