@@ -563,7 +563,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": ("f32 (grouped GEMM: TF32 hi.hi + bf16 corrections; router GEMM: 3xTF32)"
+        "dtype": ("f32 (GEMMs: TF32 hi.hi + bf16 correction products)"
                   if mixed else "f32 (3xTF32 GEMMs)"),
         "data": "synthetic (seeded; BASELINE C5 shapes and distributions)",
         "config": workload_config(tokens, world),
