@@ -92,6 +92,42 @@ def test_grouped_tc(rrlib, oracle, cuda, sizes, k, n):
     assert device_error_word(rrlib) == 0
 
 
+@pytest.mark.parametrize("k", [124, 128, 132, 144, 1040])
+def test_grouped_tc_split_boundary_and_worst_mantissas(rrlib, oracle, cuda, k):
+    """K on both sides of the mixed split's threshold (124: 3xTF32; 128 and
+    up: TF32 hi.hi plus bfloat16 corrections; 132 and 1040 end in a partial
+    k-block; 1040 = two full 512-chunks plus one k-block), with operands whose
+    split errors are largest: half the A values have all 13 low mantissa bits
+    set (lo(A) just under one TF32 ulp of A, the largest truncation
+    remainder), half the W values sit one bit off a TF32 rounding tie, so
+    lo(W) is close to half an ulp and its bfloat16 rounding is exercised at
+    every exponent. Elementwise within the accumulation-aware bound and 1e-5
+    normwise against FP64."""
+    rng = np.random.default_rng(k)
+    sizes = np.asarray([300, 1, 0, 257], np.int32)
+    e, n = sizes.size, 272
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
+    r = int(offsets[-1])
+    x = rng.uniform(-1, 1, (r, k)).astype(np.float32)
+    xb = x.view(np.uint32)
+    sel = rng.random((r, k)) < 0.5
+    xb[sel] |= np.uint32(0x1FFF)
+    w = (rng.normal(0, 1, (e, k, n)) * np.exp2(rng.integers(-20, 4, (e, k, n)))).astype(np.float32)
+    wb = w.view(np.uint32)
+    sel = rng.random((e, k, n)) < 0.5
+    wb[sel] = (wb[sel] & np.uint32(0xFFFFE000)) | np.uint32(0x0FFF)   # just below a tie
+    dx, dw = dev(x, cuda), dev(w, cuda)
+    y = torch.full((r, n), float("nan"), device=cuda)
+    rrlib.grouped_gemm(dx, dw, dev(offsets, cuda), y, e, k, n, r)
+    got = host(y)
+    ref = oracle.grouped_gemm_f64(x, w, offsets)
+    for i in range(e):
+        lo, hi = offsets[i], offsets[i + 1]
+        if hi > lo:
+            check(oracle, got[lo:hi], x[lo:hi], w[i], ref[lo:hi], k)
+    assert device_error_word(rrlib) == 0
+
+
 @pytest.mark.parametrize("k", [64, 256])
 def test_grouped_tc_extreme_magnitudes(rrlib, oracle, cuda, k):
     """Operands across the FP32 range through both splits (K = 64: 3xTF32;
