@@ -82,10 +82,13 @@ __device__ __forceinline__ void merge_lane_group(float& v1, int& i1, float& v2, 
   }
 }
 
-// Weights of a ranked row and the stores of its ids and weights.
+// Weights of a ranked row and the stores of its ids and weights (kPair: one
+// 8-byte store each, for 8-byte aligned outputs; chosen at launch, since a
+// run-time branch here measured 0.25 us slower per C5 launch).
+template <bool kPair>
 __device__ __forceinline__ void write_row(long long row, float v1, int i1, float v2, int i2,
                                           int32_t* __restrict__ ids,
-                                          float* __restrict__ weights, bool pair_stores,
+                                          float* __restrict__ weights,
                                           const int32_t* __restrict__ remap) {
   int id0 = i1;
   int id1 = i2;
@@ -104,7 +107,7 @@ __device__ __forceinline__ void write_row(long long row, float v1, int i1, float
     id0 = __ldg(remap + id0);
     id1 = __ldg(remap + id1);
   }
-  if (pair_stores) {
+  if constexpr (kPair) {
     reinterpret_cast<int2*>(ids)[row] = make_int2(id0, id1);
     reinterpret_cast<float2*>(weights)[row] = make_float2(w0, w1);
   } else {
@@ -115,9 +118,28 @@ __device__ __forceinline__ void write_row(long long row, float v1, int i1, float
   }
 }
 
+// Candidate e into a lane top-2 that already holds two valid entries
+// (v1, i1) >= (v2, i2), e above every id seen. A strict compare decides
+// (a later equal value never precedes an earlier one), and a NaN candidate
+// fails both compares, so it needs no canonical form here.
+__device__ __forceinline__ void insert_ranked(float v, int e, float& v1, int& i1, float& v2,
+                                              int& i2) {
+  const bool above1 = v > v1;
+  const bool above2 = v > v2;
+  const float tv = above2 ? v : v2;
+  const int ti = above2 ? e : i2;
+  v2 = above1 ? v1 : tv;
+  i2 = above1 ? i1 : ti;
+  v1 = above1 ? v : v1;
+  i1 = above1 ? e : i1;
+}
+
 // Candidates of one 16-byte group (experts 4q..4q+3) into the lane's top-2.
+// The lane's first group (first == true) seeds the list with its first two
+// candidates in canonical form (NaN as -inf), so every later compare sees
+// two valid entries; the lower id leads on equal values.
 __device__ __forceinline__ void insert4(float4 v, const float* __restrict__ bias, int q,
-                                        float& v1, int& i1, float& v2, int& i2) {
+                                        bool first, float& v1, int& i1, float& v2, int& i2) {
   if (bias != nullptr) {
     const float4 b = __ldg(reinterpret_cast<const float4*>(bias) + q);
     v.x = v.x + b.x;
@@ -126,37 +148,89 @@ __device__ __forceinline__ void insert4(float4 v, const float* __restrict__ bias
     v.w = v.w + b.w;
   }
   const int e = q << 2;
-  insert_in_order(canonical(v.x), e, v1, i1, v2, i2);
-  insert_in_order(canonical(v.y), e + 1, v1, i1, v2, i2);
-  insert_in_order(canonical(v.z), e + 2, v1, i1, v2, i2);
-  insert_in_order(canonical(v.w), e + 3, v1, i1, v2, i2);
+  if (first) {
+    const float a = canonical(v.x);
+    const float c = canonical(v.y);
+    const bool swap = c > a;
+    v1 = swap ? c : a;
+    i1 = swap ? e + 1 : e;
+    v2 = swap ? a : c;
+    i2 = swap ? e : e + 1;
+  } else {
+    insert_ranked(v.x, e, v1, i1, v2, i2);
+    insert_ranked(v.y, e + 1, v1, i1, v2, i2);
+  }
+  insert_ranked(v.z, e + 2, v1, i1, v2, i2);
+  insert_ranked(v.w, e + 3, v1, i1, v2, i2);
 }
 
 // kPer: 128-bit loads each lane issues before it ranks them (all in flight at
-// once); 8 for large batches so that one wave of CTAs keeps enough bytes in
-// flight to stream the logits at HBM speed, 2 for small latency-bound ones.
-template <int L, bool kVec, int kPer>
-__global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict__ logits,
-                                                        const float* __restrict__ bias,
-                                                        int32_t* __restrict__ ids,
-                                                        float* __restrict__ weights, int tokens,
-                                                        int experts, bool pair_stores,
-                                                        const int32_t* __restrict__ remap) {
+// once); 8 for large batches, 2 for small latency-bound ones. The streaming
+// instance (kPer = 8) runs three 256-thread CTAs per SM (at most 85 registers)
+// and, before any row is read, has one thread issue an L2 bulk prefetch of
+// every row group the CTA will rank: DRAM then streams the whole input while
+// the warps rank, and each warp's later groups load from L2. (Measured at
+// T=65536, E=128 with bias, one launch in a graph of 100: 10.4-10.7 us
+// before, 7.5-7.8 us with both; 2, 4 or 5 CTAs per SM, one contiguous chunk
+// of groups per CTA, the bias held in registers and register double
+// buffering of the next group were each slower.)
+template <int L, bool kVec, int kPer, bool kPair, bool kFull>
+__global__ void __launch_bounds__(256, kPer == 8 ? 3 : 1)
+    topk_gate_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                     int32_t* __restrict__ ids, float* __restrict__ weights, int tokens,
+                     int experts, const int32_t* __restrict__ remap) {
   constexpr int kRowsPerWarp = 32 / L;
   const int lane = threadIdx.x & 31;
   const int group = lane / L;
   const int j = lane % L;
-  const long long warps_total = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long wrow = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) +
-                        (threadIdx.x >> 5);
-       wrow * kRowsPerWarp < tokens; wrow += warps_total) {
-    const long long row = wrow * kRowsPerWarp + group;
+  // This CTA ranks row groups blockIdx.x, blockIdx.x + gridDim.x, ... of
+  // rows_per_cta rows each; warp w owns rows w * kRowsPerWarp .. of a group.
+  const long long rows_per_cta = static_cast<long long>(blockDim.x >> 5) * kRowsPerWarp;
+  const long long cta_stride = static_cast<long long>(gridDim.x) * rows_per_cta;
+  const long long lrow = static_cast<long long>(threadIdx.x >> 5) * kRowsPerWarp + group;
+  if constexpr (kVec && kPer == 8) {
+    // Rows are 16-byte multiples and the base is 16-byte aligned (the kVec
+    // conditions), as the bulk prefetch requires.
+    if (threadIdx.x == 0) {
+      for (long long r0 = blockIdx.x * rows_per_cta; r0 < tokens; r0 += cta_stride) {
+        const long long rows = tokens - r0 < rows_per_cta ? tokens - r0 : rows_per_cta;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(logits + r0 * experts),
+                     "r"(static_cast<unsigned>(rows * experts * 4))
+                     : "memory");
+      }
+    }
+  }
+  for (long long r0 = blockIdx.x * rows_per_cta; r0 < tokens; r0 += cta_stride) {
+    const long long row = r0 + lrow;
     const bool active = row < tokens;
     float v1 = kNegInf, v2 = kNegInf;
     int i1 = -1, i2 = -1;
     if (active) {
       const float* src = logits + row * experts;
-      if constexpr (kVec) {
+      if constexpr (kVec && kPer == 8) {
+        // One pass: launch_per picks L >= nvec / 8, so the L lanes' 8 loads
+        // cover the row. A row of exactly L * 8 groups (kFull) needs no
+        // guards; a separate instance, since a run-time choice between the
+        // two bodies measured slower.
+        const int nvec = experts >> 2;
+        const float4* src4 = reinterpret_cast<const float4*>(src);
+        float4 v[kPer];
+        if constexpr (kFull) {
+#pragma unroll
+          for (int u = 0; u < kPer; ++u) v[u] = __ldcs(src4 + j + u * L);
+#pragma unroll
+          for (int u = 0; u < kPer; ++u) insert4(v[u], bias, j + u * L, u == 0, v1, i1, v2, i2);
+        } else {
+#pragma unroll
+          for (int u = 0; u < kPer; ++u) {
+            if (j + u * L < nvec) v[u] = __ldcs(src4 + j + u * L);
+          }
+#pragma unroll
+          for (int u = 0; u < kPer; ++u) {
+            if (j + u * L < nvec) insert4(v[u], bias, j + u * L, u == 0, v1, i1, v2, i2);
+          }
+        }
+      } else if constexpr (kVec) {
         const int nvec = experts >> 2;
         const float4* src4 = reinterpret_cast<const float4*>(src);
         for (int q0 = j; q0 < nvec; q0 += L * kPer) {
@@ -169,7 +243,7 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
 #pragma unroll
           for (int u = 0; u < kPer; ++u) {
             const int q = q0 + u * L;
-            if (q < nvec) insert4(v[u], bias, q, v1, i1, v2, i2);
+            if (q < nvec) insert4(v[u], bias, q, u == 0 && q0 == j, v1, i1, v2, i2);
           }
         }
       } else {
@@ -184,21 +258,20 @@ __global__ void __launch_bounds__(256) topk_gate_kernel(const float* __restrict_
 
     merge_lane_group<L>(v1, i1, v2, i2);
     if (!active || j != 0) continue;
-    write_row(row, v1, i1, v2, i2, ids, weights, pair_stores, remap);
+    write_row<kPair>(row, v1, i1, v2, i2, ids, weights, remap);
   }
 }
 
-template <int L, bool kVec, int kPer>
+template <int L, bool kVec, int kPer, bool kPair, bool kFull>
 cudaError_t launch_l(const float* logits, const float* bias, int32_t* ids, float* weights,
-                     int tokens, int experts, bool pair, const int32_t* remap,
-                     cudaStream_t stream) {
+                     int tokens, int experts, const int32_t* remap, cudaStream_t stream) {
   constexpr int kThreads = 256;
   constexpr int kRowsPerBlock = (kThreads / 32) * (32 / L);
   // One resident wave (CTAs per SM from the occupancy of this instance).
   static int per_sm = 0;
   if (per_sm == 0) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, topk_gate_kernel<L, kVec, kPer>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, topk_gate_kernel<L, kVec, kPer, kPair, kFull>,
                                                       kThreads, 0) != cudaSuccess || n < 1) {
       cudaGetLastError();
       n = 1;
@@ -206,10 +279,30 @@ cudaError_t launch_l(const float* logits, const float* bias, int32_t* ids, float
     per_sm = n;
   }
   const int blocks = min(ceil_div(tokens, kRowsPerBlock), per_sm * sm_count());
-  topk_gate_kernel<L, kVec, kPer><<<blocks, kThreads, 0, stream>>>(
-      logits, bias, ids, weights, tokens, experts, pair, remap);
+  topk_gate_kernel<L, kVec, kPer, kPair, kFull><<<blocks, kThreads, 0, stream>>>(
+      logits, bias, ids, weights, tokens, experts, remap);
   note_launch();
   return cudaGetLastError();
+}
+
+// Instance by store width and, for the one-pass streaming instance, by
+// whether the L lanes' 8 loads exactly cover a row.
+template <int L, bool kVec, int kPer>
+cudaError_t launch_pf(const float* logits, const float* bias, int32_t* ids, float* weights,
+                      int tokens, int experts, bool pair, const int32_t* remap,
+                      cudaStream_t stream) {
+  if constexpr (kVec && kPer == 8) {
+    if ((experts >> 2) == L * kPer) {
+      return pair ? launch_l<L, kVec, kPer, true, true>(logits, bias, ids, weights, tokens,
+                                                        experts, remap, stream)
+                  : launch_l<L, kVec, kPer, false, true>(logits, bias, ids, weights, tokens,
+                                                         experts, remap, stream);
+    }
+  }
+  return pair ? launch_l<L, kVec, kPer, true, false>(logits, bias, ids, weights, tokens, experts,
+                                                     remap, stream)
+              : launch_l<L, kVec, kPer, false, false>(logits, bias, ids, weights, tokens, experts,
+                                                      remap, stream);
 }
 
 template <bool kVec, int kPer>
@@ -223,19 +316,20 @@ cudaError_t launch_per(const float* logits, const float* bias, int32_t* ids, flo
   int l = 1;
   while (l < want && l < 32) l <<= 1;
   switch (l) {
-    case 1: return launch_l<1, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 2: return launch_l<2, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 4: return launch_l<4, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 8: return launch_l<8, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    case 16: return launch_l<16, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
-    default: return launch_l<32, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 1: return launch_pf<1, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 2: return launch_pf<2, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 4: return launch_pf<4, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 8: return launch_pf<8, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    case 16: return launch_pf<16, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
+    default: return launch_pf<32, kVec, kPer>(logits, bias, ids, weights, tokens, experts, pair, remap, stream);
   }
 }
 
 // Batches from this many rows up stream the logits with 8 loads per lane.
 // (A variant that staged rows in shared memory with cp.async.bulk, 192 KB in
 // flight per SM, measured slower at C5: 26.7 us with 8 warps per SM and
-// 15.1 us with 32, against 10.7 us here.)
+// 15.1 us with 32, against 10.7 us for the register-staged kernel without
+// the L2 prefetch.)
 constexpr int kStreamingRows = 16384;
 
 }  // namespace
