@@ -687,10 +687,15 @@ cudaError_t launch_grouped_gemm_tc(const float* x, const float* w, const int32_t
                                    cudaStream_t stream, int weight_sets,
                                    const RowScatter* scatter, const RowGather* gather) {
   const int wsets = weight_sets > 0 ? weight_sets : experts;
-  // One group with at most 128 output columns and enough rows to fill every
-  // SM twice (the router GEMM): the transposed narrow kernel.
+  // One group with at most 128 output columns (the router GEMM): the
+  // transposed narrow kernel, at every row count. Its per-element arithmetic
+  // (split, K order, promotion) does not depend on the number of rows or on
+  // its token-tile height, so a token's logits are the same bits whatever
+  // batch it arrives in: a chunked chain (rr_chain_from_tokens_host) equals
+  // one chain over the whole batch. (Below two waves of rows the engine
+  // would be about as fast, but its bits differ from the narrow kernel's.)
   if (offsets == nullptr && gather == nullptr && scatter == nullptr && output <= kBN / 2 &&
-      rows >= 2LL * kBM * sm_count() && dense_narrow_enabled()) {
+      rows > 0 && dense_narrow_enabled()) {
     const cudaError_t ne = launch_dense_narrow(x, w, y, rows, hidden, output, stream);
     if (ne != cudaErrorNotSupported) return ne;
   }

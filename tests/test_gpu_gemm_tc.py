@@ -293,9 +293,10 @@ def test_grouped_tc_c5_shape_sampled(rrlib, oracle, cuda):
 
 @pytest.mark.parametrize("m,n,k", [(40000, 128, 256), (37999, 100, 64), (65536, 128, 128)])
 def test_dense_tc_two_tiles_per_cta(rrlib, oracle, cuda, m, n, k):
-    """Router-shaped GEMMs (N <= 128, at least one wave of 256-row tiles) run
-    two 128-row m-tiles per CTA sharing each B tile; ragged row counts leave
-    a shifted last tile."""
+    """Router-shaped GEMMs (N <= 128, at least one wave of 256-row tiles);
+    ragged row counts leave a shifted last tile. By default they run the
+    narrow kernel; the engine's two 128-row m-tiles per CTA (sharing each B
+    tile) run under RAGGEDROUTE_B200_NARROW_DENSE=0 (test_gpu_engines)."""
     rng = np.random.default_rng(m + n)
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     b = rng.normal(0, 1 / math.sqrt(k), (k, n)).astype(np.float32)
@@ -313,8 +314,7 @@ def test_dense_tc_two_tiles_per_cta(rrlib, oracle, cuda, m, n, k):
 
 @pytest.mark.parametrize("m,n,k", [(65536, 128, 4096), (50003, 60, 512)])
 def test_dense_narrow_router_shapes(rrlib, oracle, cuda, m, n, k):
-    """Dense GEMMs with N <= 128 and rows for two waves of tiles take the
-    transposed narrow kernel (token tiles of 224 at C5's router shape,
+    """Dense GEMMs with N <= 128 take the transposed narrow kernel (token tiles of 224 at C5's router shape,
     65536 x 4096 x 128; a ragged row count and N = 60 with a shifted last
     tile): 2048 sampled rows plus the first and last against the FP64
     oracle, elementwise within the accumulation-aware bound and normwise
@@ -332,6 +332,28 @@ def test_dense_narrow_router_shapes(rrlib, oracle, cuda, m, n, k):
     sel = torch.from_numpy(rows).to(cuda)
     a_s, c_s, b_h = host(a[sel]), host(c[sel]), host(b)
     check(oracle, c_s, a_s, b_h, oracle.dense_gemm_f64(a_s, b_h), k)
+    assert device_error_word(rrlib) == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(65536, 128, 4096), (40000, 60, 512)])
+def test_dense_narrow_batch_independent(rrlib, cuda, m, n, k):
+    """The router GEMM's result for a row does not depend on the batch the
+    row arrives in: rows computed inside the whole batch (token tiles of 224
+    or 144 rows) and inside slices of 8192, 300, 37 and 1 rows (tiles of 32)
+    are the same bits. The chunked host-memory chain relies on this."""
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m + 7 * n)
+    a = torch.randn(m, k, generator=g, device=cuda)
+    b = torch.randn(k, n, generator=g, device=cuda) / math.sqrt(k)
+    c = torch.full((m, n), float("nan"), device=cuda)
+    rrlib.dense_gemm(a, b, c, m, n, k)
+    for start, rows in [(1000, 8192), (m - 300, 300), (5, 37), (m - 1, 1), (0, 1)]:
+        a_s = a[start:start + rows].contiguous()
+        c_s = torch.full((rows, n), float("nan"), device=cuda)
+        rrlib.dense_gemm(a_s, b, c_s, rows, n, k)
+        torch.cuda.synchronize()
+        assert torch.equal(c_s.view(torch.int32), c[start:start + rows].view(torch.int32)), \
+            (start, rows)
     assert device_error_word(rrlib) == 0
 
 

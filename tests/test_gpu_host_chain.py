@@ -1,8 +1,10 @@
 """rr_chain_from_tokens_host: the chunked, copy-overlapped chain over host
 memory must give the same Y (and routing decisions) bit for bit as
 rr_chain_from_tokens over the whole batch on the device: several chunks with
-a ragged last one, a batch smaller than one chunk, an empty batch, pageable
-host memory, and a plan reused across calls (with and without the
+a ragged last one, a batch smaller than one
+chunk, an empty batch, pageable host memory, a batch of 40000 tokens in
+chunks of 8192 (the whole batch and its chunks on either side of two waves
+of router tiles), and a plan reused across calls (with and without the
 input-ready flag that lets back-to-back calls overlap)."""
 from __future__ import annotations
 
@@ -31,7 +33,8 @@ def _device_chain(rrlib, x_host, wr, we, bias, dev):
 
 
 @pytest.mark.parametrize("tokens,chunk,pinned", [(5000, 1024, True), (300, 1024, True),
-                                                 (4096, 1024, False), (0, 512, True)])
+                                                 (4096, 1024, False), (0, 512, True),
+                                                 (40000, 8192, True)])
 def test_host_chain_matches_device_chain(rrlib, cuda, tokens, chunk, pinned):
     from raggedroute_b200.workloads import normal
     wr, we, bias = _weights(cuda)
