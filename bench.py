@@ -86,6 +86,11 @@ def parse_args():
                          "given expert counts and id distributions, 3 calls each, and print "
                          "their event times: a small single-operator command for Nsight "
                          "Compute, e.g. 256:uniform,8:one")
+    ap.add_argument("--gate-only", type=int, default=None, metavar="TOKENS",
+                    help="run only topk_gate with bias at E=128 (C5's gate) over TOKENS rows "
+                         "of N(0,1) logits, 3 calls each timed with CUDA events: a small "
+                         "single-operator command for Nsight Compute (262144 rows = 134 MB "
+                         "of logits, larger than L2)")
     ap.add_argument("--only-stage", default=None,
                     choices=["dense_gemm", "topk_gate", "histogram_exclusive_scan",
                              "token_permute", "grouped_gemm", "unpermute"],
@@ -723,6 +728,34 @@ def run_c3_permute(spec: str) -> dict:
     return {"c3_permute": out}
 
 
+def run_gate_only(tokens: int) -> dict:
+    """C5's topk_gate (E = 128, per-expert bias) over `tokens` rows of N(0,1)
+    logits: three calls, each timed with CUDA events; nothing else runs."""
+    import torch
+
+    import raggedroute_b200 as rr
+    device = torch.device("cuda", 0)
+    e = 128
+    g = torch.Generator(device=device)
+    g.manual_seed(4)
+    logits = torch.randn(tokens, e, generator=g, device=device)
+    bias = torch.randn(e, generator=g, device=device)
+    ids = torch.empty(tokens, 2, dtype=torch.int32, device=device)
+    w = torch.empty(tokens, 2, device=device)
+    times = []
+    for _ in range(3):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        rr.topk_gate_biased(logits, bias, ids, w, tokens, e)
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return {"gate_only": {"tokens": tokens, "experts": e,
+                          "bytes": 4 * tokens * e + 16 * tokens,
+                          "topk_gate_us": [round(t, 2) for t in times]}}
+
+
 def run_profile_once(torch, rr, stream, ctx, inp, buf, tokens: int, e: int) -> dict:
     """One warm-up chain, then exactly one untimed chain_from_tokens call for a
     profiler (the library brackets each stage in an NVTX range named
@@ -904,8 +937,14 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float, bf16_tflops:
     gate = _event_us(torch, rr, stream, lambda c: rr.topk_gate_biased(
         logits, bias, g_ids, g_w, gt, ge, ctx=c), 50)
     gate_b = 4.0 * gt * ge + 16.0 * gt
+    # The floor of one launch in a graph: a one-expert scan (one tiny kernel).
+    one_c = torch.ones(1, dtype=torch.int32, device=device)
+    one_o = torch.empty(2, dtype=torch.int32, device=device)
+    floor_us = _event_us(torch, rr, stream, lambda c: rr.exclusive_scan(one_c, one_o, 1, ctx=c), 50)
     out["C5_topk_gate"] = {"us": round(gate, 2),
-                           "hbm_frac": round(gate_b / (gate * 1e-6) / 1e9 / hbm_gbs, 3)}
+                           "hbm_frac": round(gate_b / (gate * 1e-6) / 1e9 / hbm_gbs, 3),
+                           "hbm_frac_above_launch_floor": round(
+                               gate_b / (max(gate - floor_us, 1e-3) * 1e-6) / 1e9 / hbm_gbs, 3)}
     g_counts = torch.empty(ge, dtype=torch.int32, device=device)
     g_offsets = torch.empty(ge + 1, dtype=torch.int32, device=device)
     hs = _event_us(torch, rr, stream, lambda c: rr.histogram_exclusive_scan(
@@ -919,10 +958,6 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float, bf16_tflops:
     pos = torch.empty(routes, dtype=torch.int32, device=device)
     srt = torch.empty(routes, dtype=torch.int32, device=device)
     c3 = {}
-    # The floor of one launch in a graph: a one-expert scan (one tiny kernel).
-    one_c = torch.ones(1, dtype=torch.int32, device=device)
-    one_o = torch.empty(2, dtype=torch.int32, device=device)
-    floor_us = _event_us(torch, rr, stream, lambda c: rr.exclusive_scan(one_c, one_o, 1, ctx=c), 50)
     out["launch_floor_us"] = round(floor_us, 2)
     for e in C3["experts"]:
         counts = torch.empty(e, dtype=torch.int32, device=device)
@@ -937,6 +972,12 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float, bf16_tflops:
                              lambda c: rr.exclusive_scan(counts, offsets, e, ctx=c), 50)
             fused = _event_us(torch, rr, stream, lambda c: rr.histogram_exclusive_scan(
                 ids, counts, offsets, routes, e, ctx=c), 50)
+            # The two operators back to back in the same graph: the like-for-
+            # like comparison for the fused one (separate graphs each carry
+            # their own per-launch gaps).
+            pair = _event_us(torch, rr, stream, lambda c: (
+                rr.histogram(ids, counts, routes, e, ctx=c),
+                rr.exclusive_scan(counts, offsets, e, ctx=c)), 50)
             hist_b = 4.0 * routes + 4.0 * e
             fused_b = 4.0 * routes + 8.0 * e + 4
             perm_b = 4.0 * tokens * k + 4.0 * routes * k + 12.0 * routes + 4.0 * (e + 1)
@@ -952,6 +993,7 @@ def config_sweep(torch, rr, device, hbm_gbs: float, peak_3x: float, bf16_tflops:
                     frac(hist_b, max(hist - 2 * floor_us, 1e-3)),
                 "exclusive_scan_us": round(scan, 2),
                 "histogram_exclusive_scan_us": round(fused, 2),
+                "histogram_then_exclusive_scan_us": round(pair, 2),
                 "histogram_exclusive_scan_hbm_frac": frac(fused_b, fused)}
             if e >= 2:  # top_k = 2 needs two experts (the operator's top_k <= E rule)
                 perm = _event_us(torch, rr, stream, lambda c: rr.token_permute(
@@ -1112,6 +1154,8 @@ def _main() -> dict | None:
         return run_reference(args, rank)
     if args.c3_permute is not None:
         return run_c3_permute(args.c3_permute)
+    if args.gate_only is not None:
+        return run_gate_only(args.gate_only)
     if world > 1:
         import datetime
 
