@@ -107,14 +107,18 @@ def test_topk_special_modes(rrlib, oracle, cuda, mode):
     _topk_check(rrlib, oracle, cuda, x)
 
 
-@pytest.mark.parametrize("experts", [4, 8, 64, 128, 256, 1024])
+@pytest.mark.parametrize("experts", [4, 8, 36, 64, 100, 128, 256, 1024])
 @pytest.mark.parametrize("tokens", [16384, 40001])
 @pytest.mark.parametrize("biased", [False, True])
 def test_topk_large_batches(rrlib, oracle, cuda, experts, tokens, biased):
-    """Batches of 16384 rows and more take the bulk-copy kernel (rows staged
-    in shared memory in chunks of 24 KB): ids bit-exact and weights within
-    the reference's 1e-6 against the oracle, with ties, NaN rows, infinities
-    and signed zeros spread over the chunks and a ragged last chunk."""
+    """Batches of 16384 rows and more take the streaming instance (8 loads
+    per lane in one pass, an L2 bulk prefetch of every row group a CTA
+    ranks): rows exactly covered by the lanes' loads (E = 64 .. 1024) and
+    rows covered in part (E = 4, 8 with one lane per row; E = 36 and 100
+    with 2 and 4 lanes, some of whose load slots lie past the row). Ids
+    bit-exact and weights within the reference's 1e-6 against the oracle,
+    with ties, NaN rows, infinities and signed zeros spread over the row
+    groups and a ragged last group."""
     rng = np.random.default_rng(experts * 7 + tokens + biased)
     x = rng.standard_normal((tokens, experts)).astype(np.float32)
     x[::3] = np.round(x[::3] * 2) / 2
