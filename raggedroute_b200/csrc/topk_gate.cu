@@ -170,8 +170,8 @@ __device__ __forceinline__ void insert4(float4 v, const float* __restrict__ bias
 // and, before any row is read, has one thread issue an L2 bulk prefetch of
 // every row group the CTA will rank: DRAM then streams the whole input while
 // the warps rank, and each warp's later groups load from L2. (Measured at
-// T=65536, E=128 with bias, one launch in a graph of 100: 10.4-10.7 us
-// before, 7.5-7.8 us with both; 2, 4 or 5 CTAs per SM, one contiguous chunk
+// T=65536, E=128 with bias, one launch in a graph of 50-100: 10.4-10.7 us
+// before, 7.9-8.1 us with both; 2, 4 or 5 CTAs per SM, one contiguous chunk
 // of groups per CTA, the bias held in registers and register double
 // buffering of the next group were each slower.)
 template <int L, bool kVec, int kPer, bool kPair, bool kFull>
